@@ -1,0 +1,160 @@
+/*
+ * vxmoe.h - C ABI of the B200 (sm_100a) routed sparse-MoE block.
+ *
+ * Plain pointers, sizes and a cudaStream_t (passed as void*).  Every pointer
+ * is device memory owned by the caller; the library allocates nothing and
+ * takes scratch space only from the caller's workspace.  Every entry point
+ * is stream-ordered on the caller's stream, performs no host synchronisation
+ * and returns a vx_status code.
+ *
+ * bf16 values travel as uint16_t bit patterns.  Q4 weights use the MLX
+ * affine layout of the reference: uint32 words along the input axis, element
+ * i in bits 4*(i%8) of word i/8, bf16 scale and bias per group of 32 inputs,
+ * w = scale*q + bias (models/flashnext/metal_runtime.py:1022-1027).
+ *
+ * Reference paths below are relative to the Veystrix-Core project.
+ */
+#ifndef VXMOE_H
+#define VXMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  The Python layer maps them onto the exceptions the
+ * reference raises: SHAPE/INDEX -> ValueError, DTYPE -> TypeError,
+ * CUDA/UNSUPPORTED -> RuntimeError (metal_runtime.py:446-461, :839-895,
+ * :138-142, :824-825). */
+typedef enum vx_status {
+  VX_OK = 0,
+  VX_EINVAL_SHAPE = 1,
+  VX_EINVAL_DTYPE = 2,
+  VX_EINVAL_INDEX = 3,
+  VX_ECUDA = 4,
+  VX_ETIMEOUT = 5,
+  VX_EWORKSPACE = 6,
+  VX_EUNSUPPORTED = 7
+} vx_status;
+
+/* One packed Q4 projection bank: w [experts, out, in/8] uint32,
+ * scales/biases [experts, out, in/group_size] bf16.  Mirrors
+ * Q4G32Projection (metal_runtime.py:39-45). */
+typedef struct vx_q4 {
+  const uint32_t* w;
+  const uint16_t* scales;
+  const uint16_t* biases;
+  int32_t experts;
+  int32_t out;
+  int32_t in;
+  int32_t group_size;
+} vx_q4;
+
+/* Weights of one MoE block (adaptive_topk.py:54-293).  shared_* banks have
+ * experts == 1; shared_gate.w == NULL means "no shared expert".  router_w is
+ * the unquantised bf16 gate [num_experts, hidden] (preflight.py:70). */
+typedef struct vx_moe_weights {
+  vx_q4 gate;                 /* [E, I, d/8]  switch_mlp.gate_proj */
+  vx_q4 up;                   /* [E, I, d/8]  switch_mlp.up_proj   */
+  vx_q4 down;                 /* [E, d, I/8]  switch_mlp.down_proj */
+  vx_q4 shared_gate;          /* [1, Is, d/8] shared_expert.gate_proj */
+  vx_q4 shared_up;            /* [1, Is, d/8] shared_expert.up_proj   */
+  vx_q4 shared_down;          /* [1, d, Is/8] shared_expert.down_proj */
+  vx_q4 shared_expert_gate;   /* [1, 1, d/8]  mlp.shared_expert_gate  */
+  const uint16_t* router_w;   /* bf16 [E, d]  mlp.gate */
+  int32_t num_experts;
+  int32_t hidden;
+  int32_t top_k;
+} vx_moe_weights;
+
+/* Library identification and error text. */
+const char* vx_version(void);
+const char* vx_strerror(int status);
+/* Last CUDA error string seen by the library. */
+const char* vx_last_cuda_error(void);
+
+/* ---- Q4 arithmetic pieces -------------------------------------------- */
+
+/* Dequantise one expert of a bank to float32 [out, in]: scale*q + bias.
+ * Replaces mx.dequantize(..., mode="affine") (metal_runtime.py:770-777). */
+int vx_q4_dequant(const vx_q4* bank, int32_t expert, float* out, void* stream);
+
+/* h = silu(g) * u over n bf16 values with MLX's bf16 rounding sequence
+ * (metal_runtime.py:267-285; swiglu_contract.py:144-147). */
+int vx_swiglu_bf16(const uint16_t* gate, const uint16_t* up, uint16_t* out,
+                   int64_t n, void* stream);
+
+/* MLX gather_qmm with transpose=True, mode="affine", bits=4:
+ * out[b, m, :] = x[lhs[b]*M + m, :] . dequant(w[rhs[b]])^T, bf16 out
+ * [B, M, N].  lhs may be NULL (identity).  sorted_indices is a hint only.
+ * Replaces mx.gather_qmm (expert_cache.py:818-829). */
+size_t vx_gather_qmm_workspace(int64_t B, int32_t M, int32_t experts);
+int vx_gather_qmm(const uint16_t* x, int64_t x_rows, const vx_q4* w,
+                  const int32_t* lhs, const int32_t* rhs, int64_t B, int32_t M,
+                  int32_t sorted_indices, uint16_t* out, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
+/* ---- Router ----------------------------------------------------------- */
+
+/* softmax(precise) -> top-k -> selected scores -> renorm over bf16 logits
+ * [T, E] (adaptive_topk.py:59-65, :257-262; compiled.py:60-70).  Top-k
+ * order: bf16 logit descending, ties by lower expert id.  scores (raw
+ * selected probabilities) and mass may be NULL. */
+int vx_softmax_topk(const uint16_t* logits, int32_t T, int32_t E, int32_t k,
+                    int32_t* inds, uint16_t* scores, uint16_t* weights,
+                    uint16_t* mass, void* stream);
+
+/* Full router: bf16 logits = x . router_w^T, then vx_softmax_topk.  Also
+ * writes sg[t] = sigmoid(shared_expert_gate(x)) in bf16 when sg != NULL and
+ * the weights carry a shared expert gate.  logits may be NULL. */
+size_t vx_router_workspace(int32_t T, const vx_moe_weights* W);
+int vx_router(const uint16_t* x, int32_t T, const vx_moe_weights* W,
+              uint16_t* logits, int32_t* inds, uint16_t* weights, uint16_t* sg,
+              void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- Permutation ------------------------------------------------------ */
+
+/* Stable sort of P expert ids by expert (mlx-vlm _gather_sort, called at
+ * expert_cache.py:2017-2037): order[pos] = flat index at sorted position,
+ * inverse[i] = sorted position of flat index i, offsets[E+1] = run starts.
+ * Ids outside [0, E) are counted in *error_count (device int32, may be
+ * NULL) and dropped. */
+size_t vx_permute_workspace(int64_t P, int32_t E);
+int vx_permute(const int32_t* ids, int64_t P, int32_t E, int32_t* order,
+               int32_t* inverse, int32_t* offsets, int32_t* error_count,
+               void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- Routed experts and the whole block -------------------------------- */
+
+/* The executor: routed experts for given routes [T, k] (int32 expert ids)
+ * and scores [T, k] bf16 (MetalMoEExecutor.execute, metal_runtime.py:
+ * 799-974).  With scores: out [T, d] = bf16(float(bf16(sum_s
+ * float(bf16(y_s))*score_s)) + shared_y), where shared_y is shared_y[T, d],
+ * or bf16(shared[T,d]*shared_gate[T]) when given as parts, or absent.
+ * Without scores (NULL): out [T, k, d] holds each slot's bf16 output. */
+size_t vx_moe_experts_workspace(int32_t T, const vx_moe_weights* W);
+int vx_moe_experts(const uint16_t* x, int32_t T, const int32_t* routes,
+                   const uint16_t* scores, const vx_moe_weights* W,
+                   const uint16_t* shared_y, const uint16_t* shared,
+                   const uint16_t* shared_gate, uint16_t* out, void* workspace,
+                   size_t workspace_bytes, void* stream);
+
+/* The whole block, _moe_call at threshold 1.0 (adaptive_topk.py:54-293):
+ * router, top-k, renorm, shared expert and its gate, routed experts and the
+ * combine.  y [T, d] bf16.  inds/weights (may be NULL) receive the routing. */
+size_t vx_moe_block_workspace(int32_t T, const vx_moe_weights* W);
+int vx_moe_block(const uint16_t* x, int32_t T, const vx_moe_weights* W,
+                 uint16_t* y, int32_t* inds, uint16_t* weights, void* workspace,
+                 size_t workspace_bytes, void* stream);
+
+/* RMSNorm in float32 with a bf16 gain, bf16 out (patch_rmsnorm.py:96-120). */
+int vx_rmsnorm(const uint16_t* x, const uint16_t* gain, int32_t T, int32_t d,
+               float eps, uint16_t* y, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VXMOE_H */

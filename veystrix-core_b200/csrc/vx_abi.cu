@@ -1,0 +1,428 @@
+// C ABI of libvxmoe (declared in include/vxmoe.h): argument validation,
+// workspace carving and the launch sequence of each entry point.  No entry
+// point allocates device memory or synchronises the host.
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+
+#include "vx_common.cuh"
+#include "vx_launch.h"
+
+#define VX_VERSION_STRING "vxmoe 0.1.0 (sm_100a)"
+
+static thread_local char g_cuda_err[256] = "";
+
+int vx_cuda_fail(cudaError_t e) {
+  snprintf(g_cuda_err, sizeof(g_cuda_err), "%s: %s", cudaGetErrorName(e), cudaGetErrorString(e));
+  return VX_ECUDA;
+}
+
+namespace vx {
+
+int sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+// Carves 256-byte aligned pieces out of a caller workspace.  With a null
+// base it only measures.
+struct Carver {
+  char* base;
+  size_t off = 0;
+  explicit Carver(void* b) : base(static_cast<char*>(b)) {}
+  template <class T>
+  T* take(size_t n) {
+    off = (off + 255) & ~size_t(255);
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += n * sizeof(T);
+    return p;
+  }
+  size_t size() const { return (off + 255) & ~size_t(255); }
+};
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+static int check_q4(const vx_q4* b, int experts, int out, int in) {
+  if (!b || !b->w || !b->scales || !b->biases) return VX_EINVAL_SHAPE;
+  if (b->group_size != 32) return VX_EUNSUPPORTED;
+  if ((experts >= 0 && b->experts != experts) || b->out != out || b->in != in) return VX_EINVAL_SHAPE;
+  if (b->in <= 0 || b->in % 32 || b->out <= 0) return VX_EINVAL_SHAPE;
+  if (!aligned16(b->w)) return VX_EINVAL_SHAPE;
+  return VX_OK;
+}
+
+struct BlockDims {
+  int E, d, k, I, Is;
+  bool shared;
+};
+
+static int check_weights(const vx_moe_weights* W, bool need_router, BlockDims* dm) {
+  if (!W) return VX_EINVAL_SHAPE;
+  const int E = W->num_experts, d = W->hidden, k = W->top_k;
+  if (E < 1 || E > 1024 || d <= 0 || d % 32 || k < 1 || k > 16 || k > E) return VX_EINVAL_SHAPE;
+  const int I = W->gate.out;
+  int s;
+  if ((s = check_q4(&W->gate, E, I, d))) return s;
+  if ((s = check_q4(&W->up, E, I, d))) return s;
+  if ((s = check_q4(&W->down, E, d, I))) return s;
+  if (I % 32) return VX_EINVAL_SHAPE;
+  if (need_router && (!W->router_w || !aligned16(W->router_w))) return VX_EINVAL_SHAPE;
+  const bool shared = W->shared_gate.w != nullptr;
+  int Is = 0;
+  if (shared) {
+    Is = W->shared_gate.out;
+    if ((s = check_q4(&W->shared_gate, 1, Is, d))) return s;
+    if ((s = check_q4(&W->shared_up, 1, Is, d))) return s;
+    if ((s = check_q4(&W->shared_down, 1, d, Is))) return s;
+    if (Is % 32) return VX_EINVAL_SHAPE;
+    if (need_router && (s = check_q4(&W->shared_expert_gate, 1, 1, d))) return s;
+  }
+  *dm = {E, d, k, I, Is, shared};
+  return VX_OK;
+}
+
+// Scratch of the routed-expert pipeline for T tokens (P = T*k items plus
+// the shared expert's T items).
+struct ExpertScratch {
+  int32_t *order, *inverse, *offsets, *active, *n_active, *src_rows, *err;
+  uint16_t *h, *yd;
+  int64_t ldh;
+};
+
+static ExpertScratch carve_experts(Carver& c, int T, const BlockDims& dm) {
+  const int64_t P = int64_t(T) * dm.k, Ts = dm.shared ? T : 0;
+  ExpertScratch s;
+  s.order = c.take<int32_t>(P);
+  s.inverse = c.take<int32_t>(P);
+  s.offsets = c.take<int32_t>(dm.E + 2);
+  s.active = c.take<int32_t>(dm.E + 1);
+  s.n_active = c.take<int32_t>(1);
+  s.src_rows = c.take<int32_t>(P + Ts);
+  s.err = c.take<int32_t>(1);
+  s.ldh = std::max(dm.I, dm.Is);
+  s.h = c.take<uint16_t>((P + Ts) * s.ldh);
+  s.yd = c.take<uint16_t>((P + Ts) * dm.d);
+  return s;
+}
+
+// permute -> gate/up + SwiGLU -> down, leaving sorted bf16 outputs in s.yd.
+static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx_moe_weights* W,
+                       const BlockDims& dm, const ExpertScratch& s, cudaStream_t st) {
+  const int64_t P = int64_t(T) * dm.k;
+  const int Ts = dm.shared ? T : 0;
+  cudaError_t e = cudaMemsetAsync(s.err, 0, sizeof(int32_t), st);
+  if (e != cudaSuccess) return vx_cuda_fail(e);
+  e = launch_permute(routes, P, dm.E, Ts, dm.k, nullptr, s.order, s.inverse, s.offsets, s.active,
+                     s.n_active, s.src_rows, s.err, st);
+  if (e != cudaSuccess) return vx_cuda_fail(e);
+  const int max_active = int(std::min<int64_t>(dm.E, P)) + (dm.shared ? 1 : 0);
+
+  GroupedArgs a{};
+  a.b0 = W->gate;
+  a.b1 = W->up;
+  if (dm.shared) {
+    a.s0 = W->shared_gate;
+    a.s1 = W->shared_up;
+  }
+  a.E = dm.E;
+  a.offsets = s.offsets;
+  a.active = s.active;
+  a.n_active = s.n_active;
+  a.src_rows = s.src_rows;
+  a.dst_rows = nullptr;
+  a.x = x;
+  a.ldx = dm.d;
+  a.out = s.h;
+  a.ldo = s.ldh;
+  e = launch_grouped(kGateUpSwiGLU, a, max_active, int(s.ldh), dm.d, st);
+  if (e != cudaSuccess) return vx_cuda_fail(e);
+
+  GroupedArgs b{};
+  b.b0 = W->down;
+  if (dm.shared) b.s0 = W->shared_down;
+  b.E = dm.E;
+  b.offsets = s.offsets;
+  b.active = s.active;
+  b.n_active = s.n_active;
+  b.src_rows = nullptr;
+  b.dst_rows = nullptr;
+  b.x = s.h;
+  b.ldx = s.ldh;
+  b.out = s.yd;
+  b.ldo = dm.d;
+  e = launch_grouped(kProj, b, max_active, dm.d, int(s.ldh), st);
+  if (e != cudaSuccess) return vx_cuda_fail(e);
+  return VX_OK;
+}
+
+struct RouterScratch {
+  uint16_t* logits;
+};
+
+}  // namespace vx
+
+using namespace vx;
+
+extern "C" {
+
+const char* vx_version(void) { return VX_VERSION_STRING; }
+
+const char* vx_strerror(int status) {
+  switch (status) {
+    case VX_OK: return "ok";
+    case VX_EINVAL_SHAPE: return "invalid shape or size";
+    case VX_EINVAL_DTYPE: return "invalid dtype";
+    case VX_EINVAL_INDEX: return "index out of range";
+    case VX_ECUDA: return "CUDA error";
+    case VX_ETIMEOUT: return "timed out";
+    case VX_EWORKSPACE: return "workspace too small";
+    case VX_EUNSUPPORTED: return "unsupported configuration";
+    default: return "unknown status";
+  }
+}
+
+const char* vx_last_cuda_error(void) { return g_cuda_err; }
+
+int vx_q4_dequant(const vx_q4* bank, int32_t expert, float* out, void* stream) {
+  if (!bank || !out || !bank->w || !bank->scales || !bank->biases) return VX_EINVAL_SHAPE;
+  if (bank->group_size <= 0 || bank->in % bank->group_size || bank->in % 8) return VX_EINVAL_SHAPE;
+  if (expert < 0 || expert >= bank->experts) return VX_EINVAL_INDEX;
+  cudaError_t e = launch_dequant(*bank, expert, out, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? VX_OK : vx_cuda_fail(e);
+}
+
+int vx_swiglu_bf16(const uint16_t* gate, const uint16_t* up, uint16_t* out, int64_t n,
+                   void* stream) {
+  if (n < 0 || (n > 0 && (!gate || !up || !out))) return VX_EINVAL_SHAPE;
+  cudaError_t e = launch_swiglu(gate, up, out, n, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? VX_OK : vx_cuda_fail(e);
+}
+
+size_t vx_gather_qmm_workspace(int64_t B, int32_t M, int32_t experts) {
+  Carver c(nullptr);
+  const int64_t n = B * M;
+  c.take<int32_t>(n);            // keys
+  c.take<int32_t>(n);            // src_map
+  c.take<int32_t>(n);            // order
+  c.take<int32_t>(n);            // inverse
+  c.take<int32_t>(experts + 2);  // offsets
+  c.take<int32_t>(experts + 1);  // active
+  c.take<int32_t>(1);            // n_active
+  c.take<int32_t>(n);            // src_rows
+  c.take<int32_t>(1);            // err
+  return c.size();
+}
+
+int vx_gather_qmm(const uint16_t* x, int64_t x_rows, const vx_q4* w, const int32_t* lhs,
+                  const int32_t* rhs, int64_t B, int32_t M, int32_t sorted_indices, uint16_t* out,
+                  void* workspace, size_t workspace_bytes, void* stream) {
+  (void)sorted_indices;
+  (void)x_rows;
+  if (!w || B < 0 || M < 1) return VX_EINVAL_SHAPE;
+  int s = check_q4(w, w->experts, w->out, w->in);
+  if (s) return s;
+  if (w->experts < 1 || w->experts > 1024) return VX_EUNSUPPORTED;
+  if (B * M > 0x7FFFFFFF) return VX_EUNSUPPORTED;
+  if (B == 0) return VX_OK;
+  if (!x || !rhs || !out || !aligned16(x)) return VX_EINVAL_SHAPE;
+  if (workspace_bytes < vx_gather_qmm_workspace(B, M, w->experts) || !workspace) return VX_EWORKSPACE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t n = B * M;
+  const int E = w->experts;
+  Carver c(workspace);
+  int32_t* keys = c.take<int32_t>(n);
+  int32_t* src_map = c.take<int32_t>(n);
+  int32_t* order = c.take<int32_t>(n);
+  int32_t* inverse = c.take<int32_t>(n);
+  int32_t* offsets = c.take<int32_t>(E + 2);
+  int32_t* active = c.take<int32_t>(E + 1);
+  int32_t* n_active = c.take<int32_t>(1);
+  int32_t* src_rows = c.take<int32_t>(n);
+  int32_t* err = c.take<int32_t>(1);
+  cudaError_t e = cudaMemsetAsync(err, 0, sizeof(int32_t), st);
+  if (e == cudaSuccess) e = launch_gather_items(lhs, rhs, B, M, keys, src_map, st);
+  if (e == cudaSuccess)
+    e = launch_permute(keys, n, E, 0, 1, src_map, order, inverse, offsets, active, n_active, src_rows,
+                       err, st);
+  if (e != cudaSuccess) return vx_cuda_fail(e);
+  GroupedArgs a{};
+  a.b0 = *w;
+  a.E = E;
+  a.offsets = offsets;
+  a.active = active;
+  a.n_active = n_active;
+  a.src_rows = src_rows;
+  a.dst_rows = order;
+  a.x = x;
+  a.ldx = w->in;
+  a.out = out;
+  a.ldo = w->out;
+  e = launch_grouped(kProj, a, int(std::min<int64_t>(E, n)), w->out, w->in, st);
+  return e == cudaSuccess ? VX_OK : vx_cuda_fail(e);
+}
+
+int vx_softmax_topk(const uint16_t* logits, int32_t T, int32_t E, int32_t k, int32_t* inds,
+                    uint16_t* scores, uint16_t* weights, uint16_t* mass, void* stream) {
+  if (T < 0 || E < 1 || E > 1024 || k < 1 || k > 16 || k > E) return VX_EINVAL_SHAPE;
+  if (T == 0) return VX_OK;
+  if (!logits || !inds || !weights) return VX_EINVAL_SHAPE;
+  cudaError_t e = launch_softmax_topk(logits, T, E, k, inds, scores, weights, mass,
+                                      static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? VX_OK : vx_cuda_fail(e);
+}
+
+size_t vx_router_workspace(int32_t T, const vx_moe_weights* W) {
+  if (!W || T < 0) return 0;
+  Carver c(nullptr);
+  c.take<uint16_t>(int64_t(T) * W->num_experts);
+  return c.size();
+}
+
+static int router_impl(const uint16_t* x, int T, const vx_moe_weights* W, const BlockDims& dm,
+                       uint16_t* logits, int32_t* inds, uint16_t* weights, uint16_t* sg,
+                       cudaStream_t st) {
+  cudaError_t e = launch_router_logits(x, T, W->router_w, dm.E, dm.d, logits, st);
+  if (e == cudaSuccess) e = launch_softmax_topk(logits, T, dm.E, dm.k, inds, nullptr, weights, nullptr, st);
+  if (e == cudaSuccess && sg && W->shared_expert_gate.w) e = launch_shared_gate(x, T, W->shared_expert_gate, sg, st);
+  return e == cudaSuccess ? VX_OK : vx_cuda_fail(e);
+}
+
+int vx_router(const uint16_t* x, int32_t T, const vx_moe_weights* W, uint16_t* logits,
+              int32_t* inds, uint16_t* weights, uint16_t* sg, void* workspace,
+              size_t workspace_bytes, void* stream) {
+  BlockDims dm;
+  int s = check_weights(W, true, &dm);
+  if (s) return s;
+  if (T < 0) return VX_EINVAL_SHAPE;
+  if (T == 0) return VX_OK;
+  if (!x || !inds || !weights || !aligned16(x)) return VX_EINVAL_SHAPE;
+  if (!logits) {
+    if (!workspace || workspace_bytes < vx_router_workspace(T, W)) return VX_EWORKSPACE;
+    Carver c(workspace);
+    logits = c.take<uint16_t>(int64_t(T) * dm.E);
+  }
+  return router_impl(x, T, W, dm, logits, inds, weights, sg, static_cast<cudaStream_t>(stream));
+}
+
+size_t vx_permute_workspace(int64_t P, int32_t E) {
+  Carver c(nullptr);
+  c.take<int32_t>(E + 1);
+  c.take<int32_t>(1);
+  return c.size();
+}
+
+int vx_permute(const int32_t* ids, int64_t P, int32_t E, int32_t* order, int32_t* inverse,
+               int32_t* offsets, int32_t* error_count, void* workspace, size_t workspace_bytes,
+               void* stream) {
+  if (P < 0 || P > 0x7FFFFFFF || E < 1 || E > 4096) return VX_EINVAL_SHAPE;
+  if (!offsets) return VX_EINVAL_SHAPE;
+  if (P > 0 && (!ids || !order || !inverse)) return VX_EINVAL_SHAPE;
+  if (!workspace || workspace_bytes < vx_permute_workspace(P, E)) return VX_EWORKSPACE;
+  Carver c(workspace);
+  int32_t* active = c.take<int32_t>(E + 1);
+  int32_t* n_active = c.take<int32_t>(1);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = launch_permute(ids, P, E, -1, 1, nullptr, order, inverse, offsets, active, n_active,
+                                 nullptr, error_count, st);
+  return e == cudaSuccess ? VX_OK : vx_cuda_fail(e);
+}
+
+size_t vx_moe_experts_workspace(int32_t T, const vx_moe_weights* W) {
+  if (!W || T < 0) return 0;
+  BlockDims dm{W->num_experts, W->hidden, W->top_k, W->gate.out, 0, false};
+  Carver c(nullptr);
+  carve_experts(c, T, dm);
+  return c.size();
+}
+
+int vx_moe_experts(const uint16_t* x, int32_t T, const int32_t* routes, const uint16_t* scores,
+                   const vx_moe_weights* W, const uint16_t* shared_y, const uint16_t* shared,
+                   const uint16_t* shared_gate, uint16_t* out, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+  BlockDims dm;
+  int s = check_weights(W, false, &dm);
+  if (s) return s;
+  dm.shared = false;  // the executor takes the shared expert from its caller
+  dm.Is = 0;
+  if (T < 0) return VX_EINVAL_SHAPE;
+  if ((shared == nullptr) != (shared_gate == nullptr)) return VX_EINVAL_SHAPE;
+  if (shared_y && shared) return VX_EINVAL_SHAPE;
+  if (T == 0) return VX_OK;
+  if (!x || !routes || !out || !aligned16(x)) return VX_EINVAL_SHAPE;
+  if (!workspace || workspace_bytes < vx_moe_experts_workspace(T, W)) return VX_EWORKSPACE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carver c(workspace);
+  ExpertScratch es = carve_experts(c, T, dm);
+  s = run_experts(x, T, routes, W, dm, es, st);
+  if (s) return s;
+  cudaError_t e;
+  if (scores) {
+    SharedMode mode = shared_y ? kSharedY : (shared ? kSharedParts : kSharedNone);
+    e = launch_combine(es.yd, dm.d, es.inverse, scores, T, dm.k, dm.d, mode, es.offsets, dm.E,
+                       nullptr, shared_y, shared, shared_gate, out, st);
+  } else {
+    e = launch_unpermute(es.yd, dm.d, es.inverse, T, dm.k, dm.d, out, st);
+  }
+  return e == cudaSuccess ? VX_OK : vx_cuda_fail(e);
+}
+
+size_t vx_moe_block_workspace(int32_t T, const vx_moe_weights* W) {
+  if (!W || T < 0) return 0;
+  const bool shared = W->shared_gate.w != nullptr;
+  BlockDims dm{W->num_experts, W->hidden, W->top_k, W->gate.out, shared ? W->shared_gate.out : 0,
+               shared};
+  Carver c(nullptr);
+  c.take<uint16_t>(int64_t(T) * dm.E);   // logits
+  c.take<int32_t>(int64_t(T) * dm.k);    // inds
+  c.take<uint16_t>(int64_t(T) * dm.k);   // weights
+  c.take<uint16_t>(T);                   // sg
+  carve_experts(c, T, dm);
+  return c.size();
+}
+
+int vx_moe_block(const uint16_t* x, int32_t T, const vx_moe_weights* W, uint16_t* y, int32_t* inds,
+                 uint16_t* weights, void* workspace, size_t workspace_bytes, void* stream) {
+  BlockDims dm;
+  int s = check_weights(W, true, &dm);
+  if (s) return s;
+  if (T < 0) return VX_EINVAL_SHAPE;
+  if (T == 0) return VX_OK;
+  if (!x || !y || !aligned16(x)) return VX_EINVAL_SHAPE;
+  if (!workspace || workspace_bytes < vx_moe_block_workspace(T, W)) return VX_EWORKSPACE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carver c(workspace);
+  uint16_t* logits = c.take<uint16_t>(int64_t(T) * dm.E);
+  int32_t* inds_ws = c.take<int32_t>(int64_t(T) * dm.k);
+  uint16_t* w_ws = c.take<uint16_t>(int64_t(T) * dm.k);
+  uint16_t* sg = c.take<uint16_t>(T);
+  ExpertScratch es = carve_experts(c, T, dm);
+  if (!inds) inds = inds_ws;
+  if (!weights) weights = w_ws;
+  s = router_impl(x, T, W, dm, logits, inds, weights, dm.shared ? sg : nullptr, st);
+  if (s) return s;
+  s = run_experts(x, T, inds, W, dm, es, st);
+  if (s) return s;
+  cudaError_t e = launch_combine(es.yd, dm.d, es.inverse, weights, T, dm.k, dm.d,
+                                 dm.shared ? kSharedInternal : kSharedNone, es.offsets, dm.E, sg,
+                                 nullptr, nullptr, nullptr, y, st);
+  return e == cudaSuccess ? VX_OK : vx_cuda_fail(e);
+}
+
+int vx_rmsnorm(const uint16_t* x, const uint16_t* gain, int32_t T, int32_t d, float eps, uint16_t* y,
+               void* stream) {
+  if (T < 0 || d <= 0) return VX_EINVAL_SHAPE;
+  if (T == 0) return VX_OK;
+  if (!x || !gain || !y) return VX_EINVAL_SHAPE;
+  cudaError_t e = launch_rmsnorm(x, gain, T, d, eps, y, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? VX_OK : vx_cuda_fail(e);
+}
+
+}  // extern "C"

@@ -1,0 +1,112 @@
+// Shared device helpers for the vxmoe kernels (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "vxmoe.h"
+
+#define VX_DEVICE __device__ __forceinline__
+
+namespace vx {
+
+constexpr int kWarp = 32;
+
+// ---------------------------------------------------------------------------
+// bf16 as bit patterns.  Round-to-nearest-even, NaN kept quiet.
+// ---------------------------------------------------------------------------
+
+VX_DEVICE float bf16_to_f32(uint16_t b) { return __uint_as_float(uint32_t(b) << 16); }
+
+VX_DEVICE uint16_t f32_to_bf16(float f) {
+  uint32_t u = __float_as_uint(f);
+  if ((u & 0x7FFFFFFFu) > 0x7F800000u) return uint16_t((u >> 16) | 0x0040u);
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return uint16_t(u >> 16);
+}
+
+// Value of f rounded to bf16, kept as float.
+VX_DEVICE float bf16r(float f) { return bf16_to_f32(f32_to_bf16(f)); }
+
+// float32 exp(m) rounded to bf16 as if the float32 exp were correctly
+// rounded.  The library expf is within a few ulp; when its result sits close
+// to a bf16 rounding boundary the value is recomputed in double precision, so
+// the bf16 result is the rounding of the exact float32 exp.
+VX_DEVICE float bf16_exp(float m) {
+  float e = expf(m);
+  uint32_t low = __float_as_uint(e) & 0xFFFFu;
+  if (low >= 0x7FF0u && low <= 0x8010u) e = float(exp(double(m)));
+  return bf16r(e);
+}
+
+// MLX's stable bf16 sigmoid: every step rounded to bf16.
+// t = exp(|z|); s = 1/(1+t); sigma = z<0 ? s : 1-s.
+VX_DEVICE float sigmoid_bf16(float z) {
+  float t = bf16_exp(fabsf(z));
+  float den = bf16r(__fadd_rn(1.0f, t));
+  float s = bf16r(__fdiv_rn(1.0f, den));
+  return z < 0.0f ? s : bf16r(__fsub_rn(1.0f, s));
+}
+
+// h = silu(g) * u in bf16 (g, u already bf16 values).
+VX_DEVICE float silu_mul_bf16(float g, float u) {
+  float sg = sigmoid_bf16(g);
+  float silu = bf16r(__fmul_rn(g, sg));
+  return bf16r(__fmul_rn(silu, u));
+}
+
+// ---------------------------------------------------------------------------
+// Q4 nibbles.  For the 16-bit half h of a word, nibble p (0..3) is
+// (h >> 4p) & 15.  OR-ing the masked half into the float 2^23 and
+// subtracting 2^23 yields q * 16^p exactly (q*16^p < 2^16); the matching
+// activation is pre-scaled by 16^-p, so each product equals q*x.
+// ---------------------------------------------------------------------------
+
+VX_DEVICE float nib_scaled(uint32_t half, int p) {
+  return __uint_as_float((half & (0xFu << (4 * p))) | 0x4B000000u) - 8388608.0f;
+}
+
+VX_DEVICE uint32_t nibble(uint32_t w, int i) { return (w >> (4 * i)) & 0xFu; }
+
+// ---------------------------------------------------------------------------
+// Warp reductions
+// ---------------------------------------------------------------------------
+
+template <int WIDTH>
+VX_DEVICE float warp_sum(float v) {
+#pragma unroll
+  for (int o = WIDTH / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o, WIDTH);
+  return v;
+}
+
+VX_DEVICE float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+  return v;
+}
+
+// Address of expert e's rows in a bank (int64 offsets: a full bank of 512
+// experts spans more than 2^31 bytes).
+struct Q4Ptr {
+  const uint32_t* w;
+  const uint16_t* s;
+  const uint16_t* b;
+};
+
+VX_DEVICE Q4Ptr q4_expert(const vx_q4& bank, int e) {
+  const int64_t words = int64_t(bank.out) * (bank.in / 8);
+  const int64_t groups = int64_t(bank.out) * (bank.in / bank.group_size);
+  return {bank.w + int64_t(e) * words, bank.scales + int64_t(e) * groups,
+          bank.biases + int64_t(e) * groups};
+}
+
+}  // namespace vx
+
+// Host-side launch check used by every entry point.
+int vx_cuda_fail(cudaError_t e);
+
+#define VX_LAUNCH_CHECK()                                   \
+  do {                                                      \
+    cudaError_t _e = cudaGetLastError();                    \
+    if (_e != cudaSuccess) return vx_cuda_fail(_e);         \
+  } while (0)

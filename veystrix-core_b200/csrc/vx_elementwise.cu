@@ -1,0 +1,160 @@
+// Combine, unpermute, RMSNorm and the small Q4/bf16 contract kernels.
+#include "vx_common.cuh"
+#include "vx_launch.h"
+
+namespace vx {
+
+// Score-weighted combine of the routed outputs, in the order of the fused
+// down+combine kernel of the reference (metal_runtime.py:315-334, patched
+// helpers :404-410): every slot's output is already bf16; it is multiplied
+// by its score and accumulated in float32 in slot order without fused
+// multiply-add; the sum is rounded to bf16, then the shared component is
+// added in float32 and the result rounded to bf16.
+__global__ void __launch_bounds__(256) combine_kernel(
+    const uint16_t* __restrict__ yd, int64_t ldy, const int32_t* __restrict__ inverse,
+    const uint16_t* __restrict__ weights, int T, int k, int d, int mode,
+    const int32_t* __restrict__ offsets, int E, const uint16_t* __restrict__ sg,
+    const uint16_t* __restrict__ shared_y, const uint16_t* __restrict__ shared,
+    const uint16_t* __restrict__ shared_gate, uint16_t* __restrict__ y) {
+  const int t = blockIdx.y;
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 2;
+  if (c >= d) return;
+  float a0 = 0.f, a1 = 0.f;
+  for (int s = 0; s < k; ++s) {
+    const int pos = inverse[int64_t(t) * k + s];
+    if (pos < 0) continue;
+    const float w = bf16_to_f32(weights[int64_t(t) * k + s]);
+    const uint32_t v = *reinterpret_cast<const uint32_t*>(yd + int64_t(pos) * ldy + c);
+    a0 = __fadd_rn(a0, __fmul_rn(__uint_as_float(v << 16), w));
+    a1 = __fadd_rn(a1, __fmul_rn(__uint_as_float(v & 0xFFFF0000u), w));
+  }
+  float r0 = bf16r(a0), r1 = bf16r(a1);
+  if (mode != kSharedNone) {
+    float s0, s1;
+    if (mode == kSharedY) {
+      const uint32_t v = *reinterpret_cast<const uint32_t*>(shared_y + int64_t(t) * d + c);
+      s0 = __uint_as_float(v << 16);
+      s1 = __uint_as_float(v & 0xFFFF0000u);
+    } else {
+      const uint16_t* srow;
+      float gate;
+      if (mode == kSharedInternal) {
+        srow = yd + int64_t(offsets[E] + t) * ldy;
+        gate = bf16_to_f32(sg[t]);
+      } else {
+        srow = shared + int64_t(t) * d;
+        gate = bf16_to_f32(shared_gate[t]);
+      }
+      const uint32_t v = *reinterpret_cast<const uint32_t*>(srow + c);
+      s0 = bf16r(__fmul_rn(__uint_as_float(v << 16), gate));
+      s1 = bf16r(__fmul_rn(__uint_as_float(v & 0xFFFF0000u), gate));
+    }
+    r0 = bf16r(__fadd_rn(r0, s0));
+    r1 = bf16r(__fadd_rn(r1, s1));
+  }
+  const uint32_t outv = uint32_t(f32_to_bf16(r0)) | (uint32_t(f32_to_bf16(r1)) << 16);
+  *reinterpret_cast<uint32_t*>(y + int64_t(t) * d + c) = outv;
+}
+
+cudaError_t launch_combine(const uint16_t* yd, int64_t ldy, const int32_t* inverse,
+                           const uint16_t* weights, int T, int k, int d, SharedMode mode,
+                           const int32_t* offsets, int E, const uint16_t* sg,
+                           const uint16_t* shared_y, const uint16_t* shared,
+                           const uint16_t* shared_gate, uint16_t* y, cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  dim3 grid((d / 2 + 255) / 256, T);
+  combine_kernel<<<grid, 256, 0, st>>>(yd, ldy, inverse, weights, T, k, d, int(mode), offsets, E, sg,
+                                       shared_y, shared, shared_gate, y);
+  return cudaGetLastError();
+}
+
+// out[t, s, :] = yd[inverse[t*k+s], :]  (_scatter_unsort)
+__global__ void unpermute_kernel(const uint16_t* __restrict__ yd, int64_t ldy,
+                                 const int32_t* __restrict__ inverse, int k, int d,
+                                 uint16_t* __restrict__ out) {
+  const int64_t pair = blockIdx.y;
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 2;
+  if (c >= d) return;
+  const int pos = inverse[pair];
+  uint32_t v = 0;
+  if (pos >= 0) v = *reinterpret_cast<const uint32_t*>(yd + int64_t(pos) * ldy + c);
+  *reinterpret_cast<uint32_t*>(out + pair * d + c) = v;
+}
+
+cudaError_t launch_unpermute(const uint16_t* yd, int64_t ldy, const int32_t* inverse, int T,
+                             int k, int d, uint16_t* out, cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  dim3 grid((d / 2 + 255) / 256, T * k);
+  unpermute_kernel<<<grid, 256, 0, st>>>(yd, ldy, inverse, k, d, out);
+  return cudaGetLastError();
+}
+
+// RMSNorm (patch_rmsnorm.py:96-120): y = bf16(x * (1/sqrt(mean(x^2)+eps)) * gain)
+// with float32 arithmetic; one CTA per row.
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const uint16_t* __restrict__ x,
+                                                      const uint16_t* __restrict__ gain, int d,
+                                                      float eps, uint16_t* __restrict__ y) {
+  const int64_t t = blockIdx.x;
+  const uint16_t* xr = x + t * d;
+  float s = 0.f;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    const float v = bf16_to_f32(xr[i]);
+    s = fmaf(v, v, s);
+  }
+  __shared__ float red[8];
+  s = warp_sum<32>(s);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  float tot = 0.f;
+  for (int w = 0; w < int(blockDim.x >> 5); ++w) tot += red[w];
+  const float ms = __fdiv_rn(tot, float(d));
+  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    const float v = __fmul_rn(__fmul_rn(bf16_to_f32(xr[i]), r), bf16_to_f32(gain[i]));
+    y[t * d + i] = f32_to_bf16(v);
+  }
+}
+
+cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* gain, int T, int d, float eps,
+                           uint16_t* y, cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  rmsnorm_kernel<<<T, 256, 0, st>>>(x, gain, d, eps, y);
+  return cudaGetLastError();
+}
+
+__global__ void swiglu_kernel(const uint16_t* __restrict__ g, const uint16_t* __restrict__ u,
+                              uint16_t* __restrict__ out, int64_t n) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  out[i] = f32_to_bf16(silu_mul_bf16(bf16_to_f32(g[i]), bf16_to_f32(u[i])));
+}
+
+cudaError_t launch_swiglu(const uint16_t* g, const uint16_t* u, uint16_t* out, int64_t n,
+                          cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  swiglu_kernel<<<int((n + 255) / 256), 256, 0, st>>>(g, u, out, n);
+  return cudaGetLastError();
+}
+
+// Dequantise expert e: out[r, i] = scale*q + bias (scale*q is exact in fp32,
+// so one rounding, metal_runtime.py:1026-1027).
+__global__ void dequant_kernel(vx_q4 bank, int e, float* __restrict__ out) {
+  const int64_t n = int64_t(bank.out) * bank.in;
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const Q4Ptr p = q4_expert(bank, e);
+  const int64_t r = i / bank.in, k = i - r * bank.in;
+  const uint32_t w = p.w[r * (bank.in / 8) + k / 8];
+  const int64_t gi = r * (bank.in / bank.group_size) + k / bank.group_size;
+  const float q = float(nibble(w, int(k & 7)));
+  out[i] = __fadd_rn(__fmul_rn(bf16_to_f32(p.s[gi]), q), bf16_to_f32(p.b[gi]));
+}
+
+cudaError_t launch_dequant(const vx_q4& bank, int expert, float* out, cudaStream_t st) {
+  const int64_t n = int64_t(bank.out) * bank.in;
+  if (n == 0) return cudaSuccess;
+  dequant_kernel<<<int((n + 255) / 256), 256, 0, st>>>(bank, expert, out);
+  return cudaGetLastError();
+}
+
+}  // namespace vx

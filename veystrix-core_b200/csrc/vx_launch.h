@@ -1,0 +1,68 @@
+// Host-side launchers shared between the kernel files and the C ABI layer.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "vxmoe.h"
+
+namespace vx {
+
+// Items of a grouped projection, sorted by expert.  Expert id E is the
+// shared expert; its items sit at [offsets[E], offsets[E+1]).
+struct GroupedArgs {
+  vx_q4 b0, b1;          // routed banks (b1: up bank in gate/up mode)
+  vx_q4 s0, s1;          // shared-expert banks (expert id E); w may be null
+  int E;
+  const int32_t* offsets;   // [E+2]
+  const int32_t* active;    // experts that own items
+  const int32_t* n_active;  // device count of `active`
+  const int32_t* src_rows;  // x row of each sorted position (null: identity)
+  const int32_t* dst_rows;  // out row of each sorted position (null: identity)
+  const uint16_t* x;        // bf16 [*, ldx]
+  int64_t ldx;
+  uint16_t* out;            // bf16 [*, ldo]
+  int64_t ldo;
+  int tiles_per_expert;
+};
+
+enum GroupedMode { kProj = 0, kGateUpSwiGLU = 1 };
+
+int sm_count();
+
+// Upper bound of experts with items: min(E, items) + shared.
+cudaError_t launch_grouped(GroupedMode mode, const GroupedArgs& a, int max_active, int max_out,
+                           int max_in, cudaStream_t st);
+
+cudaError_t launch_permute(const int32_t* ids, int64_t P, int E, int shared_items, int k_div,
+                           const int32_t* src_map, int32_t* order, int32_t* inverse,
+                           int32_t* offsets, int32_t* active, int32_t* n_active,
+                           int32_t* src_rows, int32_t* err, cudaStream_t st);
+
+cudaError_t launch_router_logits(const uint16_t* x, int T, const uint16_t* wg, int E, int K,
+                                 uint16_t* logits, cudaStream_t st);
+cudaError_t launch_shared_gate(const uint16_t* x, int T, const vx_q4& seg, uint16_t* sg,
+                               cudaStream_t st);
+cudaError_t launch_softmax_topk(const uint16_t* logits, int T, int E, int k, int32_t* inds,
+                                uint16_t* scores, uint16_t* weights, uint16_t* mass,
+                                cudaStream_t st);
+
+// Combine modes for the shared part.
+enum SharedMode { kSharedNone = 0, kSharedInternal = 1, kSharedY = 2, kSharedParts = 3 };
+
+cudaError_t launch_combine(const uint16_t* yd, int64_t ldy, const int32_t* inverse,
+                           const uint16_t* weights, int T, int k, int d, SharedMode mode,
+                           const int32_t* offsets, int E, const uint16_t* sg,
+                           const uint16_t* shared_y, const uint16_t* shared,
+                           const uint16_t* shared_gate, uint16_t* y, cudaStream_t st);
+cudaError_t launch_unpermute(const uint16_t* yd, int64_t ldy, const int32_t* inverse, int T,
+                             int k, int d, uint16_t* out, cudaStream_t st);
+cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* gain, int T, int d, float eps,
+                           uint16_t* y, cudaStream_t st);
+cudaError_t launch_swiglu(const uint16_t* g, const uint16_t* u, uint16_t* out, int64_t n,
+                          cudaStream_t st);
+cudaError_t launch_dequant(const vx_q4& bank, int expert, float* out, cudaStream_t st);
+cudaError_t launch_gather_items(const int32_t* lhs, const int32_t* rhs, int64_t B, int M,
+                                int32_t* keys, int32_t* src_map, cudaStream_t st);
+
+}  // namespace vx
