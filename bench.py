@@ -1,0 +1,351 @@
+"""Benchmark of the routed sparse-MoE layer on B200 (one JSON line on rank 0).
+
+Workload: one MoE layer, a batch of 64 independent decode
+tokens per GPU, hidden 2048, 512 routed experts (top-10, renormalised) plus
+one shared expert, SwiGLU experts with intermediate 512, 4-bit affine
+group-32 weights; x bf16 ~N(0,1), synthetic random-init weights with the
+benchmark distributions.  A step is one pass of the block over one batch.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl vxmoe|reference]
+
+value      tokens/s over all ranks, inputs resident in HBM, device-timed
+           (CUDA events, max over ranks); weights rotate over several pools
+           so the working set is far larger than L2.
+e2e        the same through the public API with x copied from pinned host
+           memory and y copied back inside the timed region.
+roofline   the dominant kernel's algorithmic bytes per launch over its
+           CUDA-event duration against the measured HBM copy bandwidth.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "veystrix-core_b200"))
+
+METRIC = "MoE-layer tokens/s and achieved HBM GB/s (% of 8 TB/s) at 1/2/4/8 B200"
+HIDDEN, EXPERTS, INTER, SHARED_INTER, TOPK = 2048, 512, 512, 512, 10
+EXPERT_BYTES = 3 * (INTER * HIDDEN // 2 + 2 * INTER * (HIDDEN // 32) * 2)   # 1,966,080
+PROJ_BYTES = EXPERT_BYTES // 3                                               # 655,360
+ROUTER_BYTES = EXPERTS * HIDDEN * 2
+SHARED_GATE_BYTES = HIDDEN // 2 + 2 * (HIDDEN // 32) * 2                     # 1,280
+NOMINAL_HBM_GBS = 8000.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="vxmoe", choices=("vxmoe", "reference"))
+    ap.add_argument("--tokens", type=int, default=64)
+    ap.add_argument("--pools", type=int, default=4)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            d = json.load(fh)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def layer_bytes(U, T):
+    """Algorithmic bytes of one layer step: each touched expert once, the
+    shared expert, the router, the shared gate row, x in and y out."""
+    return U * EXPERT_BYTES + EXPERT_BYTES + ROUTER_BYTES + SHARED_GATE_BYTES + T * HIDDEN * 2 * 2
+
+
+def stage_bytes(stage, U, T):
+    P = T * TOPK
+    if stage == "gate_up_swiglu":
+        return (U + 1) * 2 * PROJ_BYTES + T * HIDDEN * 2 + (P + T) * INTER * 2
+    if stage == "down":
+        return (U + 1) * PROJ_BYTES + (P + T) * INTER * 2 + (P + T) * HIDDEN * 2
+    if stage == "router_logits":
+        return ROUTER_BYTES + T * HIDDEN * 2 + T * EXPERTS * 2
+    return None
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.path = tempfile.mktemp(suffix=".csv")
+        self.fh = open(self.path, "w")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(index)], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.fh.close()
+        sm, mx, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# --------------------------------------------------------------------------
+# reference arm: the CPU restatement of the block on this host's cores
+# --------------------------------------------------------------------------
+
+
+def cpu_oracle_time(tokens_per_step, steps, warmup, seed=0):
+    """Time the oracle's block on `tokens_per_step` tokens per step.
+    Returns (tokens/s, cores, kind, sample description)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import vxmoe_oracle as O
+    try:
+        import vxmoe_cref as C   # C/OpenMP restatement, when built
+        runner, cores, kind = C.block_runner(seed), C.threads(), "port"
+        params = None
+    except Exception:
+        C = None
+        params = O.make_params(seed=seed)
+        runner, cores, kind = (lambda x: O.moe_block(x, params)), 1, "port"
+    rng = np.random.default_rng(seed + 1)
+    xs = [O.bf16_round(rng.normal(0, 1, size=(tokens_per_step, HIDDEN))) for _ in range(steps + warmup)]
+    for i in range(warmup):
+        runner(xs[i])
+    t0 = time.perf_counter()
+    for i in range(steps):
+        runner(xs[warmup + i])
+    dt = time.perf_counter() - t0
+    impl = "C/OpenMP restatement" if C is not None else "NumPy restatement"
+    sample = (f"{impl} of the block (MLX unavailable), {steps} steps x {tokens_per_step} tokens "
+              f"of the same layer shape")
+    return steps * tokens_per_step / dt, cores, kind, sample
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    per_step = 1
+    v, cores, kind, sample = cpu_oracle_time(per_step, args.steps, max(1, min(args.warmup, 3)))
+    line = {
+        "metric": METRIC, "value": round(v, 3), "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000.0 * per_step / v, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "impl": "reference",
+        "config": config_dict(args, world),
+        "cpu_baseline": {"value": round(v, 3), "unit": "tokens/s", "cores": cores, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": round(v, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(args, world):
+    return {
+        "workload": ("BASELINE config 2: one MoE layer, batched decode of %d tokens per GPU, "
+                     "d=2048, 512 routed experts top-10 + 1 shared, SwiGLU I=512, Q4 affine g32"
+                     % args.tokens),
+        "global_batch": args.tokens * world, "tokens_per_gpu": args.tokens,
+        "experts": EXPERTS, "hidden": HIDDEN, "intermediate": INTER, "top_k": TOPK,
+        "parallelism": "replicas" if world > 1 else "single",
+        "l2": f"inputs larger than L2: {args.pools} rotating weight pools of {EXPERTS} experts",
+    }
+
+
+# --------------------------------------------------------------------------
+# vxmoe arm
+# --------------------------------------------------------------------------
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    import torch
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+
+    import vxmoe
+    from vxmoe import _lib
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    T = args.tokens
+    K, W = args.steps, max(3, args.warmup)
+    g = torch.Generator(device=dev)
+    pools = []
+    for i in range(args.pools):
+        g.manual_seed(1000 * rank + i)
+        pools.append(vxmoe.MoEWeights.random(EXPERTS, HIDDEN, INTER, SHARED_INTER, TOPK, device=dev,
+                                             generator=g))
+    g.manual_seed(7 + rank)
+    nx = K + W
+    xs = (torch.randn((nx, T, HIDDEN), device=dev, generator=g)).to(torch.bfloat16)
+    torch.cuda.synchronize()
+
+    def step(i):
+        return vxmoe.moe_block(xs[i], pools[i % len(pools)])
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if dist is None:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    stream = torch.cuda.current_stream(dev)
+    for i in range(W):
+        step(i)
+    barrier()
+    sampler = ClockSampler(dev.index) if rank == 0 else None
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    for i in range(K):
+        step(W + i)
+    e1.record(stream)
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+
+    # end to end: pinned host x -> device -> block -> pinned host y
+    hx = xs[W:W + K].cpu().pin_memory()
+    hy = torch.empty((K, T, HIDDEN), dtype=torch.bfloat16).pin_memory()
+    dx = torch.empty((T, HIDDEN), dtype=torch.bfloat16, device=dev)
+    for i in range(W):
+        dx.copy_(hx[i % K], non_blocking=True)
+        hy[i % K].copy_(vxmoe.moe_block(dx, pools[i % len(pools)]), non_blocking=True)
+    barrier()
+    e0.record(stream)
+    for i in range(K):
+        dx.copy_(hx[i], non_blocking=True)
+        y = vxmoe.moe_block(dx, pools[(W + i) % len(pools)])
+        hy[i].copy_(y, non_blocking=True)
+    e1.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    clocks = sampler.stop() if sampler else None
+
+    # routing statistics (outside the timed regions): distinct experts per step
+    Us = []
+    for i in range(K):
+        r = vxmoe.router(xs[W + i], pools[(W + i) % len(pools)])
+        Us.append(int(torch.unique(r.inds).numel()))
+    U_mean = sum(Us) / len(Us)
+
+    # per-kernel durations: the same steps again with stage events
+    _lib.profile_enable(True)
+    for i in range(K):
+        step(W + i)
+    stages = _lib.profile_read()
+    _lib.profile_enable(False)
+    barrier()
+
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    hbm_gbs, _, peak_kind = peaks()
+    value = K * T * world / (ms / 1000.0)
+    total_bytes = sum(layer_bytes(U, T) for U in Us)
+    achieved_layer = total_bytes / (ms / 1000.0) / 1e9
+    dom = max(stages, key=lambda s: stages[s][1]) if stages else None
+    roof = None
+    if dom is not None:
+        b = stage_bytes(dom, U_mean, T)
+        avg_ms = stages[dom][1]
+        ach = b / (avg_ms / 1000.0) / 1e9 if b else None
+        roof = {"kernel": dom, "bound": "hbm", "achieved": round(ach, 1) if ach else None,
+                "peak": hbm_gbs, "unit": "GB/s", "frac": round(ach / hbm_gbs, 4) if ach else None,
+                "traffic": traffic_for(dom), "peak_kind": peak_kind,
+                "algorithmic_bytes_per_launch": int(b) if b else None,
+                "avg_launch_ms": round(avg_ms, 5)}
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        v, cores, kind, sample = cpu_oracle_time(1, 8, 1)
+        cpu = {"value": round(v, 3), "unit": "tokens/s", "cores": cores, "kind": kind,
+               "sample": sample}
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": K, "warmup": W, "ms_per_step": round(ms / K, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": config_dict(args, world),
+        "hbm": {"achieved_gbs": round(achieved_layer, 1),
+                "frac_of_8tbps": round(achieved_layer / NOMINAL_HBM_GBS, 4),
+                "frac_of_measured": round(achieved_layer / hbm_gbs, 4),
+                "bytes_per_step": int(total_bytes / K), "distinct_experts_mean": round(U_mean, 1)},
+        "roofline": roof,
+        "stages_ms": {k: round(v[1], 5) for k, v in stages.items()},
+        "e2e": {"value": round(K * T * world / (e2e_ms / 1000.0), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": T * HIDDEN * 2, "d2h_bytes_per_step": T * HIDDEN * 2},
+        "cpu_baseline": cpu,
+        "clocks": clocks,
+        "gpu_launches": 7 * K,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def traffic_for(kernel):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    try:
+        with open(path) as fh:
+            d = json.load(fh)
+        return d.get(kernel, {}).get("dram_bytes_per_launch")
+    except Exception:
+        return None
+
+
+if __name__ == "__main__":
+    main()

@@ -153,6 +153,19 @@ int vx_moe_block(const uint16_t* x, int32_t T, const vx_moe_weights* W,
 int vx_rmsnorm(const uint16_t* x, const uint16_t* gain, int32_t T, int32_t d,
                float eps, uint16_t* y, void* stream);
 
+/* ---- Stage timing ----------------------------------------------------- */
+
+/* Per-kernel boundary timing, the role of the reference's BoundaryProfiler
+ * (boundary_profiler.py:1-25; used at metal_runtime.py:618-637).  While
+ * enabled, vx_moe_block / vx_moe_experts / vx_router record a CUDA event on
+ * the caller's stream after each kernel.  Enabling resets the records.
+ * vx_profile_read waits for the last event and returns, per stage label,
+ * the number of launches and their average duration in milliseconds;
+ * labels are written newline-separated into `labels`. */
+int vx_profile_enable(int enabled);
+int vx_profile_read(int max_stages, char* labels, int labels_cap, double* avg_ms,
+                    int32_t* counts, int32_t* n_stages);
+
 #ifdef __cplusplus
 }
 #endif

@@ -8,6 +8,7 @@
 
 #include "vx_common.cuh"
 #include "vx_launch.h"
+#include "vx_profile.h"
 
 #define VX_VERSION_STRING "vxmoe 0.1.0 (sm_100a)"
 
@@ -123,6 +124,7 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
   e = launch_permute(routes, P, dm.E, Ts, dm.k, nullptr, s.order, s.inverse, s.offsets, s.active,
                      s.n_active, s.src_rows, s.err, st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
+  profile_mark(st, "permute");
   const int max_active = int(std::min<int64_t>(dm.E, P)) + (dm.shared ? 1 : 0);
 
   GroupedArgs a{};
@@ -144,6 +146,7 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
   a.ldo = s.ldh;
   e = launch_grouped(kGateUpSwiGLU, a, max_active, int(s.ldh), dm.d, st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
+  profile_mark(st, "gate_up_swiglu");
 
   GroupedArgs b{};
   b.b0 = W->down;
@@ -160,6 +163,7 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
   b.ldo = dm.d;
   e = launch_grouped(kProj, b, max_active, dm.d, int(s.ldh), st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
+  profile_mark(st, "down");
   return VX_OK;
 }
 
@@ -289,10 +293,19 @@ size_t vx_router_workspace(int32_t T, const vx_moe_weights* W) {
 static int router_impl(const uint16_t* x, int T, const vx_moe_weights* W, const BlockDims& dm,
                        uint16_t* logits, int32_t* inds, uint16_t* weights, uint16_t* sg,
                        cudaStream_t st) {
+  profile_mark(st, "");
   cudaError_t e = launch_router_logits(x, T, W->router_w, dm.E, dm.d, logits, st);
-  if (e == cudaSuccess) e = launch_softmax_topk(logits, T, dm.E, dm.k, inds, nullptr, weights, nullptr, st);
-  if (e == cudaSuccess && sg && W->shared_expert_gate.w) e = launch_shared_gate(x, T, W->shared_expert_gate, sg, st);
-  return e == cudaSuccess ? VX_OK : vx_cuda_fail(e);
+  if (e != cudaSuccess) return vx_cuda_fail(e);
+  profile_mark(st, "router_logits");
+  e = launch_softmax_topk(logits, T, dm.E, dm.k, inds, nullptr, weights, nullptr, st);
+  if (e != cudaSuccess) return vx_cuda_fail(e);
+  profile_mark(st, "softmax_topk");
+  if (sg && W->shared_expert_gate.w) {
+    e = launch_shared_gate(x, T, W->shared_expert_gate, sg, st);
+    if (e != cudaSuccess) return vx_cuda_fail(e);
+    profile_mark(st, "shared_gate");
+  }
+  return VX_OK;
 }
 
 int vx_router(const uint16_t* x, int32_t T, const vx_moe_weights* W, uint16_t* logits,
@@ -361,6 +374,7 @@ int vx_moe_experts(const uint16_t* x, int32_t T, const int32_t* routes, const ui
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   Carver c(workspace);
   ExpertScratch es = carve_experts(c, T, dm);
+  profile_mark(st, "");
   s = run_experts(x, T, routes, W, dm, es, st);
   if (s) return s;
   cudaError_t e;
@@ -371,7 +385,9 @@ int vx_moe_experts(const uint16_t* x, int32_t T, const int32_t* routes, const ui
   } else {
     e = launch_unpermute(es.yd, dm.d, es.inverse, T, dm.k, dm.d, out, st);
   }
-  return e == cudaSuccess ? VX_OK : vx_cuda_fail(e);
+  if (e != cudaSuccess) return vx_cuda_fail(e);
+  profile_mark(st, scores ? "combine" : "unpermute");
+  return VX_OK;
 }
 
 size_t vx_moe_block_workspace(int32_t T, const vx_moe_weights* W) {
@@ -413,7 +429,9 @@ int vx_moe_block(const uint16_t* x, int32_t T, const vx_moe_weights* W, uint16_t
   cudaError_t e = launch_combine(es.yd, dm.d, es.inverse, weights, T, dm.k, dm.d,
                                  dm.shared ? kSharedInternal : kSharedNone, es.offsets, dm.E, sg,
                                  nullptr, nullptr, nullptr, y, st);
-  return e == cudaSuccess ? VX_OK : vx_cuda_fail(e);
+  if (e != cudaSuccess) return vx_cuda_fail(e);
+  profile_mark(st, "combine");
+  return VX_OK;
 }
 
 int vx_rmsnorm(const uint16_t* x, const uint16_t* gain, int32_t T, int32_t d, float eps, uint16_t* y,

@@ -69,6 +69,10 @@ SIGNATURES = {
     "vx_moe_block": (ctypes.c_int, [P, c_int32, ctypes.POINTER(VxMoEWeights), P, P, P, P,
                                     c_size_t, P]),
     "vx_rmsnorm": (ctypes.c_int, [P, P, c_int32, c_int32, c_float, P, P]),
+    "vx_profile_enable": (ctypes.c_int, [ctypes.c_int]),
+    "vx_profile_read": (ctypes.c_int, [ctypes.c_int, ctypes.c_char_p, ctypes.c_int,
+                                       ctypes.POINTER(ctypes.c_double),
+                                       ctypes.POINTER(c_int32), ctypes.POINTER(c_int32)]),
 }
 
 _lock = threading.Lock()
@@ -112,3 +116,20 @@ def check(status: int, what: str = "") -> None:
     if status == VX_ECUDA:
         msg += f" ({lib.vx_last_cuda_error().decode()})"
     raise RuntimeError(msg)
+
+
+def profile_enable(enabled: bool = True) -> None:
+    """Start (and reset) or stop per-stage CUDA-event timing."""
+    check(load().vx_profile_enable(int(bool(enabled))), "profile_enable")
+
+
+def profile_read(max_stages: int = 32) -> dict:
+    """{stage label: (launches, average ms)} since the last enable."""
+    lib = load()
+    labels = ctypes.create_string_buffer(4096)
+    avg = (ctypes.c_double * max_stages)()
+    cnt = (c_int32 * max_stages)()
+    n = c_int32(0)
+    check(lib.vx_profile_read(max_stages, labels, 4096, avg, cnt, ctypes.byref(n)), "profile_read")
+    names = labels.value.decode().split("\n")[: n.value]
+    return {name: (int(cnt[i]), float(avg[i])) for i, name in enumerate(names)}
