@@ -118,6 +118,38 @@ def test_gather_qmm_lhs_indices_and_slot_inputs(small_params):
                                   O.bf16_bits(np32(out[:, :, 0]).reshape(T * k, -1)[order]))
 
 
+@pytest.mark.parametrize("K,N", [(32, 8), (96, 24), (160, 40), (2560, 640), (640, 2560)])
+def test_gather_qmm_ragged_widths(K, N):
+    """Odd group counts, widths that are not a multiple of 128 and row counts
+    that are not a multiple of 16 (the Qwen production shape 2560/640 too)."""
+    import vxmoe
+    rng = np.random.default_rng(K + N)
+    bank = O.make_q4_bank(rng, 3, N, K)
+    T = 7
+    x = O.make_x(K, T, K)
+    inds = rng.integers(0, 3, size=(T, 2)).astype(np.int32)
+    out = vxmoe.gather_qmm(bf16_t(x)[:, None, None, :], *bank_t(bank),
+                           rhs_indices=torch.from_numpy(inds).to(DEV))
+    ref = np.stack([np.stack([O.bf16_round(O.qmv(x[t], bank.w[e], bank.scales[e], bank.biases[e])
+                                            .astype(np.float32)) for e in inds[t]]) for t in range(T)])
+    assert_bf16_close(np32(out[:, :, 0]), ref, what=f"gather_qmm K={K} N={N}")
+
+
+def test_gather_qmm_many_tokens_per_expert(small_params):
+    """An expert with more tokens than one work item holds (items chunked)."""
+    import vxmoe
+    p = small_params
+    T = 50
+    x = O.make_x(77, T, p.hidden)
+    inds = np.zeros((T, 1), np.int32)
+    inds[::3] = 5
+    out = vxmoe.gather_qmm(bf16_t(x)[:, None, None, :], *bank_t(p.up),
+                           rhs_indices=torch.from_numpy(inds).to(DEV))
+    ref = np.stack([O.bf16_round(O.qmv(x[t], p.up.w[inds[t, 0]], p.up.scales[inds[t, 0]],
+                                       p.up.biases[inds[t, 0]]).astype(np.float32)) for t in range(T)])
+    assert_bf16_close(np32(out[:, 0, 0]), ref, what="many tokens per expert")
+
+
 def test_gather_qmm_production_width(prod_params):
     import vxmoe
     p = prod_params

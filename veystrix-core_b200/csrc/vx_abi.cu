@@ -93,9 +93,10 @@ static int check_weights(const vx_moe_weights* W, bool need_router, BlockDims* d
 // Scratch of the routed-expert pipeline for T tokens (P = T*k items plus
 // the shared expert's T items).
 struct ExpertScratch {
-  int32_t *order, *inverse, *offsets, *active, *n_active, *src_rows, *err;
+  int32_t *order, *inverse, *offsets, *active, *n_active, *src_rows, *err, *items, *n_items;
   uint16_t *h, *yd;
   int64_t ldh;
+  int max_items;
 };
 
 static ExpertScratch carve_experts(Carver& c, int T, const BlockDims& dm) {
@@ -108,6 +109,9 @@ static ExpertScratch carve_experts(Carver& c, int T, const BlockDims& dm) {
   s.n_active = c.take<int32_t>(1);
   s.src_rows = c.take<int32_t>(P + Ts);
   s.err = c.take<int32_t>(1);
+  s.max_items = max_items_bound(P, dm.E, int(Ts));
+  s.items = c.take<int32_t>(3 * int64_t(s.max_items));
+  s.n_items = c.take<int32_t>(1);
   s.ldh = std::max(dm.I, dm.Is);
   s.h = c.take<uint16_t>((P + Ts) * s.ldh);
   s.yd = c.take<uint16_t>((P + Ts) * dm.d);
@@ -122,12 +126,11 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
   cudaError_t e = cudaMemsetAsync(s.err, 0, sizeof(int32_t), st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
   e = launch_permute(routes, P, dm.E, Ts, dm.k, nullptr, s.order, s.inverse, s.offsets, s.active,
-                     s.n_active, s.src_rows, s.err, st);
+                     s.n_active, s.src_rows, s.err, kItemChunk, s.items, s.n_items, st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
   profile_mark(st, "permute");
-  const int max_active = int(std::min<int64_t>(dm.E, P)) + (dm.shared ? 1 : 0);
 
-  GroupedArgs a{};
+  MmaArgs a{};
   a.b0 = W->gate;
   a.b1 = W->up;
   if (dm.shared) {
@@ -135,33 +138,31 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
     a.s1 = W->shared_up;
   }
   a.E = dm.E;
-  a.offsets = s.offsets;
-  a.active = s.active;
-  a.n_active = s.n_active;
+  a.items = s.items;
+  a.n_items = s.n_items;
   a.src_rows = s.src_rows;
   a.dst_rows = nullptr;
   a.x = x;
   a.ldx = dm.d;
   a.out = s.h;
   a.ldo = s.ldh;
-  e = launch_grouped(kGateUpSwiGLU, a, max_active, int(s.ldh), dm.d, st);
+  e = launch_gemv_mma(true, a, s.max_items, int(s.ldh), st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
   profile_mark(st, "gate_up_swiglu");
 
-  GroupedArgs b{};
+  MmaArgs b{};
   b.b0 = W->down;
   if (dm.shared) b.s0 = W->shared_down;
   b.E = dm.E;
-  b.offsets = s.offsets;
-  b.active = s.active;
-  b.n_active = s.n_active;
+  b.items = s.items;
+  b.n_items = s.n_items;
   b.src_rows = nullptr;
   b.dst_rows = nullptr;
   b.x = s.h;
   b.ldx = s.ldh;
   b.out = s.yd;
   b.ldo = dm.d;
-  e = launch_grouped(kProj, b, max_active, dm.d, int(s.ldh), st);
+  e = launch_gemv_mma(false, b, s.max_items, dm.d, st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
   profile_mark(st, "down");
   return VX_OK;
@@ -222,6 +223,8 @@ size_t vx_gather_qmm_workspace(int64_t B, int32_t M, int32_t experts) {
   c.take<int32_t>(1);            // n_active
   c.take<int32_t>(n);            // src_rows
   c.take<int32_t>(1);            // err
+  c.take<int32_t>(3 * int64_t(max_items_bound(n, experts, 0)));  // items
+  c.take<int32_t>(1);            // n_items
   return c.size();
 }
 
@@ -229,7 +232,6 @@ int vx_gather_qmm(const uint16_t* x, int64_t x_rows, const vx_q4* w, const int32
                   const int32_t* rhs, int64_t B, int32_t M, int32_t sorted_indices, uint16_t* out,
                   void* workspace, size_t workspace_bytes, void* stream) {
   (void)sorted_indices;
-  (void)x_rows;
   if (!w || B < 0 || M < 1) return VX_EINVAL_SHAPE;
   int s = check_q4(w, w->experts, w->out, w->in);
   if (s) return s;
@@ -251,25 +253,27 @@ int vx_gather_qmm(const uint16_t* x, int64_t x_rows, const vx_q4* w, const int32
   int32_t* n_active = c.take<int32_t>(1);
   int32_t* src_rows = c.take<int32_t>(n);
   int32_t* err = c.take<int32_t>(1);
+  const int max_items = max_items_bound(n, E, 0);
+  int32_t* items = c.take<int32_t>(3 * int64_t(max_items));
+  int32_t* n_items = c.take<int32_t>(1);
   cudaError_t e = cudaMemsetAsync(err, 0, sizeof(int32_t), st);
-  if (e == cudaSuccess) e = launch_gather_items(lhs, rhs, B, M, keys, src_map, st);
+  if (e == cudaSuccess) e = launch_gather_items(lhs, rhs, B, M, x_rows, keys, src_map, st);
   if (e == cudaSuccess)
     e = launch_permute(keys, n, E, 0, 1, src_map, order, inverse, offsets, active, n_active, src_rows,
-                       err, st);
+                       err, kItemChunk, items, n_items, st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
-  GroupedArgs a{};
+  MmaArgs a{};
   a.b0 = *w;
   a.E = E;
-  a.offsets = offsets;
-  a.active = active;
-  a.n_active = n_active;
+  a.items = items;
+  a.n_items = n_items;
   a.src_rows = src_rows;
   a.dst_rows = order;
   a.x = x;
   a.ldx = w->in;
   a.out = out;
   a.ldo = w->out;
-  e = launch_grouped(kProj, a, int(std::min<int64_t>(E, n)), w->out, w->in, st);
+  e = launch_gemv_mma(false, a, max_items, w->out, st);
   return e == cudaSuccess ? VX_OK : vx_cuda_fail(e);
 }
 
@@ -344,7 +348,7 @@ int vx_permute(const int32_t* ids, int64_t P, int32_t E, int32_t* order, int32_t
   int32_t* n_active = c.take<int32_t>(1);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = launch_permute(ids, P, E, -1, 1, nullptr, order, inverse, offsets, active, n_active,
-                                 nullptr, error_count, st);
+                                 nullptr, error_count, kItemChunk, nullptr, nullptr, st);
   return e == cudaSuccess ? VX_OK : vx_cuda_fail(e);
 }
 

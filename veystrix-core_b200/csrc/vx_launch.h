@@ -8,36 +8,43 @@
 
 namespace vx {
 
-// Items of a grouped projection, sorted by expert.  Expert id E is the
-// shared expert; its items sit at [offsets[E], offsets[E+1]).
-struct GroupedArgs {
-  vx_q4 b0, b1;          // routed banks (b1: up bank in gate/up mode)
-  vx_q4 s0, s1;          // shared-expert banks (expert id E); w may be null
+// Tokens per work item of the tensor-pipe GEMV (an expert's run is cut into
+// items of at most this many positions).
+constexpr int kItemChunk = 16;
+
+struct MmaArgs {
+  vx_q4 b0, b1;              // routed banks (b1: up in gate/up mode)
+  vx_q4 s0, s1;              // shared expert banks (expert id E)
   int E;
-  const int32_t* offsets;   // [E+2]
-  const int32_t* active;    // experts that own items
-  const int32_t* n_active;  // device count of `active`
-  const int32_t* src_rows;  // x row of each sorted position (null: identity)
-  const int32_t* dst_rows;  // out row of each sorted position (null: identity)
-  const uint16_t* x;        // bf16 [*, ldx]
+  const int32_t* items;      // [n][3] expert, first position, count
+  const int32_t* n_items;
+  const int32_t* src_rows;   // x row of each position (null: identity)
+  const int32_t* dst_rows;   // out row of each position (null: identity)
+  const uint16_t* x;
   int64_t ldx;
-  uint16_t* out;            // bf16 [*, ldo]
+  uint16_t* out;
   int64_t ldo;
-  int tiles_per_expert;
+  int tiles_per_item;        // set by the launcher
 };
 
-enum GroupedMode { kProj = 0, kGateUpSwiGLU = 1 };
+cudaError_t launch_gemv_mma(bool gateup, const MmaArgs& a, int max_items, int max_out,
+                            cudaStream_t st);
+
+// Upper bound of the number of work items for P routed positions over E
+// experts plus Ts shared-expert positions.
+inline int max_items_bound(int64_t P, int E, int Ts) {
+  int64_t routed = (P + kItemChunk - 1) / kItemChunk + (P < E ? P : E);
+  if (routed > P) routed = P;
+  return int(routed + (Ts + kItemChunk - 1) / kItemChunk);
+}
 
 int sm_count();
-
-// Upper bound of experts with items: min(E, items) + shared.
-cudaError_t launch_grouped(GroupedMode mode, const GroupedArgs& a, int max_active, int max_out,
-                           int max_in, cudaStream_t st);
 
 cudaError_t launch_permute(const int32_t* ids, int64_t P, int E, int shared_items, int k_div,
                            const int32_t* src_map, int32_t* order, int32_t* inverse,
                            int32_t* offsets, int32_t* active, int32_t* n_active,
-                           int32_t* src_rows, int32_t* err, cudaStream_t st);
+                           int32_t* src_rows, int32_t* err, int item_chunk, int32_t* items,
+                           int32_t* n_items, cudaStream_t st);
 
 cudaError_t launch_router_logits(const uint16_t* x, int T, const uint16_t* wg, int E, int K,
                                  uint16_t* logits, cudaStream_t st);
@@ -63,6 +70,6 @@ cudaError_t launch_swiglu(const uint16_t* g, const uint16_t* u, uint16_t* out, i
                           cudaStream_t st);
 cudaError_t launch_dequant(const vx_q4& bank, int expert, float* out, cudaStream_t st);
 cudaError_t launch_gather_items(const int32_t* lhs, const int32_t* rhs, int64_t B, int M,
-                                int32_t* keys, int32_t* src_map, cudaStream_t st);
+                                int64_t x_rows, int32_t* keys, int32_t* src_map, cudaStream_t st);
 
 }  // namespace vx

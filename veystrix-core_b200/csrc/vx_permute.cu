@@ -49,7 +49,8 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(
     const int32_t* __restrict__ ids, int P, int E, int shared_items, int k_div,
     const int32_t* __restrict__ src_map, int32_t* __restrict__ order,
     int32_t* __restrict__ inverse, int32_t* __restrict__ offsets, int32_t* __restrict__ active,
-    int32_t* __restrict__ n_active, int32_t* __restrict__ src_rows, int32_t* __restrict__ err) {
+    int32_t* __restrict__ n_active, int32_t* __restrict__ src_rows, int32_t* __restrict__ err,
+    int item_chunk, int32_t* __restrict__ items, int32_t* __restrict__ n_items) {
   extern __shared__ int smem[];
   int* counts = smem;                         // [E]
   int* base = counts + E;                     // [E]  run start
@@ -104,6 +105,36 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(
     if (src_rows) src_rows[carry + t] = t;
   }
 
+  // Work items for the grouped kernels: each expert's run cut into chunks of
+  // at most item_chunk positions, in expert order: {expert, first, count}.
+  if (items) {
+    const int na = acarry + (shared_items > 0 ? 1 : 0);
+    int icarry = 0;
+    for (int a0 = 0; a0 < na; a0 += kPermThreads) {
+      const int ai = a0 + tid;
+      int e = -1, n = 0, first = 0;
+      if (ai < na) {
+        e = ai < acarry ? active[ai] : E;
+        n = e < E ? counts[e] : shared_items;
+        first = e < E ? base[e] : carry;
+      }
+      const int nch = (n + item_chunk - 1) / item_chunk;
+      const int ex = block_exclusive_scan(nch, warp_tot);
+      for (int j = 0; j < nch; ++j) {
+        int32_t* it = items + 3 * (icarry + ex + j);
+        it[0] = e;
+        it[1] = first + j * item_chunk;
+        it[2] = min(item_chunk, n - j * item_chunk);
+      }
+      __shared__ int tot_i;
+      if (tid == kPermThreads - 1) tot_i = ex + nch;
+      __syncthreads();
+      icarry += tot_i;
+      __syncthreads();
+    }
+    if (tid == 0) *n_items = icarry;
+  }
+
   // Stable scatter.
   for (int c0 = 0; c0 < P; c0 += kPermThreads) {
     const int i = c0 + tid;
@@ -140,7 +171,8 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(
 cudaError_t launch_permute(const int32_t* ids, int64_t P, int E, int shared_items, int k_div,
                            const int32_t* src_map, int32_t* order, int32_t* inverse,
                            int32_t* offsets, int32_t* active, int32_t* n_active,
-                           int32_t* src_rows, int32_t* err, cudaStream_t st) {
+                           int32_t* src_rows, int32_t* err, int item_chunk, int32_t* items,
+                           int32_t* n_items, cudaStream_t st) {
   const size_t smem = size_t(E) * (3 + kPermWarps) * sizeof(int);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -148,26 +180,30 @@ cudaError_t launch_permute(const int32_t* ids, int64_t P, int E, int shared_item
     if (e != cudaSuccess) return e;
   }
   permute_kernel<<<1, kPermThreads, smem, st>>>(ids, int(P), E, shared_items, k_div, src_map, order,
-                                                inverse, offsets, active, n_active, src_rows, err);
+                                                inverse, offsets, active, n_active, src_rows, err,
+                                                item_chunk, items, n_items);
   return cudaGetLastError();
 }
 
 // Items of a gather_qmm call: item i = b*M + m has key rhs[b] and x row
-// (lhs ? lhs[b] : b)*M + m.
+// (lhs ? lhs[b] : b)*M + m.  An lhs entry outside the x batch gets key -1,
+// so the permutation drops (and counts) the item instead of reading past x.
 __global__ void gather_items_kernel(const int32_t* lhs, const int32_t* rhs, int64_t B, int M,
-                                    int32_t* keys, int32_t* src_map) {
+                                    int64_t x_rows, int32_t* keys, int32_t* src_map) {
   const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= B * M) return;
   const int64_t b = i / M, m = i - b * M;
-  keys[i] = rhs[b];
-  src_map[i] = int32_t((lhs ? int64_t(lhs[b]) : b) * M + m);
+  const int64_t l = lhs ? int64_t(lhs[b]) : b;
+  const bool ok = l >= 0 && (l + 1) * M <= x_rows;
+  keys[i] = ok ? rhs[b] : -1;
+  src_map[i] = ok ? int32_t(l * M + m) : 0;
 }
 
 cudaError_t launch_gather_items(const int32_t* lhs, const int32_t* rhs, int64_t B, int M,
-                                int32_t* keys, int32_t* src_map, cudaStream_t st) {
+                                int64_t x_rows, int32_t* keys, int32_t* src_map, cudaStream_t st) {
   const int64_t n = B * M;
   if (n == 0) return cudaSuccess;
-  gather_items_kernel<<<int((n + 255) / 256), 256, 0, st>>>(lhs, rhs, B, M, keys, src_map);
+  gather_items_kernel<<<int((n + 255) / 256), 256, 0, st>>>(lhs, rhs, B, M, x_rows, keys, src_map);
   return cudaGetLastError();
 }
 
