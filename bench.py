@@ -42,7 +42,7 @@ NOMINAL_HBM_GBS = 8000.0
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="vxmoe", choices=("vxmoe", "reference"))
     ap.add_argument("--tokens", type=int, default=64)
@@ -89,7 +89,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(index)], stdout=self.fh, stderr=subprocess.DEVNULL)
+                 "-lms", "100", "-i", str(index)], stdout=self.fh, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
 

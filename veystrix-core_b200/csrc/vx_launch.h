@@ -9,8 +9,9 @@
 namespace vx {
 
 // Tokens per work item of the tensor-pipe GEMV (an expert's run is cut into
-// items of at most this many positions).
-constexpr int kItemChunk = 16;
+// items of at most this many positions).  The GEMV handles an item's tokens
+// two per MMA, all in one sweep over the expert's weights.
+constexpr int kItemChunk = 4;
 
 struct MmaArgs {
   vx_q4 b0, b1;              // routed banks (b1: up in gate/up mode)

@@ -16,48 +16,51 @@
 
 namespace vx {
 
-// ---- logits: one warp per expert row, 8 tokens per pass ------------------
-constexpr int kRouterTok = 8;
+// ---- logits on the tensor pipe ---------------------------------------------
+// A CTA owns 16 experts x 8 tokens; its kRouterSlices warps split K and meet
+// in shared memory.  Lane (g, c) loads 16 bytes (8 bf16) of expert rows g and
+// g+8 and of token g's x at the same k offset 8c: the same k permutation on
+// both operands, so two m16n8k16 MMAs consume one 16-byte load per operand
+// with no shuffling.  float32 accumulation, bf16 logits.
+constexpr int kRouterSlices = 8;
 
-__global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __restrict__ x, int T,
-                                                            const uint16_t* __restrict__ wg, int E,
-                                                            int K, uint16_t* __restrict__ logits) {
+__global__ void __launch_bounds__(32 * kRouterSlices) router_logits_kernel(
+    const uint16_t* __restrict__ x, int T, const uint16_t* __restrict__ wg, int E, int K,
+    uint16_t* __restrict__ logits) {
+  __shared__ float red[kRouterSlices][32][4];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e = blockIdx.x * 8 + warp;
-  if (e >= E) return;
-  const uint16_t* wr = wg + int64_t(e) * K;
-  for (int t0 = 0; t0 < T; t0 += kRouterTok) {
-    const int nt = min(kRouterTok, T - t0);
-    float acc[kRouterTok];
+  const int g = lane >> 2, c = lane & 3;
+  const int e0 = blockIdx.x * 16, t0 = blockIdx.y * 8;
+  const int ea = e0 + g, eb = e0 + g + 8, tx = t0 + g;
+  const uint16_t* ra = wg + int64_t(ea < E ? ea : 0) * K;
+  const uint16_t* rb = wg + int64_t(eb < E ? eb : 0) * K;
+  const uint16_t* rx = x + int64_t(tx < T ? tx : 0) * K;
+  const int steps = K / 32;
+  const int per = (steps + kRouterSlices - 1) / kRouterSlices;
+  const int s0 = warp * per, s1 = min(steps, s0 + per);
+  float d[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int s = s0; s < s1; ++s) {
+    const int k = s * 32 + c * 8;
+    const uint4 wa = ea < E ? ldg_nc(ra + k) : make_uint4(0, 0, 0, 0);
+    const uint4 wb = eb < E ? ldg_nc(rb + k) : make_uint4(0, 0, 0, 0);
+    const uint4 xb = tx < T ? __ldg(reinterpret_cast<const uint4*>(rx + k)) : make_uint4(0, 0, 0, 0);
+    mma16816(d, wa.x, wb.x, wa.y, wb.y, xb.x, xb.y);
+    mma16816(d, wa.z, wb.z, wa.w, wb.w, xb.z, xb.w);
+  }
 #pragma unroll
-    for (int t = 0; t < kRouterTok; ++t) acc[t] = 0.f;
-    for (int k0 = lane * 8; k0 < K; k0 += 256) {
-      const uint4 wv = __ldg(reinterpret_cast<const uint4*>(wr + k0));
-      float w[8] = {__uint_as_float(wv.x << 16), __uint_as_float(wv.x & 0xFFFF0000u),
-                    __uint_as_float(wv.y << 16), __uint_as_float(wv.y & 0xFFFF0000u),
-                    __uint_as_float(wv.z << 16), __uint_as_float(wv.z & 0xFFFF0000u),
-                    __uint_as_float(wv.w << 16), __uint_as_float(wv.w & 0xFFFF0000u)};
+  for (int i = 0; i < 4; ++i) red[warp][lane][i] = d[i];
+  __syncthreads();
+  if (warp == 0) {
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int w = 0; w < kRouterSlices; ++w)
 #pragma unroll
-      for (int t = 0; t < kRouterTok; ++t) {
-        if (t < nt) {
-          const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x + int64_t(t0 + t) * K + k0));
-          float a = acc[t];
-          a = fmaf(__uint_as_float(xv.x << 16), w[0], a);
-          a = fmaf(__uint_as_float(xv.x & 0xFFFF0000u), w[1], a);
-          a = fmaf(__uint_as_float(xv.y << 16), w[2], a);
-          a = fmaf(__uint_as_float(xv.y & 0xFFFF0000u), w[3], a);
-          a = fmaf(__uint_as_float(xv.z << 16), w[4], a);
-          a = fmaf(__uint_as_float(xv.z & 0xFFFF0000u), w[5], a);
-          a = fmaf(__uint_as_float(xv.w << 16), w[6], a);
-          a = fmaf(__uint_as_float(xv.w & 0xFFFF0000u), w[7], a);
-          acc[t] = a;
-        }
-      }
-    }
+      for (int i = 0; i < 4; ++i) v[i] += red[w][lane][i];
+    // D[g][2c], D[g][2c+1], D[g+8][2c], D[g+8][2c+1]: (expert, token)
 #pragma unroll
-    for (int t = 0; t < kRouterTok; ++t) {
-      const float v = warp_sum<32>(acc[t]);
-      if (lane == 0 && t < nt) logits[int64_t(t0 + t) * E + e] = f32_to_bf16(v);
+    for (int i = 0; i < 4; ++i) {
+      const int e = (i < 2) ? ea : eb;
+      const int t = t0 + 2 * c + (i & 1);
+      if (e < E && t < T) logits[int64_t(t) * E + e] = f32_to_bf16(v[i]);
     }
   }
 }
@@ -65,7 +68,8 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __re
 cudaError_t launch_router_logits(const uint16_t* x, int T, const uint16_t* wg, int E, int K,
                                  uint16_t* logits, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  router_logits_kernel<<<(E + 7) / 8, 256, 0, st>>>(x, T, wg, E, K, logits);
+  dim3 grid((E + 15) / 16, (T + 7) / 8);
+  router_logits_kernel<<<grid, 32 * kRouterSlices, 0, st>>>(x, T, wg, E, K, logits);
   return cudaGetLastError();
 }
 
@@ -84,11 +88,13 @@ __global__ void __launch_bounds__(256) shared_gate_kernel(const uint16_t* __rest
     float q = 0.f, xs = 0.f;
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
+      const uint4 xv = __ldg(reinterpret_cast<const uint4*>(xr + g * 32 + c * 8));
+      const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
       for (int n = 0; n < 8; ++n) {
-        const float xv = bf16_to_f32(xr[g * 32 + c * 8 + n]);
-        q = fmaf(float(nibble(ws[c], n)), xv, q);
-        xs += xv;
+        const float v = __uint_as_float((n & 1) ? (xw[n >> 1] & 0xFFFF0000u) : (xw[n >> 1] << 16));
+        q = fmaf(float(nibble(ws[c], n)), v, q);
+        xs += v;
       }
     }
     acc += fmaf(bf16_to_f32(seg.scales[g]), q, bf16_to_f32(seg.biases[g]) * xs);
@@ -105,7 +111,6 @@ cudaError_t launch_shared_gate(const uint16_t* x, int T, const vx_q4& seg, uint1
 }
 
 // ---- softmax + top-k + renorm: one warp per token --------------------------
-constexpr int kMaxPer = 32;   // E <= 1024
 constexpr int kMaxK = 16;
 
 template <int PER>
@@ -182,11 +187,13 @@ __global__ void __launch_bounds__(256) softmax_topk_kernel(const uint16_t* __res
   const float diff = bf16r(__fsub_rn(sel_sum, msum));
   const float norm = bf16r(__fadd_rn(msum, bf16r(diff)));
   for (int r = lane; r < k; r += 32) {
-    // r is warp-uniform per lane: pick the lane's slot from the arrays
     float p = 0.f;
     int id = 0;
     for (int q = 0; q < k; ++q)
-      if (q == r) { p = sel_p[q]; id = sel_i[q]; }
+      if (q == r) {
+        p = sel_p[q];
+        id = sel_i[q];
+      }
     inds[int64_t(t) * k + r] = id;
     if (scores) scores[int64_t(t) * k + r] = f32_to_bf16(p);
     weights[int64_t(t) * k + r] = f32_to_bf16(bf16r(__fdiv_rn(p, norm)));
