@@ -149,6 +149,21 @@ int vx_moe_block(const uint16_t* x, int32_t T, const vx_moe_weights* W,
                  uint16_t* y, int32_t* inds, uint16_t* weights, void* workspace,
                  size_t workspace_bytes, void* stream);
 
+/* The whole block without a workspace, for callers that cannot allocate
+ * device memory (a plugin living inside another runtime's memory pool, or
+ * code that must not call cudaMalloc once it is running).  No counterpart in
+ * the reference.  Scratch comes from a static device array of
+ * VX_NOALLOC_SCRATCH_BYTES inside the library, which every GPU that loads the
+ * library keeps until the process exits.  A batch whose scratch
+ * (vx_moe_block_workspace) exceeds the array returns VX_EWORKSPACE.  The
+ * first call on a device looks up the array's device address (set-up, once
+ * per device); make that first call before any stream capture.  All calls
+ * share one array: calls that overlap on the GPU (other streams, other host
+ * threads) race and must be serialised by the caller.  Allocates nothing. */
+#define VX_NOALLOC_SCRATCH_BYTES (2u << 20)
+int vx_moe_block_noalloc(const uint16_t* x, int32_t T, const vx_moe_weights* W,
+                         uint16_t* y, int32_t* inds, uint16_t* weights, void* stream);
+
 /* RMSNorm in float32 with a bf16 gain, bf16 out (patch_rmsnorm.py:96-120). */
 int vx_rmsnorm(const uint16_t* x, const uint16_t* gain, int32_t T, int32_t d,
                float eps, uint16_t* y, void* stream);

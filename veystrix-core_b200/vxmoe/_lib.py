@@ -68,6 +68,8 @@ SIGNATURES = {
     "vx_moe_block_workspace": (c_size_t, [c_int32, ctypes.POINTER(VxMoEWeights)]),
     "vx_moe_block": (ctypes.c_int, [P, c_int32, ctypes.POINTER(VxMoEWeights), P, P, P, P,
                                     c_size_t, P]),
+    "vx_moe_block_noalloc": (ctypes.c_int, [P, c_int32, ctypes.POINTER(VxMoEWeights), P, P, P,
+                                            P]),
     "vx_rmsnorm": (ctypes.c_int, [P, P, c_int32, c_int32, c_float, P, P]),
     "vx_profile_enable": (ctypes.c_int, [ctypes.c_int]),
     "vx_profile_read": (ctypes.c_int, [ctypes.c_int, ctypes.c_char_p, ctypes.c_int,
