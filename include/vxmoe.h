@@ -90,7 +90,8 @@ int vx_swiglu_bf16(const uint16_t* gate, const uint16_t* up, uint16_t* out,
  * out[b, m, :] = x[lhs[b]*M + m, :] . dequant(w[rhs[b]])^T, bf16 out
  * [B, M, N].  lhs may be NULL (identity).  sorted_indices is a hint only.
  * Replaces mx.gather_qmm (expert_cache.py:818-829). */
-size_t vx_gather_qmm_workspace(int64_t B, int32_t M, int32_t experts);
+size_t vx_gather_qmm_workspace(int64_t B, int32_t M, int32_t experts, int64_t x_rows,
+                               int32_t K);
 int vx_gather_qmm(const uint16_t* x, int64_t x_rows, const vx_q4* w,
                   const int32_t* lhs, const int32_t* rhs, int64_t B, int32_t M,
                   int32_t sorted_indices, uint16_t* out, void* workspace,

@@ -59,7 +59,7 @@ def test_workspace_sizes_are_consistent(lib):
     assert 0 < small < big
     # h and yd dominate: (T*k) * (I + d) * 2 bytes
     assert big >= 64 * 10 * (512 + 2048) * 2
-    assert lib.vx_gather_qmm_workspace(10, 1, 512) > 0
+    assert lib.vx_gather_qmm_workspace(10, 1, 512, 10, 2048) > 10 * 2048 * 2
     assert lib.vx_permute_workspace(100, 512) > 0
 
 

@@ -94,8 +94,9 @@ static int check_weights(const vx_moe_weights* W, bool need_router, BlockDims* d
 // the shared expert's T items).
 struct ExpertScratch {
   int32_t *order, *inverse, *offsets, *active, *n_active, *src_rows, *err, *items, *n_items;
-  uint16_t *h, *yd;
-  int64_t ldh;
+  uint16_t *h, *yd, *xb;     // xb: x in B order
+  float* xs;                 // per-group sum(x) of the T input rows
+  int64_t ldh, ldxs;
   int max_items;
 };
 
@@ -108,13 +109,16 @@ static ExpertScratch carve_experts(Carver& c, int T, const BlockDims& dm) {
   s.active = c.take<int32_t>(dm.E + 1);
   s.n_active = c.take<int32_t>(1);
   s.src_rows = c.take<int32_t>(P + Ts);
-  s.err = c.take<int32_t>(1);
+  s.err = c.take<int32_t>(2);      // [0] dropped ids, [1] pipeline timeouts
   s.max_items = max_items_bound(P, dm.E, int(Ts));
   s.items = c.take<int32_t>(3 * int64_t(s.max_items));
   s.n_items = c.take<int32_t>(1);
   s.ldh = std::max(dm.I, dm.Is);
   s.h = c.take<uint16_t>((P + Ts) * s.ldh);
   s.yd = c.take<uint16_t>((P + Ts) * dm.d);
+  s.xb = c.take<uint16_t>(int64_t(T) * dm.d);
+  s.ldxs = xsum_stride(dm.d);
+  s.xs = c.take<float>(int64_t(T) * s.ldxs);
   return s;
 }
 
@@ -123,10 +127,12 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
                        const BlockDims& dm, const ExpertScratch& s, cudaStream_t st) {
   const int64_t P = int64_t(T) * dm.k;
   const int Ts = dm.shared ? T : 0;
-  cudaError_t e = cudaMemsetAsync(s.err, 0, sizeof(int32_t), st);
+  cudaError_t e = cudaMemsetAsync(s.err, 0, 2 * sizeof(int32_t), st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
   e = launch_permute(routes, P, dm.E, Ts, dm.k, nullptr, s.order, s.inverse, s.offsets, s.active,
                      s.n_active, s.src_rows, s.err, kItemChunk, s.items, s.n_items, st);
+  if (e != cudaSuccess) return vx_cuda_fail(e);
+  e = launch_xprep(x, T, dm.d, s.xb, s.xs, s.ldxs, st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
   profile_mark(st, "permute");
 
@@ -138,12 +144,15 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
     a.s1 = W->shared_up;
   }
   a.E = dm.E;
+  a.err = s.err + 1;
   a.items = s.items;
   a.n_items = s.n_items;
   a.src_rows = s.src_rows;
   a.dst_rows = nullptr;
-  a.x = x;
+  a.x = s.xb;
   a.ldx = dm.d;
+  a.xsum = s.xs;
+  a.ldxs = s.ldxs;
   a.out = s.h;
   a.ldo = s.ldh;
   e = launch_gemv_mma(true, a, s.max_items, int(s.ldh), st);
@@ -154,6 +163,7 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
   b.b0 = W->down;
   if (dm.shared) b.s0 = W->shared_down;
   b.E = dm.E;
+  b.err = s.err + 1;
   b.items = s.items;
   b.n_items = s.n_items;
   b.src_rows = nullptr;
@@ -211,9 +221,11 @@ int vx_swiglu_bf16(const uint16_t* gate, const uint16_t* up, uint16_t* out, int6
   return e == cudaSuccess ? VX_OK : vx_cuda_fail(e);
 }
 
-size_t vx_gather_qmm_workspace(int64_t B, int32_t M, int32_t experts) {
+size_t vx_gather_qmm_workspace(int64_t B, int32_t M, int32_t experts, int64_t x_rows, int32_t K) {
   Carver c(nullptr);
   const int64_t n = B * M;
+  c.take<uint16_t>(x_rows * K);                 // x in B order
+  c.take<float>(x_rows * xsum_stride(K));       // sum(x) per group
   c.take<int32_t>(n);            // keys
   c.take<int32_t>(n);            // src_map
   c.take<int32_t>(n);            // order
@@ -222,7 +234,7 @@ size_t vx_gather_qmm_workspace(int64_t B, int32_t M, int32_t experts) {
   c.take<int32_t>(experts + 1);  // active
   c.take<int32_t>(1);            // n_active
   c.take<int32_t>(n);            // src_rows
-  c.take<int32_t>(1);            // err
+  c.take<int32_t>(2);            // err
   c.take<int32_t>(3 * int64_t(max_items_bound(n, experts, 0)));  // items
   c.take<int32_t>(1);            // n_items
   return c.size();
@@ -239,11 +251,16 @@ int vx_gather_qmm(const uint16_t* x, int64_t x_rows, const vx_q4* w, const int32
   if (B * M > 0x7FFFFFFF) return VX_EUNSUPPORTED;
   if (B == 0) return VX_OK;
   if (!x || !rhs || !out || !aligned16(x)) return VX_EINVAL_SHAPE;
-  if (workspace_bytes < vx_gather_qmm_workspace(B, M, w->experts) || !workspace) return VX_EWORKSPACE;
+  if (x_rows < 0) return VX_EINVAL_SHAPE;
+  if (workspace_bytes < vx_gather_qmm_workspace(B, M, w->experts, x_rows, w->in) || !workspace)
+    return VX_EWORKSPACE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int64_t n = B * M;
   const int E = w->experts;
   Carver c(workspace);
+  uint16_t* xb = c.take<uint16_t>(x_rows * w->in);
+  const int64_t ldxs = xsum_stride(w->in);
+  float* xs = c.take<float>(x_rows * ldxs);
   int32_t* keys = c.take<int32_t>(n);
   int32_t* src_map = c.take<int32_t>(n);
   int32_t* order = c.take<int32_t>(n);
@@ -252,11 +269,12 @@ int vx_gather_qmm(const uint16_t* x, int64_t x_rows, const vx_q4* w, const int32
   int32_t* active = c.take<int32_t>(E + 1);
   int32_t* n_active = c.take<int32_t>(1);
   int32_t* src_rows = c.take<int32_t>(n);
-  int32_t* err = c.take<int32_t>(1);
+  int32_t* err = c.take<int32_t>(2);
   const int max_items = max_items_bound(n, E, 0);
   int32_t* items = c.take<int32_t>(3 * int64_t(max_items));
   int32_t* n_items = c.take<int32_t>(1);
-  cudaError_t e = cudaMemsetAsync(err, 0, sizeof(int32_t), st);
+  cudaError_t e = cudaMemsetAsync(err, 0, 2 * sizeof(int32_t), st);
+  if (e == cudaSuccess) e = launch_xprep(x, x_rows, w->in, xb, xs, ldxs, st);
   if (e == cudaSuccess) e = launch_gather_items(lhs, rhs, B, M, x_rows, keys, src_map, st);
   if (e == cudaSuccess)
     e = launch_permute(keys, n, E, 0, 1, src_map, order, inverse, offsets, active, n_active, src_rows,
@@ -264,13 +282,16 @@ int vx_gather_qmm(const uint16_t* x, int64_t x_rows, const vx_q4* w, const int32
   if (e != cudaSuccess) return vx_cuda_fail(e);
   MmaArgs a{};
   a.b0 = *w;
+  a.err = err + 1;
   a.E = E;
   a.items = items;
   a.n_items = n_items;
   a.src_rows = src_rows;
   a.dst_rows = order;
-  a.x = x;
+  a.x = xb;
   a.ldx = w->in;
+  a.xsum = xs;
+  a.ldxs = ldxs;
   a.out = out;
   a.ldo = w->out;
   e = launch_gemv_mma(false, a, max_items, w->out, st);

@@ -112,6 +112,15 @@ VX_DEVICE uint4 ldg_nc(const void* p) {
   return v;
 }
 
+// "B order" of an activation row: inside each block of 8 inputs the 16-bit
+// slots hold x0 x4 x1 x5 x2 x6 x3 x7, so one 32-bit word is the bf16x2 pair
+// that meets the nibble pairs (0,4) (1,5) (2,6) (3,7) of a packed word in an
+// MMA fragment.  Returns the slot of logical column `col`.
+VX_DEVICE int b_order_col(int col) {
+  const int e = col & 7;
+  return (col & ~7) | (e < 4 ? 2 * e : 2 * (e - 4) + 1);
+}
+
 // Address of expert e's rows in a bank (int64 offsets: a full bank of 512
 // experts spans more than 2^31 bytes).
 struct Q4Ptr {

@@ -68,6 +68,51 @@ cudaError_t launch_combine(const uint16_t* yd, int64_t ldy, const int32_t* inver
   return cudaGetLastError();
 }
 
+// Activations for the grouped GEMV: B order and per-group sums.  One thread
+// per 8-input block; the four threads of a quant group are adjacent lanes
+// (K/8 is a multiple of 4), so the group sum is a two-step xor shuffle:
+// (s0 + s1) + (s2 + s3), each s a left-to-right float32 sum of 8 inputs.
+__global__ void xprep_kernel(const uint16_t* __restrict__ x, int64_t rows, int K,
+                             uint16_t* __restrict__ xb, float* __restrict__ xs, int64_t ldxs) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int nb = K / 8;
+  const int64_t n = rows * nb;
+  const bool live = i < n;
+  const int64_t r = live ? i / nb : 0;
+  const int blk = live ? int(i - r * nb) : 0;
+  uint4 v = make_uint4(0, 0, 0, 0);
+  if (live) v = *reinterpret_cast<const uint4*>(x + r * K + blk * 8);
+  float s = 0.f;
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    s += __uint_as_float(w[j] << 16);
+    s += __uint_as_float(w[j] & 0xFFFF0000u);
+  }
+  s += __shfl_xor_sync(0xFFFFFFFFu, s, 1);
+  s += __shfl_xor_sync(0xFFFFFFFFu, s, 2);
+  if (!live) return;
+  uint4 o;
+  o.x = prmt(v.x, v.z, 0x5410);   // (x0, x4)
+  o.y = prmt(v.x, v.z, 0x7632);   // (x1, x5)
+  o.z = prmt(v.y, v.w, 0x5410);   // (x2, x6)
+  o.w = prmt(v.y, v.w, 0x7632);   // (x3, x7)
+  *reinterpret_cast<uint4*>(xb + r * K + blk * 8) = o;
+  if ((blk & 3) == 0) {
+    const int grp = blk >> 2;
+    xs[r * ldxs + grp] = s;
+    if (grp + 1 == K / 32 && (K / 32) < ldxs) xs[r * ldxs + grp + 1] = 0.f;
+  }
+}
+
+cudaError_t launch_xprep(const uint16_t* x, int64_t rows, int K, uint16_t* xb, float* xs,
+                         int64_t ldxs, cudaStream_t st) {
+  const int64_t n = rows * (K / 8);
+  if (n == 0) return cudaSuccess;
+  xprep_kernel<<<int((n + 255) / 256), 256, 0, st>>>(x, rows, K, xb, xs, ldxs);
+  return cudaGetLastError();
+}
+
 // out[t, s, :] = yd[inverse[t*k+s], :]  (_scatter_unsort)
 __global__ void unpermute_kernel(const uint16_t* __restrict__ yd, int64_t ldy,
                                  const int32_t* __restrict__ inverse, int k, int d,

@@ -2,171 +2,226 @@
 //
 // Regime: few tokens per expert (decode, batched decode).  Work unit = one
 // warp x (item, block of 16*MT output rows); an item is an expert with up to
-// kItemChunk expert-sorted tokens (built by the permute kernel).  Every warp
-// streams its rows over the whole input width through its own 3-stage
-// cp.async ring in shared memory (weights, scales and activations), so the
-// bytes in flight do not cost registers and no block synchronisation is
-// needed: each lane only reads back what it copied itself.
+// two expert-sorted tokens (built by the permute kernel).  Each warp streams
+// its rows over the whole input width through its own 3-stage pipeline in
+// shared memory: one lane issues a 2-D TMA copy per projection per
+// 128-input chunk (16*MT rows x 64 bytes, completed on an mbarrier), and the
+// small operands - activations, their per-group sums, the group
+// scales/biases - ride cp.async copies into the same stage.  No block
+// synchronisation: the warp's own mbarriers and async-copy groups order it.
 //
-// Layout trick ("block-diagonal B").  Lane (g = lane/4, c = lane%4) copies 16
-// bytes of row g (and row g+8): words 4c..4c+3 of a 128-input chunk, i.e. the
-// whole quant group c of that chunk.  Each nibble becomes an exact bf16 via
-// lop3 (0x4300 | q = 128+q) and a bf16x2 subtract of 128.  Within one
-// m16n8k16 MMA lane c supplies four inputs of its own group, so one MMA mixes
-// four groups along k.  B is block-diagonal: column n = 4*tok + grp holds
-// token tok's x only on the k positions of group grp and zero elsewhere, so
-// D[row][4*tok + grp] is the per-group partial sum(q*x) of that row - the
-// quantity MLX's qmv scales by the group's scale (models/flashnext/
-// metal_runtime.py:1014-1029).  Eight MMAs cover a chunk of 4 groups for two
-// tokens; an MMA with A = ones over the same B yields sum(x) per group.  The
-// epilogue adds scale*sum(q*x) + bias*sum(x) per group in float32, and the
-// two lanes holding a row's group halves meet in one shuffle.  An item's
-// token pairs share one sweep over the weights: every unpacked A fragment
-// feeds one MMA per pair.
+// Layout trick ("block-diagonal B").  Lane (g = lane/4, c = lane%4) reads 16
+// bytes of row g (and row g+8): words 4c..4c+3 of the chunk, i.e. the whole
+// quant group c.  A nibble q becomes the exact bf16 128+q through one lop3
+// with 0x4300.  Within one m16n8k16 MMA lane c supplies four inputs of its
+// own group, so one MMA mixes four groups along k.  B is block-diagonal:
+// column n = 4*tok + grp holds token tok's x only on the k positions of
+// group grp, so D[row][4*tok + grp] = sum((128+q)*x) over that group.  The
+// epilogue applies MLX's qmv formula per group (models/flashnext/
+// metal_runtime.py:1014-1029),
+//     scale*sum(q*x) + bias*sum(x) = scale*D + (bias - 128*scale)*sum(x),
+// in float32; the two lanes holding a row's group halves meet in one shuffle.
+//
+// Activations arrive in "B order" (within each 8-input block the words hold
+// the pairs (0,4) (1,5) (2,6) (3,7)), so a B lane's 16-byte loads are its
+// MMA fragments as they stand; sum(x) per group comes from a precomputed
+// table (gate/up, gather_qmm) or from an MMA with A = ones over the same B
+// (down, whose input h this kernel writes itself).
+#include <cudaTypedefs.h>
+
 #include "vx_common.cuh"
 #include "vx_launch.h"
 
 namespace vx {
 
 constexpr int kMmaThreads = 256;
+constexpr int kWarps = kMmaThreads / 32;
 constexpr int kStages = 3;
-constexpr int kPairs = kItemChunk / 2;
+constexpr uint32_t kSpinLimit = 1u << 24;   // bounded mbarrier waits
 
-VX_DEVICE uint32_t nib_pair(uint32_t w_shifted) {
-  // {128 + (w & 15), 128 + ((w >> 16) & 15)} as bf16x2, then minus 128: exact.
+VX_DEVICE uint32_t nib_pair128(uint32_t w_shifted) {
+  // {128 + (w & 15), 128 + ((w >> 16) & 15)} as bf16x2 (exact).
   uint32_t r;
   asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(w_shifted), "r"(0x000F000Fu), "r"(0x43004300u));
-  uint32_t out;
-  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(out) : "r"(r), "r"(0x3F803F80u), "r"(0xC300C300u));
-  return out;
+  return r;
 }
 
 VX_DEVICE uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-// 16/4-byte async copies; src_bytes = 0 writes zeros without reading.
-VX_DEVICE void cp16(void* dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
-               "r"(valid ? 16 : 0)
+// Async copies.  src_bytes = 0 writes zeros without reading; the _if form
+// issues nothing when the predicate is false.
+VX_DEVICE void cp16_if(uint32_t dst, const void* src, int src_bytes, bool pred) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %3, 0; @p cp.async.cg.shared.global [%0], [%1], 16, %2; }" ::"r"(dst),
+      "l"(src), "r"(src_bytes), "r"(int(pred))
+      : "memory");
+}
+VX_DEVICE void cp4(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(valid ? 4 : 0)
                : "memory");
 }
-VX_DEVICE void cp4(void* dst, const void* src, bool valid) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src),
-               "r"(valid ? 4 : 0)
+VX_DEVICE void cp8(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst), "l"(src), "r"(valid ? 8 : 0)
                : "memory");
 }
 VX_DEVICE void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 VX_DEVICE void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// Per-warp stage, in 16-byte units.
-template <int NP, int MT>
-struct StageLayout {
-  static constexpr int kW = NP * MT * 2 * 32;            // weights [p][m][h][lane]
-  static constexpr int kS = NP * MT * 2 * 32 / 2;        // scale+bias pairs, 8 B each
-  static constexpr int kX = kPairs * 8 * 4;              // x: [pair][b-lane g][4]
-  static constexpr int kTotal = kW + kS + kX;
+VX_DEVICE uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+VX_DEVICE uint2 lds64(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
+
+// mbarrier helpers (one barrier per warp per stage, count 1: the issuing lane).
+VX_DEVICE void mbar_init(uint32_t bar) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
+}
+VX_DEVICE void mbar_expect(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+VX_DEVICE bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Waits with an iteration limit; on expiry the caller records an error.
+VX_DEVICE bool mbar_wait(uint32_t bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i)
+    if (mbar_try(bar, parity)) return true;
+  return false;
+}
+VX_DEVICE void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// One pipeline stage of one warp, bytes (multiples of 128).
+template <int NP, int MT, bool XMMA>
+struct Stage {
+  static constexpr int kWRows = 16 * MT;
+  static constexpr int kW = NP * kWRows * 64;            // TMA boxes [p][row][64 B]
+  static constexpr int kS = NP * MT * 32 * 16;           // scales [p][m][lane]{s_g b_g s_g8 b_g8}
+  static constexpr int kX = 4 * 8 * 16;                  // x: [i][b-lane g][16 B]
+  static constexpr int kXS = XMMA ? 0 : 32 * 8;          // sum(x) pairs [lane]
+  static constexpr int kRaw = kW + kS + kX + kXS;
+  static constexpr int kBytes = (kRaw + 127) & ~127;
 };
 
-template <bool GATEUP, int MT>
-__global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(MmaArgs a) {
+template <bool GATEUP, int MT, bool XMMA, bool EVEN>
+__global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(const __grid_constant__ MmaArgs a) {
   constexpr int NP = GATEUP ? 2 : 1;
-  using L = StageLayout<NP, MT>;
-  extern __shared__ uint4 smem4[];
+  using S = Stage<NP, MT, XMMA>;
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ __align__(8) uint64_t bars[kWarps][kStages];
+  __shared__ __align__(16) uint32_t zero16[4];   // B operand of the non-B lanes
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
-  uint4* ring = smem4 + warp * kStages * L::kTotal;
+  if (threadIdx.x < 4) zero16[threadIdx.x] = 0u;
+  if (lane == 0)
+    for (int s = 0; s < kStages; ++s) mbar_init(smem_u32(&bars[warp][s]));
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  __syncthreads();
+  const uint32_t ring = smem_u32(smem) + warp * kStages * S::kBytes;
+  const uint32_t bar0 = smem_u32(&bars[warp][0]);
+  const uint32_t zaddr = smem_u32(zero16);
+  const bool blane = (g & 3) == c;   // carries token (g >> 2) on group c
   const int n_items = *a.n_items;
   const int total = n_items * a.tiles_per_item;
-  const int nw = gridDim.x * (kMmaThreads / 32);
-  for (int t = blockIdx.x * (kMmaThreads / 32) + warp; t < total; t += nw) {
+  const int nw = gridDim.x * kWarps;
+  // Ring position of the next chunk to issue / consume, and the mbarrier
+  // phase parity of the consumed stage.
+  int st_issue = 0, st_use = 0;
+  uint32_t parity_bits = 0;          // bit s: parity expected next on stage s
+  bool timed_out = false;
+
+  for (int t = blockIdx.x * kWarps + warp; t < total; t += nw) {
     const int item = t / a.tiles_per_item, rb = t - item * a.tiles_per_item;
     const int e = __ldg(a.items + 3 * item), p0 = __ldg(a.items + 3 * item + 1);
     const int cnt = __ldg(a.items + 3 * item + 2);
     const bool sh = e == a.E;
-    Q4Ptr pp[NP];
     const vx_q4& B0 = sh ? a.s0 : a.b0;
+    Q4Ptr pp[NP];
     pp[0] = q4_expert(B0, sh ? 0 : e);
     if (GATEUP) pp[NP - 1] = q4_expert(sh ? a.s1 : a.b1, sh ? 0 : e);
-    const int N = B0.out, K = B0.in, KW = K >> 3, G = K >> 5;
-    const bool even_g = (G & 1) == 0;
+    const CUtensorMap* tm[NP];
+    tm[0] = sh ? &a.tm_s0 : &a.tm_b0;
+    if (GATEUP) tm[NP - 1] = sh ? &a.tm_s1 : &a.tm_b1;
+    const int N = B0.out, K = B0.in, G = K >> 5;
     const int nch = (K + 127) >> 7;
     const int row0 = rb * 16 * MT;
     if (row0 >= N) continue;  // warp-uniform
-    const int npairs = (cnt + 1) >> 1;
+    const int trow = (sh ? 0 : e * N) + row0;   // first row in the bank's 2-D view
 
-    int rows[MT][2];
+    int soff[MT][2];
     bool rv[MT][2];
 #pragma unroll
     for (int m = 0; m < MT; ++m)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        rows[m][h] = row0 + 16 * m + g + 8 * h;
-        rv[m][h] = rows[m][h] < N;
+        const int row = row0 + 16 * m + g + 8 * h;
+        rv[m][h] = row < N;
+        soff[m][h] = (rv[m][h] ? row : 0) * G + 2 * (c & 1);
       }
-    // B lanes: (g & 3) == c carries token 2*pair + (g >> 2) on group c.
-    const bool blane = (g & 3) == c;
-    const uint16_t* xrow[kPairs];
-#pragma unroll
-    for (int q = 0; q < kPairs; ++q) {
-      const int tok = 2 * q + (g >> 2);
-      xrow[q] = nullptr;
-      if (blane && tok < cnt) {
-        const int pos = p0 + tok;
-        const int64_t r = a.src_rows ? __ldg(a.src_rows + pos) : pos;
-        xrow[q] = a.x + r * a.ldx;
-      }
-    }
+    const int tb = g >> 2, ts = c >> 1;
+    const bool xbv = blane && tb < cnt, xsv = ts < cnt;
+    int64_t rb_ = 0, rs_ = 0;
+    if (xbv) rb_ = a.src_rows ? __ldg(a.src_rows + p0 + tb) : p0 + tb;
+    if (!XMMA && xsv) rs_ = a.src_rows ? __ldg(a.src_rows + p0 + ts) : p0 + ts;
+    const uint16_t* xb = a.x + rb_ * a.ldx + c * 32;
+    const float* xsp = XMMA ? a.xsum : a.xsum + rs_ * a.ldxs + 2 * (c & 1);
 
     auto issue = [&](int ch) {
-      uint4* st = ring + (ch % kStages) * L::kTotal;
-      const int grp = 4 * ch + c;
+      const uint32_t st = ring + st_issue * S::kBytes;
+      if (lane == 0) {
+        const uint32_t bar = bar0 + 8 * st_issue;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_expect(bar, NP * S::kWRows * 64);
 #pragma unroll
-      for (int p = 0; p < NP; ++p)
-#pragma unroll
-        for (int m = 0; m < MT; ++m)
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const bool ok = rv[m][h] && grp < G;
-            const uint32_t* src = ok ? pp[p].w + int64_t(rows[m][h]) * KW + grp * 4 : pp[p].w;
-            cp16(st + ((p * MT + m) * 2 + h) * 32 + lane, src, ok);
-          }
-      if (even_g) {
-        const int gA = 4 * ch + 2 * (c & 1);
-        uint32_t* sp = reinterpret_cast<uint32_t*>(st + L::kW);
+        for (int p = 0; p < NP; ++p) tma_load_2d(st + p * S::kWRows * 64, tm[p], ch * 16, trow, bar);
+      }
+      const bool sok = 4 * ch + 2 * (c & 1) < G;
+      if (EVEN) {
 #pragma unroll
         for (int p = 0; p < NP; ++p)
 #pragma unroll
-          for (int m = 0; m < MT; ++m)
+          for (int m = 0; m < MT; ++m) {
+            const uint32_t d = st + S::kW + ((p * MT + m) * 32 + lane) * 16;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              const bool ok = rv[m][h] && gA < G;
-              const int64_t mi = ok ? int64_t(rows[m][h]) * G + gA : 0;
-              const int slot = ((p * MT + m) * 2 + h) * 32 + lane;
-              cp4(sp + 2 * slot, pp[p].s + mi, ok);
-              cp4(sp + 2 * slot + 1, pp[p].b + mi, ok);
+              cp4(d + 8 * h, pp[p].s + soff[m][h] + ch * 4, rv[m][h] && sok);
+              cp4(d + 8 * h + 4, pp[p].b + soff[m][h] + ch * 4, rv[m][h] && sok);
             }
+          }
       }
-      if (blane) {
-        uint4* xp = st + L::kW + L::kS;
+      const int nbytes = (xbv && 4 * ch + c < G) ? 16 : 0;
 #pragma unroll
-        for (int q = 0; q < kPairs; ++q) {
-          const bool ok = xrow[q] != nullptr && grp < G;
-          const uint16_t* src = ok ? xrow[q] + grp * 32 : a.x;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) cp16(xp + (q * 8 + g) * 4 + i, src + 8 * i, ok);
-        }
-      }
+      for (int i = 0; i < 4; ++i)
+        cp16_if(st + S::kW + S::kS + (i * 8 + g) * 16, xb + ch * 128 + 8 * i, nbytes, blane);
+      if (!XMMA) cp8(st + S::kW + S::kS + S::kX + lane * 8, xsp + ch * 4, xsv && sok);
+      st_issue = st_issue == kStages - 1 ? 0 : st_issue + 1;
     };
 
-    float acc[kPairs][NP][MT][2];
+    float acc[NP][MT][2];
 #pragma unroll
-    for (int q = 0; q < kPairs; ++q)
+    for (int p = 0; p < NP; ++p)
 #pragma unroll
-      for (int p = 0; p < NP; ++p)
-#pragma unroll
-        for (int m = 0; m < MT; ++m) acc[q][p][m][0] = acc[q][p][m][1] = 0.f;
+      for (int m = 0; m < MT; ++m) acc[p][m][0] = acc[p][m][1] = 0.f;
 
 #pragma unroll
     for (int s = 0; s < kStages - 1; ++s) {
@@ -177,142 +232,204 @@ __global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(MmaArgs a) {
       if (ch + kStages - 1 < nch) issue(ch + kStages - 1);
       cp_commit();
       cp_wait<kStages - 1>();
-      const uint4* st = ring + (ch % kStages) * L::kTotal;
-      // B fragments and sum(x) per pair.
-      uint32_t bq[kPairs][16];
-      float xs[kPairs][4];
+      const uint32_t st = ring + st_use * S::kBytes;
+      if (!mbar_wait(bar0 + 8 * st_use, (parity_bits >> st_use) & 1u)) timed_out = true;
+      parity_bits ^= 1u << st_use;
+
+      uint32_t bq[16];
+      const uint32_t xa = blane ? st + S::kW + S::kS + g * 16 : zaddr;
+      const uint32_t xstep = blane ? 8 * 16 : 0;
 #pragma unroll
-      for (int q = 0; q < kPairs; ++q) {
-        if (q < npairs && blane) {
-          const uint4* xp = st + L::kW + L::kS + (q * 8 + g) * 4;
+      for (int i = 0; i < 4; ++i) {
+        const uint4 v = lds128(xa + i * xstep);
+        bq[4 * i + 0] = v.x;
+        bq[4 * i + 1] = v.y;
+        bq[4 * i + 2] = v.z;
+        bq[4 * i + 3] = v.w;
+      }
+      float xs0, xs1;
+      if (XMMA) {
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint4 v = xp[i];
-            bq[q][4 * i + 0] = prmt(v.x, v.z, 0x5410);   // (x0, x4)
-            bq[q][4 * i + 1] = prmt(v.x, v.z, 0x7632);   // (x1, x5)
-            bq[q][4 * i + 2] = prmt(v.y, v.w, 0x5410);   // (x2, x6)
-            bq[q][4 * i + 3] = prmt(v.y, v.w, 0x7632);   // (x3, x7)
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) bq[q][i] = 0u;
-        }
-        xs[q][0] = xs[q][1] = xs[q][2] = xs[q][3] = 0.f;
-        if (q < npairs) {
-#pragma unroll
-          for (int mm = 0; mm < 8; ++mm)
-            mma16816(xs[q], 0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u, bq[q][2 * mm],
-                     bq[q][2 * mm + 1]);
-        }
+        for (int mm = 0; mm < 8; ++mm)
+          mma16816(d, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u, bq[2 * mm], bq[2 * mm + 1]);
+        xs0 = d[0];
+        xs1 = d[1];
+      } else {
+        const uint2 v = lds64(st + S::kW + S::kS + S::kX + lane * 8);
+        xs0 = __uint_as_float(v.x);
+        xs1 = __uint_as_float(v.y);
       }
       const int gA = 4 * ch + 2 * (c & 1);   // groups of D columns 2c, 2c+1
 #pragma unroll
       for (int p = 0; p < NP; ++p) {
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
-          const uint4 wg = st[((p * MT + m) * 2 + 0) * 32 + lane];
-          const uint4 w8 = st[((p * MT + m) * 2 + 1) * 32 + lane];
+          const uint32_t wrow = st + p * S::kWRows * 64 + (16 * m + g) * 64 + c * 16;
+          const uint4 wg = lds128(wrow), w8 = lds128(wrow + 8 * 64);
           const uint32_t ag[4] = {wg.x, wg.y, wg.z, wg.w};
           const uint32_t a8[4] = {w8.x, w8.y, w8.z, w8.w};
-          float d[kPairs][4];
+          // Two independent accumulator chains (even / odd MMAs) halve the
+          // dependent MMA latency per chunk.
+          float d[4] = {0.f, 0.f, 0.f, 0.f}, e2[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int q = 0; q < kPairs; ++q) d[q][0] = d[q][1] = d[q][2] = d[q][3] = 0.f;
-#pragma unroll
-          for (int mm = 0; mm < 8; ++mm) {
+          for (int mm = 0; mm < 8; mm += 2) {
             const int wi = mm >> 1;
-            const int s = (mm & 1) ? 8 : 0;
-            const uint32_t a0 = nib_pair(ag[wi] >> s), a1 = nib_pair(a8[wi] >> s);
-            const uint32_t a2 = nib_pair(ag[wi] >> (s + 4)), a3 = nib_pair(a8[wi] >> (s + 4));
-            mma16816(d[0], a0, a1, a2, a3, bq[0][2 * mm], bq[0][2 * mm + 1]);
+            mma16816(d, nib_pair128(ag[wi]), nib_pair128(a8[wi]), nib_pair128(ag[wi] >> 4),
+                     nib_pair128(a8[wi] >> 4), bq[2 * mm], bq[2 * mm + 1]);
+            mma16816(e2, nib_pair128(ag[wi] >> 8), nib_pair128(a8[wi] >> 8),
+                     nib_pair128(ag[wi] >> 12), nib_pair128(a8[wi] >> 12), bq[2 * mm + 2],
+                     bq[2 * mm + 3]);
+          }
 #pragma unroll
-            for (int q = 1; q < kPairs; ++q)
-              if (q < npairs) mma16816(d[q], a0, a1, a2, a3, bq[q][2 * mm], bq[q][2 * mm + 1]);
+          for (int i = 0; i < 4; ++i) d[i] += e2[i];
+          float sc[2][4];   // [h] {s0, s1, b0, b1}
+          if (EVEN) {
+            const uint4 sb = lds128(st + S::kW + ((p * MT + m) * 32 + lane) * 16);
+            const uint32_t sw[4] = {sb.x, sb.y, sb.z, sb.w};
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              sc[h][0] = __uint_as_float(sw[2 * h] << 16);
+              sc[h][1] = __uint_as_float(sw[2 * h] & 0xFFFF0000u);
+              sc[h][2] = __uint_as_float(sw[2 * h + 1] << 16);
+              sc[h][3] = __uint_as_float(sw[2 * h + 1] & 0xFFFF0000u);
+            }
+          } else {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const bool ok0 = rv[m][h] && gA < G, ok1 = rv[m][h] && gA + 1 < G;
+              const int64_t mi = soff[m][h] + ch * 4;
+              sc[h][0] = ok0 ? bf16_to_f32(pp[p].s[mi]) : 0.f;
+              sc[h][1] = ok1 ? bf16_to_f32(pp[p].s[mi + 1]) : 0.f;
+              sc[h][2] = ok0 ? bf16_to_f32(pp[p].b[mi]) : 0.f;
+              sc[h][3] = ok1 ? bf16_to_f32(pp[p].b[mi + 1]) : 0.f;
+            }
           }
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            if (!rv[m][h] || gA >= G) continue;
-            float s0, s1, b0, b1;
-            if (even_g) {
-              const uint2 sb = reinterpret_cast<const uint2*>(st + L::kW)[((p * MT + m) * 2 + h) * 32 + lane];
-              s0 = __uint_as_float(sb.x << 16);
-              s1 = __uint_as_float(sb.x & 0xFFFF0000u);
-              b0 = __uint_as_float(sb.y << 16);
-              b1 = __uint_as_float(sb.y & 0xFFFF0000u);
-            } else {
-              const int64_t mi = int64_t(rows[m][h]) * G + gA;
-              const bool two = gA + 1 < G;
-              s0 = bf16_to_f32(pp[p].s[mi]);
-              b0 = bf16_to_f32(pp[p].b[mi]);
-              s1 = two ? bf16_to_f32(pp[p].s[mi + 1]) : 0.f;
-              b1 = two ? bf16_to_f32(pp[p].b[mi + 1]) : 0.f;
-            }
-#pragma unroll
-            for (int q = 0; q < kPairs; ++q) {
-              float v = acc[q][p][m][h];
-              v += fmaf(s0, d[q][2 * h], b0 * xs[q][0]);
-              v += fmaf(s1, d[q][2 * h + 1], b1 * xs[q][1]);
-              acc[q][p][m][h] = v;
-            }
+            // bias - 128*scale: the lop3 operands carry q + 128.
+            const float c0 = fmaf(-128.f, sc[h][0], sc[h][2]);
+            const float c1 = fmaf(-128.f, sc[h][1], sc[h][3]);
+            float v = acc[p][m][h];
+            v = fmaf(sc[h][0], d[2 * h], v);
+            v = fmaf(c0, xs0, v);
+            v = fmaf(sc[h][1], d[2 * h + 1], v);
+            v = fmaf(c1, xs1, v);
+            acc[p][m][h] = v;
           }
         }
       }
+      __syncwarp();   // the stage is read out before the warp refills it
+      st_use = st_use == kStages - 1 ? 0 : st_use + 1;
     }
-    cp_wait<0>();
+
     // lanes c and c^1 hold the two group halves of the same (row, token)
 #pragma unroll
-    for (int q = 0; q < kPairs; ++q) {
+    for (int p = 0; p < NP; ++p)
 #pragma unroll
-      for (int p = 0; p < NP; ++p)
+      for (int m = 0; m < MT; ++m)
 #pragma unroll
-        for (int m = 0; m < MT; ++m)
+        for (int h = 0; h < 2; ++h) acc[p][m][h] += __shfl_xor_sync(0xFFFFFFFFu, acc[p][m][h], 1);
+    const int tok = c >> 1;
+    if ((c & 1) == 0 && tok < cnt) {
+      const int pos = p0 + tok;
+      const int64_t dst = a.dst_rows ? __ldg(a.dst_rows + pos) : pos;
 #pragma unroll
-          for (int h = 0; h < 2; ++h)
-            acc[q][p][m][h] += __shfl_xor_sync(0xFFFFFFFFu, acc[q][p][m][h], 1);
-      const int tok = 2 * q + (c >> 1);
-      if ((c & 1) == 0 && tok < cnt) {
-        const int pos = p0 + tok;
-        const int64_t dst = a.dst_rows ? __ldg(a.dst_rows + pos) : pos;
+      for (int m = 0; m < MT; ++m)
 #pragma unroll
-        for (int m = 0; m < MT; ++m)
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            if (!rv[m][h]) continue;
-            float v;
-            if (GATEUP) v = silu_mul_bf16(bf16r(acc[q][0][m][h]), bf16r(acc[q][NP - 1][m][h]));
-            else v = acc[q][0][m][h];
-            a.out[dst * a.ldo + rows[m][h]] = f32_to_bf16(v);
+        for (int h = 0; h < 2; ++h) {
+          if (!rv[m][h]) continue;
+          const int row = row0 + 16 * m + g + 8 * h;
+          if (GATEUP) {
+            // h is the next projection's input: store it in B order.
+            const float v = silu_mul_bf16(bf16r(acc[0][m][h]), bf16r(acc[NP - 1][m][h]));
+            a.out[dst * a.ldo + b_order_col(row)] = f32_to_bf16(v);
+          } else {
+            a.out[dst * a.ldo + row] = f32_to_bf16(acc[0][m][h]);
           }
-      }
+        }
     }
   }
+  cp_wait<0>();
+  if (timed_out && a.err) atomicOr(a.err, 0x100);
 }
 
-template <bool GATEUP, int MT>
+// ---- host side --------------------------------------------------------------
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// The packed words of a bank as a 2-D tensor [experts*out rows][in/8 words];
+// box = 16 words (64 B) x box_rows rows; out-of-range reads fill zeros.
+static cudaError_t encode_bank(CUtensorMap* m, const vx_q4& b, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  const cuuint64_t dims[2] = {cuuint64_t(b.in / 8), cuuint64_t(b.experts) * cuuint64_t(b.out)};
+  const cuuint64_t strides[1] = {cuuint64_t(b.in / 8) * 4};
+  const cuuint32_t box[2] = {16, cuuint32_t(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t*>(b.w), dims, strides,
+                        box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+template <bool GATEUP, int MT, bool XMMA, bool EVEN>
 static cudaError_t launch_mma_t(MmaArgs a, int max_items, int max_out, cudaStream_t st) {
   constexpr int NP = GATEUP ? 2 : 1;
+  cudaError_t err = encode_bank(&a.tm_b0, a.b0, 16 * MT);
+  if (err == cudaSuccess && GATEUP) err = encode_bank(&a.tm_b1, a.b1, 16 * MT);
+  if (err == cudaSuccess && a.s0.w) err = encode_bank(&a.tm_s0, a.s0, 16 * MT);
+  if (err == cudaSuccess && GATEUP && a.s1.w) err = encode_bank(&a.tm_s1, a.s1, 16 * MT);
+  if (err != cudaSuccess) return err;
   a.tiles_per_item = (max_out + 16 * MT - 1) / (16 * MT);
-  const size_t smem = size_t(kMmaThreads / 32) * kStages * StageLayout<NP, MT>::kTotal * sizeof(uint4);
-  auto kern = gemv_mma_kernel<GATEUP, MT>;
-  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  const size_t smem = size_t(kWarps) * kStages * Stage<NP, MT, XMMA>::kBytes;
+  auto kern = gemv_mma_kernel<GATEUP, MT, XMMA, EVEN>;
+  err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (err != cudaSuccess) return err;
   const int64_t warps = int64_t(max_items) * a.tiles_per_item;
   const int64_t cap = int64_t(sm_count()) * 2;  // two resident CTAs per SM, persistent
-  int64_t grid = (warps + 7) / 8;
+  int64_t grid = (warps + kWarps - 1) / kWarps;
   if (grid > cap) grid = cap;
   if (grid <= 0) return cudaSuccess;
   kern<<<int(grid), kMmaThreads, smem, st>>>(a);
   return cudaGetLastError();
 }
 
+template <bool GATEUP, int MT, bool XMMA>
+static cudaError_t launch_even(const MmaArgs& a, bool even, int max_items, int max_out, cudaStream_t st) {
+  return even ? launch_mma_t<GATEUP, MT, XMMA, true>(a, max_items, max_out, st)
+              : launch_mma_t<GATEUP, MT, XMMA, false>(a, max_items, max_out, st);
+}
+
 cudaError_t launch_gemv_mma(bool gateup, const MmaArgs& a, int max_items, int max_out,
                             cudaStream_t st) {
-  // gate/up holds two projections per row block: one m-tile each.  The down
-  // projection takes 32-row tiles when there is plenty of work.
-  if (gateup) return launch_mma_t<true, 1>(a, max_items, max_out, st);
+  // Even group counts (every input width that is a multiple of 64) copy the
+  // scales with the pipeline; odd ones read them directly.
+  bool even = (a.b0.in / 32) % 2 == 0;
+  if (a.s0.w) even = even && (a.s0.in / 32) % 2 == 0;
+  const bool xmma = a.xsum == nullptr;
+  if (gateup) {
+    return xmma ? launch_even<true, 1, true>(a, even, max_items, max_out, st)
+                : launch_even<true, 1, false>(a, even, max_items, max_out, st);
+  }
+  // gate/up holds two projections per row block: one m-tile each.  The
+  // single projection takes 32-row tiles when there is plenty of work.
   const int64_t rows_work = int64_t(max_items) * max_out;
   const bool small = rows_work < int64_t(sm_count()) * 16 * 32;
-  return small ? launch_mma_t<false, 1>(a, max_items, max_out, st)
-               : launch_mma_t<false, 2>(a, max_items, max_out, st);
+  if (xmma) return small ? launch_even<false, 1, true>(a, even, max_items, max_out, st)
+                         : launch_even<false, 2, true>(a, even, max_items, max_out, st);
+  return small ? launch_even<false, 1, false>(a, even, max_items, max_out, st)
+               : launch_even<false, 2, false>(a, even, max_items, max_out, st);
 }
 
 }  // namespace vx

@@ -1,6 +1,7 @@
 // Host-side launchers shared between the kernel files and the C ABI layer.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -9,11 +10,14 @@
 namespace vx {
 
 // Tokens per work item of the tensor-pipe GEMV (an expert's run is cut into
-// items of at most this many positions).  The GEMV handles an item's tokens
-// two per MMA, all in one sweep over the expert's weights.
-constexpr int kItemChunk = 4;
+// items of at most this many positions).  The GEMV's block-diagonal B holds
+// two tokens per MMA.
+constexpr int kItemChunk = 2;
 
 struct MmaArgs {
+  CUtensorMap tm_b0, tm_b1;  // 2-D views of the packed words (set by the launcher)
+  CUtensorMap tm_s0, tm_s1;
+  int32_t* err;              // bit 8 set when a pipeline wait ran out (may be null)
   vx_q4 b0, b1;              // routed banks (b1: up in gate/up mode)
   vx_q4 s0, s1;              // shared expert banks (expert id E)
   int E;
@@ -21,12 +25,20 @@ struct MmaArgs {
   const int32_t* n_items;
   const int32_t* src_rows;   // x row of each position (null: identity)
   const int32_t* dst_rows;   // out row of each position (null: identity)
-  const uint16_t* x;
+  const uint16_t* x;         // activations in B order (see b_order_col)
   int64_t ldx;
-  uint16_t* out;
+  const float* xsum;         // [rows][ldxs] sum(x) per group, or null: sum on the tensor pipe
+  int64_t ldxs;
+  uint16_t* out;             // gate/up mode writes B order, projection mode plain rows
   int64_t ldo;
   int tiles_per_item;        // set by the launcher
 };
+
+// x [rows, K] bf16 -> xb [rows, K] in B order and xs [rows, ldxs] float32
+// per-group sums (ldxs = K/32 rounded up to even; the pad column is zero).
+cudaError_t launch_xprep(const uint16_t* x, int64_t rows, int K, uint16_t* xb, float* xs,
+                         int64_t ldxs, cudaStream_t st);
+inline int64_t xsum_stride(int K) { return ((K / 32) + 1) & ~1; }
 
 cudaError_t launch_gemv_mma(bool gateup, const MmaArgs& a, int max_items, int max_out,
                             cudaStream_t st);

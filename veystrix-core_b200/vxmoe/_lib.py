@@ -53,7 +53,7 @@ SIGNATURES = {
     "vx_last_cuda_error": (ctypes.c_char_p, []),
     "vx_q4_dequant": (ctypes.c_int, [ctypes.POINTER(VxQ4), c_int32, P, P]),
     "vx_swiglu_bf16": (ctypes.c_int, [P, P, P, c_int64, P]),
-    "vx_gather_qmm_workspace": (c_size_t, [c_int64, c_int32, c_int32]),
+    "vx_gather_qmm_workspace": (c_size_t, [c_int64, c_int32, c_int32, c_int64, c_int32]),
     "vx_gather_qmm": (ctypes.c_int, [P, c_int64, ctypes.POINTER(VxQ4), P, P, c_int64, c_int32,
                                      c_int32, P, P, c_size_t, P]),
     "vx_softmax_topk": (ctypes.c_int, [P, c_int32, c_int32, c_int32, P, P, P, P, P]),

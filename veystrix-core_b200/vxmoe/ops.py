@@ -331,7 +331,7 @@ def gather_qmm(x, w, scales, biases, lhs_indices=None, rhs_indices=None, transpo
     if B == 0:
         return out
     lib = _lib.load()
-    nbytes = lib.vx_gather_qmm_workspace(B, M, proj.experts)
+    nbytes = lib.vx_gather_qmm_workspace(B, M, proj.experts, nb * M, K)
     ws = _WS.get(nbytes, dev)
     q = proj.vx()
     _lib.check(lib.vx_gather_qmm(x.data_ptr(), nb * M, ctypes.byref(q), lhs_b.data_ptr(),
