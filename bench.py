@@ -128,39 +128,48 @@ class ClockSampler:
 # --------------------------------------------------------------------------
 
 
-def cpu_oracle_time(tokens_per_step, steps, warmup, seed=0):
-    """Time the oracle's block on `tokens_per_step` tokens per step.
-    Returns (tokens/s, cores, kind, sample description)."""
+def cpu_oracle_time(steps, warmup, budget_s, tokens=64, seed=0):
+    """Time the CPU restatement of the block (the reference's MLX path is not
+    installable here) on steps of the benchmark workload, shrinking the
+    tokens per step (powers of two) so `steps` fit in about `budget_s`.
+    Returns (tokens/s, cores, kind, sample description, tokens per step)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import numpy as np
     import vxmoe_oracle as O
     try:
-        import vxmoe_cref as C   # C/OpenMP restatement, when built
-        runner, cores, kind = C.block_runner(seed), C.threads(), "port"
-        params = None
+        import vxmoe_cref as C   # C/OpenMP restatement
+        runner, cores = C.block_runner(seed), C.threads()
+        impl = f"C/OpenMP restatement of the block on {cores} host threads"
     except Exception:
-        C = None
         params = O.make_params(seed=seed)
-        runner, cores, kind = (lambda x: O.moe_block(x, params)), 1, "port"
+        runner, cores = (lambda x: O.moe_block(x, params)), 1
+        impl = "NumPy restatement of the block on 1 host thread"
     rng = np.random.default_rng(seed + 1)
-    xs = [O.bf16_round(rng.normal(0, 1, size=(tokens_per_step, HIDDEN))) for _ in range(steps + warmup)]
+    probe = O.bf16_round(rng.normal(0, 1, size=(tokens, HIDDEN)))
+    runner(probe)
+    t0 = time.perf_counter()
+    runner(probe)
+    t_full = time.perf_counter() - t0
+    per = tokens
+    while per > 1 and steps * t_full * per / tokens > budget_s:
+        per //= 2
+    xs = [O.bf16_round(rng.normal(0, 1, size=(per, HIDDEN))) for _ in range(steps + warmup)]
     for i in range(warmup):
         runner(xs[i])
     t0 = time.perf_counter()
     for i in range(steps):
         runner(xs[warmup + i])
     dt = time.perf_counter() - t0
-    impl = "C/OpenMP restatement" if C is not None else "NumPy restatement"
-    sample = (f"{impl} of the block (MLX unavailable), {steps} steps x {tokens_per_step} tokens "
-              f"of the same layer shape")
-    return steps * tokens_per_step / dt, cores, kind, sample
+    sample = (f"{impl} (MLX unavailable): {steps} steps of {per} of the workload's {tokens} "
+              f"decode tokens, same layer shape and distributions")
+    return steps * per / dt, cores, "port", sample, per
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    per_step = 1
-    v, cores, kind, sample = cpu_oracle_time(per_step, args.steps, max(1, min(args.warmup, 3)))
+    v, cores, kind, sample, per_step = cpu_oracle_time(args.steps, max(1, min(args.warmup, 3)),
+                                                       budget_s=150.0, tokens=args.tokens)
     line = {
         "metric": METRIC, "value": round(v, 3), "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000.0 * per_step / v, 3),
@@ -313,7 +322,7 @@ def main():
                 "avg_launch_ms": round(avg_ms, 5)}
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        v, cores, kind, sample = cpu_oracle_time(1, 8, 1)
+        v, cores, kind, sample, _ = cpu_oracle_time(40, 2, budget_s=15.0, tokens=T)
         cpu = {"value": round(v, 3), "unit": "tokens/s", "cores": cores, "kind": kind,
                "sample": sample}
     line = {

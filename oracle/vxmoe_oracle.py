@@ -540,7 +540,7 @@ def weighted_combine(expert_outputs, routes, scores):
 def make_q4_bank(rng, experts, out_w, in_w, group_size=GROUP_SIZE) -> Q4Bank:
     """Codes uniform in 0..15 (uniform uint32 words), scale =
     bf16(|N(0,0.02)|/8), bias = -8*scale (exact in bf16)."""
-    w = rng.integers(0, 2**32, size=(experts, out_w, in_w // 8), dtype=np.uint64).astype(np.uint32)
+    w = rng.integers(0, 2**32, size=(experts, out_w, in_w // 8), dtype=np.uint32)
     s = bf16_round(np.abs(rng.normal(0.0, 0.02, size=(experts, out_w, in_w // group_size))) / 8)
     b = (np.float32(-8) * s).astype(np.float32)
     return Q4Bank(w, s, b)
