@@ -191,7 +191,8 @@ def config_dict(args, world):
                      % args.tokens),
         "global_batch": args.tokens * world, "tokens_per_gpu": args.tokens,
         "experts": EXPERTS, "hidden": HIDDEN, "intermediate": INTER, "top_k": TOPK,
-        "parallelism": "replicas" if world > 1 else "single",
+        "parallelism": (f"ep{world}: {EXPERTS // world} experts per GPU, NCCL all-to-all "
+                        f"dispatch/combine" if world > 1 else "single GPU, all experts resident"),
         "l2": f"inputs larger than L2: {args.pools} rotating weight pools of {EXPERTS} experts",
     }
 
@@ -227,18 +228,32 @@ def main():
     T = args.tokens
     K, W = args.steps, max(3, args.warmup)
     g = torch.Generator(device=dev)
-    pools = []
+    gr = torch.Generator(device=dev)
+    pools, layers = [], []
     for i in range(args.pools):
         g.manual_seed(1000 * rank + i)
-        pools.append(vxmoe.MoEWeights.random(EXPERTS, HIDDEN, INTER, SHARED_INTER, TOPK, device=dev,
-                                             generator=g))
+        gr.manual_seed(5000 + i)          # router and shared expert: the same on every rank
+        if world == 1:
+            w = vxmoe.MoEWeights.random(EXPERTS, HIDDEN, INTER, SHARED_INTER, TOPK, device=dev,
+                                        generator=g)
+            pools.append(w)
+            layers.append(lambda x, w=w: vxmoe.moe_block(x, w))
+        else:
+            # expert parallel: this rank holds experts [rank*E/N, (rank+1)*E/N)
+            from vxmoe.ep import ExpertParallelMoE
+            w = vxmoe.MoEWeights.random(EXPERTS // world, HIDDEN, INTER, SHARED_INTER, TOPK,
+                                        device=dev, generator=g, router_experts=EXPERTS,
+                                        router_generator=gr)
+            pools.append(w)
+            layers.append(ExpertParallelMoE(w, EXPERTS))
     g.manual_seed(7 + rank)
     nx = K + W
     xs = (torch.randn((nx, T, HIDDEN), device=dev, generator=g)).to(torch.bfloat16)
     torch.cuda.synchronize()
+    launches_per_step = 8 if world == 1 else 13
 
     def step(i):
-        return vxmoe.moe_block(xs[i], pools[i % len(pools)])
+        return layers[i % len(layers)](xs[i])
 
     def barrier():
         if dist is not None:
@@ -272,24 +287,39 @@ def main():
     dx = torch.empty((T, HIDDEN), dtype=torch.bfloat16, device=dev)
     for i in range(W):
         dx.copy_(hx[i % K], non_blocking=True)
-        hy[i % K].copy_(vxmoe.moe_block(dx, pools[i % len(pools)]), non_blocking=True)
+        hy[i % K].copy_(layers[i % len(layers)](dx), non_blocking=True)
     barrier()
     e0.record(stream)
     for i in range(K):
         dx.copy_(hx[i], non_blocking=True)
-        y = vxmoe.moe_block(dx, pools[(W + i) % len(pools)])
+        y = layers[(W + i) % len(layers)](dx)
         hy[i].copy_(y, non_blocking=True)
     e1.record(stream)
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
     clocks = sampler.stop() if sampler else None
 
-    # routing statistics (outside the timed regions): distinct experts per step
+    # routing statistics (outside the timed regions): distinct experts this
+    # rank's weights serve per step (under expert parallelism, among the
+    # tokens of all ranks routed to its shard)
     Us = []
+    El = EXPERTS // world
     for i in range(K):
-        r = vxmoe.router(xs[W + i], pools[(W + i) % len(pools)])
-        Us.append(int(torch.unique(r.inds).numel()))
+        w = pools[(W + i) % len(pools)]
+        r = vxmoe.route(xs[W + i], w.router_w, TOPK, w.shared_expert_gate)
+        inds = r.inds.reshape(-1)
+        if dist is not None:
+            allr = [torch.empty_like(inds) for _ in range(world)]
+            dist.all_gather(allr, inds)
+            inds = torch.cat(allr)
+            inds = inds[(inds // El) == rank]
+        Us.append(int(torch.unique(inds).numel()))
     U_mean = sum(Us) / len(Us)
+    if dist is not None:
+        t = torch.tensor([U_mean], device=dev, dtype=torch.float64)
+        dist.all_reduce(t)
+        U_mean = float(t.item()) / world
+        Us = [U_mean] * K
 
     # per-kernel durations: the same steps again with stage events
     _lib.profile_enable(True)
@@ -340,7 +370,7 @@ def main():
                 "h2d_bytes_per_step": T * HIDDEN * 2, "d2h_bytes_per_step": T * HIDDEN * 2},
         "cpu_baseline": cpu,
         "clocks": clocks,
-        "gpu_launches": 7 * K,
+        "gpu_launches": launches_per_step * K,
     }
     print(json.dumps(line), flush=True)
 

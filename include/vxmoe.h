@@ -142,6 +142,16 @@ int vx_moe_experts(const uint16_t* x, int32_t T, const int32_t* routes,
                    const uint16_t* shared_gate, uint16_t* out, void* workspace,
                    size_t workspace_bytes, void* stream);
 
+/* Expert-parallel share of the executor: routes [T, k] hold expert ids of
+ * this bank or -1 (slot served elsewhere); out [T, d] float32 receives the
+ * unrounded slot-order sum of bf16(y_s)*score_s over the present slots.  The
+ * rank that owns the tokens adds the partials of all ranks in rank order and
+ * rounds once, as the single-GPU combine does (metal_runtime.py:315-334).
+ * Uses vx_moe_experts_workspace. */
+int vx_moe_experts_partial(const uint16_t* x, int32_t T, const int32_t* routes,
+                           const uint16_t* scores, const vx_moe_weights* W, float* out,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
 /* The whole block, _moe_call at threshold 1.0 (adaptive_topk.py:54-293):
  * router, top-k, renorm, shared expert and its gate, routed experts and the
  * combine.  y [T, d] bf16.  inds/weights (may be NULL) receive the routing. */

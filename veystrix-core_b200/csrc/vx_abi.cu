@@ -336,9 +336,17 @@ static int router_impl(const uint16_t* x, int T, const vx_moe_weights* W, const 
 int vx_router(const uint16_t* x, int32_t T, const vx_moe_weights* W, uint16_t* logits,
               int32_t* inds, uint16_t* weights, uint16_t* sg, void* workspace,
               size_t workspace_bytes, void* stream) {
-  BlockDims dm;
-  int s = check_weights(W, true, &dm);
-  if (s) return s;
+  // The router needs only the gate weights and the shared expert gate (an
+  // expert-parallel rank holds just its shard of the expert banks).
+  if (!W) return VX_EINVAL_SHAPE;
+  BlockDims dm{W->num_experts, W->hidden, W->top_k, 0, 0, false};
+  if (dm.E < 1 || dm.E > 1024 || dm.d <= 0 || dm.d % 32 || dm.k < 1 || dm.k > 16 || dm.k > dm.E)
+    return VX_EINVAL_SHAPE;
+  if (!W->router_w || !aligned16(W->router_w)) return VX_EINVAL_SHAPE;
+  if (W->shared_expert_gate.w) {
+    int s = check_q4(&W->shared_expert_gate, 1, 1, dm.d);
+    if (s) return s;
+  }
   if (T < 0) return VX_EINVAL_SHAPE;
   if (T == 0) return VX_OK;
   if (!x || !inds || !weights || !aligned16(x)) return VX_EINVAL_SHAPE;
@@ -412,6 +420,30 @@ int vx_moe_experts(const uint16_t* x, int32_t T, const int32_t* routes, const ui
   }
   if (e != cudaSuccess) return vx_cuda_fail(e);
   profile_mark(st, scores ? "combine" : "unpermute");
+  return VX_OK;
+}
+
+int vx_moe_experts_partial(const uint16_t* x, int32_t T, const int32_t* routes,
+                           const uint16_t* scores, const vx_moe_weights* W, float* out,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+  BlockDims dm;
+  int s = check_weights(W, false, &dm);
+  if (s) return s;
+  dm.shared = false;
+  dm.Is = 0;
+  if (T < 0) return VX_EINVAL_SHAPE;
+  if (T == 0) return VX_OK;
+  if (!x || !routes || !scores || !out || !aligned16(x)) return VX_EINVAL_SHAPE;
+  if (!workspace || workspace_bytes < vx_moe_experts_workspace(T, W)) return VX_EWORKSPACE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carver c(workspace);
+  ExpertScratch es = carve_experts(c, T, dm);
+  profile_mark(st, "");
+  s = run_experts(x, T, routes, W, dm, es, st);
+  if (s) return s;
+  cudaError_t e = launch_combine_partial(es.yd, dm.d, es.inverse, scores, T, dm.k, dm.d, out, st);
+  if (e != cudaSuccess) return vx_cuda_fail(e);
+  profile_mark(st, "combine_partial");
   return VX_OK;
 }
 

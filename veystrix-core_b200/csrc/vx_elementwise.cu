@@ -113,6 +113,36 @@ cudaError_t launch_xprep(const uint16_t* x, int64_t rows, int K, uint16_t* xb, f
   return cudaGetLastError();
 }
 
+// Float32 partial combine for expert parallelism: the same slot-order
+// float32 sum as combine_kernel, left unrounded and without the shared part
+// (the home rank adds the partials of all ranks, then rounds).
+__global__ void __launch_bounds__(256) combine_partial_kernel(
+    const uint16_t* __restrict__ yd, int64_t ldy, const int32_t* __restrict__ inverse,
+    const uint16_t* __restrict__ weights, int k, int d, float* __restrict__ out) {
+  const int t = blockIdx.y;
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 2;
+  if (c >= d) return;
+  float a0 = 0.f, a1 = 0.f;
+  for (int s = 0; s < k; ++s) {
+    const int pos = inverse[int64_t(t) * k + s];
+    if (pos < 0) continue;
+    const float w = bf16_to_f32(weights[int64_t(t) * k + s]);
+    const uint32_t v = *reinterpret_cast<const uint32_t*>(yd + int64_t(pos) * ldy + c);
+    a0 = __fadd_rn(a0, __fmul_rn(__uint_as_float(v << 16), w));
+    a1 = __fadd_rn(a1, __fmul_rn(__uint_as_float(v & 0xFFFF0000u), w));
+  }
+  *reinterpret_cast<float2*>(out + int64_t(t) * d + c) = make_float2(a0, a1);
+}
+
+cudaError_t launch_combine_partial(const uint16_t* yd, int64_t ldy, const int32_t* inverse,
+                                   const uint16_t* weights, int T, int k, int d, float* out,
+                                   cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  dim3 grid((d / 2 + 255) / 256, T);
+  combine_partial_kernel<<<grid, 256, 0, st>>>(yd, ldy, inverse, weights, k, d, out);
+  return cudaGetLastError();
+}
+
 // out[t, s, :] = yd[inverse[t*k+s], :]  (_scatter_unsort)
 __global__ void unpermute_kernel(const uint16_t* __restrict__ yd, int64_t ldy,
                                  const int32_t* __restrict__ inverse, int k, int d,

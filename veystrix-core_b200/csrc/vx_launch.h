@@ -75,6 +75,9 @@ cudaError_t launch_combine(const uint16_t* yd, int64_t ldy, const int32_t* inver
                            const int32_t* offsets, int E, const uint16_t* sg,
                            const uint16_t* shared_y, const uint16_t* shared,
                            const uint16_t* shared_gate, uint16_t* y, cudaStream_t st);
+cudaError_t launch_combine_partial(const uint16_t* yd, int64_t ldy, const int32_t* inverse,
+                                   const uint16_t* weights, int T, int k, int d, float* out,
+                                   cudaStream_t st);
 cudaError_t launch_unpermute(const uint16_t* yd, int64_t ldy, const int32_t* inverse, int T,
                              int k, int d, uint16_t* out, cudaStream_t st);
 cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* gain, int T, int d, float eps,

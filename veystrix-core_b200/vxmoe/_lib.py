@@ -65,6 +65,8 @@ SIGNATURES = {
     "vx_moe_experts_workspace": (c_size_t, [c_int32, ctypes.POINTER(VxMoEWeights)]),
     "vx_moe_experts": (ctypes.c_int, [P, c_int32, P, P, ctypes.POINTER(VxMoEWeights), P, P, P,
                                       P, P, c_size_t, P]),
+    "vx_moe_experts_partial": (ctypes.c_int, [P, c_int32, P, P, ctypes.POINTER(VxMoEWeights), P,
+                                              P, c_size_t, P]),
     "vx_moe_block_workspace": (c_size_t, [c_int32, ctypes.POINTER(VxMoEWeights)]),
     "vx_moe_block": (ctypes.c_int, [P, c_int32, ctypes.POINTER(VxMoEWeights), P, P, P, P,
                                     c_size_t, P]),

@@ -169,7 +169,8 @@ class MoEWeights:
     ``mlp.gate``, ``mlp.shared_expert.*``, ``mlp.shared_expert_gate``)."""
 
     def __init__(self, gate, up, down, router_w=None, shared_gate=None, shared_up=None,
-                 shared_down=None, shared_expert_gate=None, top_k: int = 10, device=None):
+                 shared_down=None, shared_expert_gate=None, top_k: int = 10, device=None,
+                 check_router: bool = True):
         device = torch.device(device) if device is not None else torch.device("cuda")
         self.gate = Q4Projection.from_any(gate, device)
         self.up = Q4Projection.from_any(up, device)
@@ -190,7 +191,8 @@ class MoEWeights:
             raise ValueError("gate and up projection widths must match")
         if tuple(self.down.weight.shape) != (E, d, I // 8):
             raise ValueError(f"down weight shape {tuple(self.down.weight.shape)} != {(E, d, I // 8)}")
-        if self.router_w is not None and tuple(self.router_w.shape) != (E, d):
+        # An expert-parallel shard keeps the full router: check_router=False.
+        if check_router and self.router_w is not None and tuple(self.router_w.shape) != (E, d):
             raise ValueError(f"router weight shape {tuple(self.router_w.shape)} != {(E, d)}")
         self._struct = None
 
@@ -232,12 +234,17 @@ class MoEWeights:
 
     @staticmethod
     def random(num_experts=512, hidden=2048, inter=512, shared_inter=512, top_k=10,
-               device=None, generator=None, hot_experts=None) -> "MoEWeights":
+               device=None, generator=None, router_experts=None,
+               router_generator=None) -> "MoEWeights":
         """Synthetic weights with the benchmark distributions: codes uniform
         in 0..15, scale = bf16(|N(0, 0.02)|/8), bias = -8*scale, router
-        bf16 N(0, 0.02)."""
+        bf16 N(0, 0.02).  An expert-parallel shard passes the full expert
+        count as `router_experts` and a generator shared by all ranks as
+        `router_generator` (router and shared expert are replicated)."""
         device = torch.device(device) if device is not None else torch.device("cuda")
         g = generator
+        gr = router_generator if router_generator is not None else generator
+        n_router = router_experts if router_experts is not None else num_experts
 
         def bank(E, out, inn):
             w = torch.randint(-2**31, 2**31 - 1, (E, out, inn // 8), dtype=torch.int32,
@@ -250,11 +257,13 @@ class MoEWeights:
         gate = bank(num_experts, inter, hidden)
         up = bank(num_experts, inter, hidden)
         down = bank(num_experts, hidden, inter)
-        router = (torch.randn((num_experts, hidden), device=device, generator=g) * 0.02).to(torch.bfloat16)
+        g = gr
+        router = (torch.randn((n_router, hidden), device=device, generator=g) * 0.02).to(torch.bfloat16)
         sh = [bank(1, shared_inter, hidden), bank(1, shared_inter, hidden), bank(1, hidden, shared_inter)] \
             if shared_inter else [None, None, None]
         seg = bank(1, 1, hidden) if shared_inter else None
-        return MoEWeights(gate, up, down, router, *sh, seg, top_k=top_k, device=device)
+        return MoEWeights(gate, up, down, router, *sh, seg, top_k=top_k, device=device,
+                          check_router=n_router == num_experts)
 
 
 # --------------------------------------------------------------------------
@@ -393,17 +402,29 @@ class RouterOut:
 def router(x: torch.Tensor, weights: MoEWeights) -> RouterOut:
     """Router of the block: bf16 logits, top-k, renormalised weights and the
     shared expert's sigmoid gate."""
+    return route(x, weights.router_w, weights.top_k, weights.shared_expert_gate)
+
+
+def route(x: torch.Tensor, router_w: torch.Tensor, top_k: int,
+          shared_expert_gate: Optional[Q4Projection] = None) -> RouterOut:
+    """The router from its own tensors: bf16 gate [E, d] and, optionally,
+    the Q4 shared-expert gate [1, 1, d/8] (no expert bank needed)."""
     x = _bf16(x, "x")
-    d = weights.hidden
+    router_w = _bf16(router_w, "router_w")
+    E, d = int(router_w.shape[0]), int(router_w.shape[1])
     x2 = x.reshape(-1, d)
     T = int(x2.shape[0])
     dev = x.device
-    E, k = weights.num_experts, weights.top_k
+    k = int(top_k)
     logits = torch.empty((T, E), dtype=torch.bfloat16, device=dev)
     inds = torch.empty((T, k), dtype=torch.int32, device=dev)
     w = torch.empty((T, k), dtype=torch.bfloat16, device=dev)
-    sg = torch.empty((T,), dtype=torch.bfloat16, device=dev) if weights.shared_expert_gate is not None else None
-    st = weights.vx()
+    sg = torch.empty((T,), dtype=torch.bfloat16, device=dev) if shared_expert_gate is not None else None
+    st = VxMoEWeights()
+    st.router_w = router_w.data_ptr()
+    if shared_expert_gate is not None:
+        st.shared_expert_gate = shared_expert_gate.vx()
+    st.num_experts, st.hidden, st.top_k = E, d, k
     _lib.check(_lib.load().vx_router(x2.data_ptr(), T, ctypes.byref(st), logits.data_ptr(),
                                       inds.data_ptr(), w.data_ptr(), _ptr(sg), None, 0,
                                       _stream(dev)), "router")
@@ -467,6 +488,32 @@ def moe_experts(x: torch.Tensor, routes, weights: MoEWeights, scores=None, share
     _lib.check(lib.vx_moe_experts(x2.data_ptr(), T, r.data_ptr(), _ptr(sc), ctypes.byref(st),
                                   _ptr(sy), _ptr(sh), _ptr(shg), out.data_ptr(), ws.data_ptr(),
                                   ws.numel(), _stream(dev)), "moe_experts")
+    return out
+
+
+def moe_experts_partial(x: torch.Tensor, routes: torch.Tensor, scores: torch.Tensor,
+                        weights: MoEWeights) -> torch.Tensor:
+    """Expert-parallel share: float32 [T, d] unrounded slot-order sum of
+    bf16(y_s)*score_s over the slots whose route is an expert of this bank
+    (routes -1 elsewhere)."""
+    x = _bf16(x, "x")
+    d = weights.hidden
+    x2 = x.reshape(-1, d)
+    T = int(x2.shape[0])
+    dev = x.device
+    r = _i32(routes, dev, "routes").reshape(T, -1)
+    k = int(r.shape[1])
+    sc = _bf16(scores, "scores").reshape(T, k)
+    st = weights.vx(with_shared=False)
+    st.top_k = k
+    lib = _lib.load()
+    out = torch.empty((T, d), dtype=torch.float32, device=dev)
+    if T == 0:
+        return out
+    ws = _WS.get(lib.vx_moe_experts_workspace(T, ctypes.byref(st)), dev)
+    _lib.check(lib.vx_moe_experts_partial(x2.data_ptr(), T, r.data_ptr(), sc.data_ptr(),
+                                          ctypes.byref(st), out.data_ptr(), ws.data_ptr(),
+                                          ws.numel(), _stream(dev)), "moe_experts_partial")
     return out
 
 
