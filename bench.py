@@ -48,6 +48,8 @@ def parse():
     ap.add_argument("--tokens", type=int, default=64)
     ap.add_argument("--pools", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layout", default="tiled", choices=("tiled", "mlx"),
+                    help="expert weights as the tiled resident pool (default) or the MLX arrays")
     return ap.parse_args()
 
 
@@ -194,6 +196,8 @@ def config_dict(args, world):
         "parallelism": (f"ep{world}: {EXPERTS // world} experts per GPU, NCCL all-to-all "
                         f"dispatch/combine" if world > 1 else "single GPU, all experts resident"),
         "l2": f"inputs larger than L2: {args.pools} rotating weight pools of {EXPERTS} experts",
+        "weight_layout": ("tiled resident pool (packed once at load)" if args.layout == "tiled"
+                          else "MLX arrays"),
     }
 
 
@@ -236,6 +240,8 @@ def main():
         if world == 1:
             w = vxmoe.MoEWeights.random(EXPERTS, HIDDEN, INTER, SHARED_INTER, TOPK, device=dev,
                                         generator=g)
+            if args.layout == "tiled":
+                w.pack()
             pools.append(w)
             layers.append(lambda x, w=w: vxmoe.moe_block(x, w))
         else:
@@ -244,6 +250,8 @@ def main():
             w = vxmoe.MoEWeights.random(EXPERTS // world, HIDDEN, INTER, SHARED_INTER, TOPK,
                                         device=dev, generator=g, router_experts=EXPERTS,
                                         router_generator=gr)
+            if args.layout == "tiled":
+                w.pack()
             pools.append(w)
             layers.append(ExpertParallelMoE(w, EXPERTS))
     g.manual_seed(7 + rank)

@@ -52,9 +52,38 @@ typedef struct vx_q4 {
   int32_t group_size;
 } vx_q4;
 
+/* A bank re-tiled into the resident expert pool (vx_q4_tile): the B200
+ * counterpart of the reference's fixed-stride expert records
+ * (slab_pack.py:1-25, expert_pool.py:1-22).  Expert e's records start at
+ * e * vx_q4_tiles_bytes(1, out, in, nproj, tile_rows); inside, one record of
+ * nproj * (tile_rows/16) * 1280 bytes per (row tile, 128-input chunk) holds
+ * the packed words and the bf16 scales/biases in the order the decode GEMV
+ * reads them.  nproj 2 interleaves a gate/up pair. */
+typedef struct vx_q4_tiles {
+  const void* records;
+  int32_t experts;
+  int32_t out;
+  int32_t in;
+  int32_t group_size;
+  int32_t nproj;              /* 2: gate and up interleaved; 1: one projection */
+  int32_t tile_rows;          /* 16 (gate/up) or 16/32 (single projection) */
+} vx_q4_tiles;
+
+/* The tiled pool of one block.  gate_up: routed gate+up (nproj 2, tile_rows
+ * 16); down: routed down (nproj 1, tile_rows 32 or 16); shared_*: the shared
+ * expert (records NULL when the block has none). */
+typedef struct vx_moe_pool {
+  vx_q4_tiles gate_up;
+  vx_q4_tiles down;
+  vx_q4_tiles shared_gate_up;
+  vx_q4_tiles shared_down;
+} vx_moe_pool;
+
 /* Weights of one MoE block (adaptive_topk.py:54-293).  shared_* banks have
  * experts == 1; shared_gate.w == NULL means "no shared expert".  router_w is
- * the unquantised bf16 gate [num_experts, hidden] (preflight.py:70). */
+ * the unquantised bf16 gate [num_experts, hidden] (preflight.py:70).  pool,
+ * when not NULL, is the same experts re-tiled by vx_q4_tile: the routed and
+ * shared passes then stream the pool (the MLX banks still give the shapes). */
 typedef struct vx_moe_weights {
   vx_q4 gate;                 /* [E, I, d/8]  switch_mlp.gate_proj */
   vx_q4 up;                   /* [E, I, d/8]  switch_mlp.up_proj   */
@@ -67,6 +96,7 @@ typedef struct vx_moe_weights {
   int32_t num_experts;
   int32_t hidden;
   int32_t top_k;
+  const vx_moe_pool* pool;    /* may be NULL */
 } vx_moe_weights;
 
 /* Library identification and error text. */
@@ -80,6 +110,19 @@ const char* vx_last_cuda_error(void);
 /* Dequantise one expert of a bank to float32 [out, in]: scale*q + bias.
  * Replaces mx.dequantize(..., mode="affine") (metal_runtime.py:770-777). */
 int vx_q4_dequant(const vx_q4* bank, int32_t expert, float* out, void* stream);
+
+/* Size in bytes of a tiled pool for `experts` experts of an [out, in] bank
+ * (nproj 1 or 2, tile_rows 16 or 32); 0 for an invalid shape. */
+size_t vx_q4_tiles_bytes(int32_t experts, int32_t out, int32_t in, int32_t nproj,
+                         int32_t tile_rows);
+/* Re-tile bank a (and b, the up half of a gate/up pair, when nproj == 2;
+ * same shape as a) into records (device, 16-byte aligned, records_bytes >=
+ * vx_q4_tiles_bytes).  Out-of-range rows and groups are zero-filled.  A
+ * one-time load step, the role of the reference's slab packing
+ * (slab_pack.py:1-25); the decode passes then read each expert's records
+ * with one bulk copy per chunk. */
+int vx_q4_tile(const vx_q4* a, const vx_q4* b, int32_t nproj, int32_t tile_rows,
+               void* records, size_t records_bytes, void* stream);
 
 /* h = silu(g) * u over n bf16 values with MLX's bf16 rounding sequence
  * (metal_runtime.py:267-285; swiglu_contract.py:144-147). */

@@ -63,7 +63,29 @@ static int check_q4(const vx_q4* b, int experts, int out, int in) {
 struct BlockDims {
   int E, d, k, I, Is;
   bool shared;
+  const vx_moe_pool* pool = nullptr;
 };
+
+static int check_tiles(const vx_q4_tiles& t, int experts, int out, int in, int nproj) {
+  if (!t.records || !aligned16(t.records)) return VX_EINVAL_SHAPE;
+  if (t.experts != experts || t.out != out || t.in != in || t.nproj != nproj) return VX_EINVAL_SHAPE;
+  if (t.group_size != 32) return VX_EUNSUPPORTED;
+  if (t.tile_rows != 16 && !(nproj == 1 && t.tile_rows == 32)) return VX_EINVAL_SHAPE;
+  return VX_OK;
+}
+
+static int check_pool(const vx_moe_pool* p, int E, int d, int I, int Is, bool shared) {
+  int s;
+  if ((s = check_tiles(p->gate_up, E, I, d, 2))) return s;
+  if ((s = check_tiles(p->down, E, d, I, 1))) return s;
+  if (shared) {
+    if ((s = check_tiles(p->shared_gate_up, 1, Is, d, 2))) return s;
+    if ((s = check_tiles(p->shared_down, 1, d, Is, 1))) return s;
+    // one launch serves routed and shared rows: the same row tiling
+    if (p->shared_down.tile_rows != p->down.tile_rows) return VX_EINVAL_SHAPE;
+  }
+  return VX_OK;
+}
 
 static int check_weights(const vx_moe_weights* W, bool need_router, BlockDims* dm) {
   if (!W) return VX_EINVAL_SHAPE;
@@ -86,7 +108,8 @@ static int check_weights(const vx_moe_weights* W, bool need_router, BlockDims* d
     if (Is % 32) return VX_EINVAL_SHAPE;
     if (need_router && (s = check_q4(&W->shared_expert_gate, 1, 1, d))) return s;
   }
-  *dm = {E, d, k, I, Is, shared};
+  if (W->pool && (s = check_pool(W->pool, E, d, I, Is, shared))) return s;
+  *dm = {E, d, k, I, Is, shared, W->pool};
   return VX_OK;
 }
 
@@ -135,6 +158,51 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
   e = launch_xprep(x, T, dm.d, s.xb, s.xs, s.ldxs, st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
   profile_mark(st, "permute");
+
+  if (dm.pool) {
+    const vx_moe_pool& pl = *dm.pool;
+    TiledArgs a{};
+    a.err = s.err + 1;
+    a.rec_b = static_cast<const unsigned char*>(pl.gate_up.records);
+    a.stride_b = tile_pool_bytes(1, dm.I, dm.d, 2, pl.gate_up.tile_rows);
+    a.rec_s = dm.shared ? static_cast<const unsigned char*>(pl.shared_gate_up.records) : nullptr;
+    a.N_b = dm.I;
+    a.N_s = dm.Is;
+    a.K_b = a.K_s = dm.d;
+    a.E = dm.E;
+    a.items = s.items;
+    a.n_items = s.n_items;
+    a.src_rows = s.src_rows;
+    a.x = s.xb;
+    a.ldx = dm.d;
+    a.xsum = s.xs;
+    a.ldxs = s.ldxs;
+    a.out = s.h;
+    a.ldo = s.ldh;
+    e = launch_gemv_tiled(true, pl.gate_up.tile_rows, a, s.max_items, int(s.ldh), st);
+    if (e != cudaSuccess) return vx_cuda_fail(e);
+    profile_mark(st, "gate_up_swiglu");
+
+    TiledArgs b{};
+    b.err = s.err + 1;
+    b.rec_b = static_cast<const unsigned char*>(pl.down.records);
+    b.stride_b = tile_pool_bytes(1, dm.d, dm.I, 1, pl.down.tile_rows);
+    b.rec_s = dm.shared ? static_cast<const unsigned char*>(pl.shared_down.records) : nullptr;
+    b.N_b = b.N_s = dm.d;
+    b.K_b = dm.I;
+    b.K_s = dm.Is;
+    b.E = dm.E;
+    b.items = s.items;
+    b.n_items = s.n_items;
+    b.x = s.h;
+    b.ldx = s.ldh;
+    b.out = s.yd;
+    b.ldo = dm.d;
+    e = launch_gemv_tiled(false, pl.down.tile_rows, b, s.max_items, dm.d, st);
+    if (e != cudaSuccess) return vx_cuda_fail(e);
+    profile_mark(st, "down");
+    return VX_OK;
+  }
 
   MmaArgs a{};
   a.b0 = W->gate;
@@ -205,6 +273,31 @@ const char* vx_strerror(int status) {
 }
 
 const char* vx_last_cuda_error(void) { return g_cuda_err; }
+
+size_t vx_q4_tiles_bytes(int32_t experts, int32_t out, int32_t in, int32_t nproj,
+                         int32_t tile_rows) {
+  if (experts < 1 || out < 1 || in < 32 || in % 32 || (nproj != 1 && nproj != 2)) return 0;
+  if (tile_rows != 16 && !(nproj == 1 && tile_rows == 32)) return 0;
+  return size_t(tile_pool_bytes(experts, out, in, nproj, tile_rows));
+}
+
+int vx_q4_tile(const vx_q4* a, const vx_q4* b, int32_t nproj, int32_t tile_rows, void* records,
+               size_t records_bytes, void* stream) {
+  if (!a) return VX_EINVAL_SHAPE;
+  int s = check_q4(a, -1, a->out, a->in);
+  if (s) return s;
+  if (nproj == 2) {
+    if (!b) return VX_EINVAL_SHAPE;
+    if ((s = check_q4(b, a->experts, a->out, a->in))) return s;
+  }
+  const size_t need = vx_q4_tiles_bytes(a->experts, a->out, a->in, nproj, tile_rows);
+  if (need == 0) return VX_EINVAL_SHAPE;
+  if (!records || !aligned16(records)) return VX_EINVAL_SHAPE;
+  if (records_bytes < need) return VX_EWORKSPACE;
+  cudaError_t e = launch_tile_pack(*a, nproj == 2 ? *b : *a, nproj, tile_rows, records,
+                                   static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? VX_OK : vx_cuda_fail(e);
+}
 
 int vx_q4_dequant(const vx_q4* bank, int32_t expert, float* out, void* stream) {
   if (!bank || !out || !bank->w || !bank->scales || !bank->biases) return VX_EINVAL_SHAPE;

@@ -29,6 +29,7 @@
 // (down, whose input h this kernel writes itself).
 #include <cudaTypedefs.h>
 
+#include "vx_async.cuh"
 #include "vx_common.cuh"
 #include "vx_launch.h"
 
@@ -37,80 +38,6 @@ namespace vx {
 constexpr int kMmaThreads = 256;
 constexpr int kWarps = kMmaThreads / 32;
 constexpr int kStages = 3;
-constexpr uint32_t kSpinLimit = 1u << 24;   // bounded mbarrier waits
-
-VX_DEVICE uint32_t nib_pair128(uint32_t w_shifted) {
-  // {128 + (w & 15), 128 + ((w >> 16) & 15)} as bf16x2 (exact).
-  uint32_t r;
-  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(w_shifted), "r"(0x000F000Fu), "r"(0x43004300u));
-  return r;
-}
-
-VX_DEVICE uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-// Async copies.  src_bytes = 0 writes zeros without reading; the _if form
-// issues nothing when the predicate is false.
-VX_DEVICE void cp16_if(uint32_t dst, const void* src, int src_bytes, bool pred) {
-  asm volatile(
-      "{ .reg .pred p; setp.ne.b32 p, %3, 0; @p cp.async.cg.shared.global [%0], [%1], 16, %2; }" ::"r"(dst),
-      "l"(src), "r"(src_bytes), "r"(int(pred))
-      : "memory");
-}
-VX_DEVICE void cp4(uint32_t dst, const void* src, bool valid) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(valid ? 4 : 0)
-               : "memory");
-}
-VX_DEVICE void cp8(uint32_t dst, const void* src, bool valid) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst), "l"(src), "r"(valid ? 8 : 0)
-               : "memory");
-}
-VX_DEVICE void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-VX_DEVICE void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
-VX_DEVICE uint4 lds128(uint32_t addr) {
-  uint4 v;
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
-  return v;
-}
-VX_DEVICE uint2 lds64(uint32_t addr) {
-  uint2 v;
-  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
-  return v;
-}
-
-// mbarrier helpers (one barrier per warp per stage, count 1: the issuing lane).
-VX_DEVICE void mbar_init(uint32_t bar) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
-}
-VX_DEVICE void mbar_expect(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-VX_DEVICE bool mbar_try(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Waits with an iteration limit; on expiry the caller records an error.
-VX_DEVICE bool mbar_wait(uint32_t bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i)
-    if (mbar_try(bar, parity)) return true;
-  return false;
-}
-VX_DEVICE void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
-      "[%4];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
-      : "memory");
-}
-
 // One pipeline stage of one warp, bytes (multiples of 128).
 template <int NP, int MT, bool XMMA>
 struct Stage {

@@ -43,6 +43,37 @@ inline int64_t xsum_stride(int K) { return ((K / 32) + 1) & ~1; }
 cudaError_t launch_gemv_mma(bool gateup, const MmaArgs& a, int max_items, int max_out,
                             cudaStream_t st);
 
+// Tiled expert pool: bytes of one record per (projection, 16-row m-tile) and
+// 128-input chunk: 1024 of packed words + 256 of scales and biases.
+constexpr int kTileRecordUnit = 1280;
+
+struct TiledArgs {
+  int32_t* err;                 // bit 8 set when a pipeline wait ran out (may be null)
+  const unsigned char* rec_b;   // routed experts' records
+  int64_t stride_b;             // bytes per routed expert
+  const unsigned char* rec_s;   // shared expert's records (expert id E), may be null
+  int N_b, N_s;                 // output rows of the routed / shared projection
+  int K_b, K_s;                 // inputs of the routed / shared projection
+  int E;
+  const int32_t* items;         // [n][3] expert, first position, count
+  const int32_t* n_items;
+  const int32_t* src_rows;
+  const int32_t* dst_rows;
+  const uint16_t* x;            // activations in B order
+  int64_t ldx;
+  const float* xsum;            // null: sum(x) on the tensor pipe
+  int64_t ldxs;
+  uint16_t* out;
+  int64_t ldo;
+  int tiles_per_item;           // set by the launcher
+};
+
+int64_t tile_pool_bytes(int64_t experts, int out, int in, int nproj, int tile_rows);
+cudaError_t launch_tile_pack(const vx_q4& a, const vx_q4& b, int nproj, int tile_rows, void* out,
+                             cudaStream_t st);
+cudaError_t launch_gemv_tiled(bool gateup, int tile_rows, const TiledArgs& a, int max_items,
+                              int max_out, cudaStream_t st);
+
 // Upper bound of the number of work items for P routed positions over E
 // experts plus Ts shared-expert positions.
 inline int max_items_bound(int64_t P, int E, int Ts) {

@@ -35,6 +35,20 @@ class VxQ4(ctypes.Structure):
     ]
 
 
+class VxQ4Tiles(ctypes.Structure):
+    _fields_ = [
+        ("records", c_void_p), ("experts", c_int32), ("out", c_int32), ("in_", c_int32),
+        ("group_size", c_int32), ("nproj", c_int32), ("tile_rows", c_int32),
+    ]
+
+
+class VxMoEPool(ctypes.Structure):
+    _fields_ = [
+        ("gate_up", VxQ4Tiles), ("down", VxQ4Tiles),
+        ("shared_gate_up", VxQ4Tiles), ("shared_down", VxQ4Tiles),
+    ]
+
+
 class VxMoEWeights(ctypes.Structure):
     _fields_ = [
         ("gate", VxQ4), ("up", VxQ4), ("down", VxQ4),
@@ -42,6 +56,7 @@ class VxMoEWeights(ctypes.Structure):
         ("shared_expert_gate", VxQ4),
         ("router_w", c_void_p),
         ("num_experts", c_int32), ("hidden", c_int32), ("top_k", c_int32),
+        ("pool", ctypes.POINTER(VxMoEPool)),
     ]
 
 
@@ -51,6 +66,9 @@ SIGNATURES = {
     "vx_version": (ctypes.c_char_p, []),
     "vx_strerror": (ctypes.c_char_p, [ctypes.c_int]),
     "vx_last_cuda_error": (ctypes.c_char_p, []),
+    "vx_q4_tiles_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32, c_int32]),
+    "vx_q4_tile": (ctypes.c_int, [ctypes.POINTER(VxQ4), ctypes.POINTER(VxQ4), c_int32, c_int32,
+                                  P, c_size_t, P]),
     "vx_q4_dequant": (ctypes.c_int, [ctypes.POINTER(VxQ4), c_int32, P, P]),
     "vx_swiglu_bf16": (ctypes.c_int, [P, P, P, c_int64, P]),
     "vx_gather_qmm_workspace": (c_size_t, [c_int64, c_int32, c_int32, c_int64, c_int32]),

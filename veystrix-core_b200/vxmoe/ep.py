@@ -39,6 +39,8 @@ class CudaBackend:
         if shard.shared_gate is not None:
             self.shared_w = ops.MoEWeights(shard.shared_gate, shard.shared_up, shard.shared_down,
                                            top_k=1, device=shard.device)
+            if shard.pool is not None:
+                self.shared_w.pack(shard.pool.down_rows)
 
     def route(self, x, num_experts):
         r = ops.route(x, self.router_w, self.w.top_k, self.seg)

@@ -194,7 +194,15 @@ class MoEWeights:
         # An expert-parallel shard keeps the full router: check_router=False.
         if check_router and self.router_w is not None and tuple(self.router_w.shape) != (E, d):
             raise ValueError(f"router weight shape {tuple(self.router_w.shape)} != {(E, d)}")
-        self._struct = None
+        self.pool: Optional[TiledPool] = None
+
+    def pack(self, down_rows: int = 32) -> "MoEWeights":
+        """Re-tile the experts into the resident pool the decode kernels
+        stream (one bulk copy per chunk); every later call on these weights
+        reads the pool.  A load-time step (the role of the reference's slab
+        packing, ``slab_pack.py:1-25``).  Returns self."""
+        self.pool = TiledPool(self, down_rows)
+        return self
 
     @property
     def num_experts(self) -> int:
@@ -225,6 +233,8 @@ class MoEWeights:
             s.shared_expert_gate = self.shared_expert_gate.vx()
         s.router_w = _ptr(self.router_w)
         s.num_experts, s.hidden, s.top_k = self.num_experts, self.hidden, self.top_k
+        if self.pool is not None:
+            s.pool = ctypes.pointer(self.pool.vx())
         return s
 
     def nbytes_per_expert(self) -> int:
@@ -264,6 +274,59 @@ class MoEWeights:
         seg = bank(1, 1, hidden) if shared_inter else None
         return MoEWeights(gate, up, down, router, *sh, seg, top_k=top_k, device=device,
                           check_router=n_router == num_experts)
+
+
+def tile_bank(a: Q4Projection, b: Optional[Q4Projection] = None, tile_rows: int = 16) -> torch.Tensor:
+    """Records of bank `a` (with `b` interleaved as the up half of a gate/up
+    pair) in the tiled pool layout, uint8 on a's device."""
+    nproj = 1 if b is None else 2
+    lib = _lib.load()
+    n = lib.vx_q4_tiles_bytes(a.experts, a.out_features, a.in_features, nproj, tile_rows)
+    if n == 0:
+        raise ValueError(f"no tiled layout for {a.out_features}x{a.in_features}, "
+                         f"nproj {nproj}, tile_rows {tile_rows}")
+    rec = torch.empty(n, dtype=torch.uint8, device=a.weight.device)
+    qa = a.vx()
+    qb = b.vx() if b is not None else None
+    _lib.check(lib.vx_q4_tile(ctypes.byref(qa), ctypes.byref(qb) if qb is not None else None, nproj,
+                              tile_rows, rec.data_ptr(), n, _stream(rec.device)), "tile_bank")
+    return rec
+
+
+class TiledPool:
+    """The block's experts re-tiled for the decode GEMV: routed gate/up
+    interleaved in 16-row tiles, routed down in `down_rows`-row tiles, and the
+    shared expert likewise.  Expert e's records sit at e * stride, the
+    counterpart of the reference's fixed-stride slab records
+    (``slab_pack.py:1-25``, ``expert_pool.py:1-22``)."""
+
+    def __init__(self, w: "MoEWeights", down_rows: int = 32):
+        if down_rows not in (16, 32):
+            raise ValueError("down_rows must be 16 or 32")
+        self.down_rows = down_rows
+        self.gate_up = tile_bank(w.gate, w.up, 16)
+        self.down = tile_bank(w.down, None, down_rows)
+        self.shapes = {"gate_up": (w.num_experts, w.intermediate, w.hidden, 2, 16),
+                       "down": (w.num_experts, w.hidden, w.intermediate, 1, down_rows)}
+        self.shared_gate_up = self.shared_down = None
+        if w.shared_gate is not None:
+            Is = w.shared_gate.out_features
+            self.shared_gate_up = tile_bank(w.shared_gate, w.shared_up, 16)
+            self.shared_down = tile_bank(w.shared_down, None, down_rows)
+            self.shapes["shared_gate_up"] = (1, Is, w.hidden, 2, 16)
+            self.shapes["shared_down"] = (1, w.hidden, Is, 1, down_rows)
+        self._struct = _lib.VxMoEPool()
+        for name, (E, out, inn, nproj, rows) in self.shapes.items():
+            t = getattr(self._struct, name)
+            t.records = getattr(self, name).data_ptr()
+            t.experts, t.out, t.in_, t.group_size, t.nproj, t.tile_rows = E, out, inn, GROUP_SIZE, nproj, rows
+            setattr(self._struct, name, t)
+
+    def vx(self) -> "_lib.VxMoEPool":
+        return self._struct
+
+    def nbytes(self) -> int:
+        return sum(int(getattr(self, n).numel()) for n in self.shapes)
 
 
 # --------------------------------------------------------------------------
