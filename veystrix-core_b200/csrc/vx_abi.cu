@@ -117,8 +117,9 @@ static int check_weights(const vx_moe_weights* W, bool need_router, BlockDims* d
 // the shared expert's T items).
 struct ExpertScratch {
   int32_t *order, *inverse, *offsets, *active, *n_active, *src_rows, *err, *items, *n_items;
-  uint16_t *h, *yd, *xb;     // xb: x in B order
-  float* xs;                 // per-group sum(x) of the T input rows
+  uint16_t *h, *yd, *xb;     // xb: x in B order (MLX-layout path)
+  float* xs;                 // per-group sum(x) of the T input rows (MLX-layout path)
+  unsigned char *act, *hrec; // activation records of x and of h (tiled-pool path)
   int64_t ldh, ldxs;
   int max_items;
 };
@@ -137,11 +138,19 @@ static ExpertScratch carve_experts(Carver& c, int T, const BlockDims& dm) {
   s.items = c.take<int32_t>(3 * int64_t(s.max_items));
   s.n_items = c.take<int32_t>(1);
   s.ldh = std::max(dm.I, dm.Is);
-  s.h = c.take<uint16_t>((P + Ts) * s.ldh);
   s.yd = c.take<uint16_t>((P + Ts) * dm.d);
-  s.xb = c.take<uint16_t>(int64_t(T) * dm.d);
   s.ldxs = xsum_stride(dm.d);
-  s.xs = c.take<float>(int64_t(T) * s.ldxs);
+  s.h = s.xb = nullptr;
+  s.xs = nullptr;
+  s.act = s.hrec = nullptr;
+  if (dm.pool) {
+    s.act = c.take<unsigned char>(act_record_bytes(dm.d, P + Ts));
+    s.hrec = c.take<unsigned char>(act_record_bytes(int(s.ldh), P + Ts));
+  } else {
+    s.h = c.take<uint16_t>((P + Ts) * s.ldh);
+    s.xb = c.take<uint16_t>(int64_t(T) * dm.d);
+    s.xs = c.take<float>(int64_t(T) * s.ldxs);
+  }
   return s;
 }
 
@@ -153,9 +162,17 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
   cudaError_t e = cudaMemsetAsync(s.err, 0, 2 * sizeof(int32_t), st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
   e = launch_permute(routes, P, dm.E, Ts, dm.k, nullptr, s.order, s.inverse, s.offsets, s.active,
-                     s.n_active, s.src_rows, s.err, kItemChunk, s.items, s.n_items, st);
+                     s.n_active, s.src_rows, s.err, dm.pool ? kTiledItemChunk : kItemChunk, s.items,
+                     s.n_items, st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
-  e = launch_xprep(x, T, dm.d, s.xb, s.xs, s.ldxs, st);
+  if (dm.pool) {
+    // activation records of the sorted positions (valid count: offsets[E+1])
+    e = launch_act_records(x, dm.d, dm.d, s.src_rows, s.offsets + dm.E + 1, P + Ts, s.act, st);
+    if (e == cudaSuccess && (dm.I % 128 || dm.Is % 128))   // zero chunk padding of h
+      e = cudaMemsetAsync(s.hrec, 0, size_t(act_record_bytes(int(s.ldh), P + Ts)), st);
+  } else {
+    e = launch_xprep(x, T, dm.d, s.xb, s.xs, s.ldxs, st);
+  }
   if (e != cudaSuccess) return vx_cuda_fail(e);
   profile_mark(st, "permute");
 
@@ -172,13 +189,9 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
     a.E = dm.E;
     a.items = s.items;
     a.n_items = s.n_items;
-    a.src_rows = s.src_rows;
-    a.x = s.xb;
-    a.ldx = dm.d;
-    a.xsum = s.xs;
-    a.ldxs = s.ldxs;
-    a.out = s.h;
-    a.ldo = s.ldh;
+    a.act = s.act;
+    a.act_rows = P + Ts;
+    a.hrec = s.hrec;
     e = launch_gemv_tiled(true, pl.gate_up.tile_rows, a, s.max_items, int(s.ldh), st);
     if (e != cudaSuccess) return vx_cuda_fail(e);
     profile_mark(st, "gate_up_swiglu");
@@ -194,8 +207,8 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
     b.E = dm.E;
     b.items = s.items;
     b.n_items = s.n_items;
-    b.x = s.h;
-    b.ldx = s.ldh;
+    b.act = s.hrec;
+    b.act_rows = P + Ts;
     b.out = s.yd;
     b.ldo = dm.d;
     e = launch_gemv_tiled(false, pl.down.tile_rows, b, s.max_items, dm.d, st);
@@ -476,7 +489,7 @@ int vx_permute(const int32_t* ids, int64_t P, int32_t E, int32_t* order, int32_t
 
 size_t vx_moe_experts_workspace(int32_t T, const vx_moe_weights* W) {
   if (!W || T < 0) return 0;
-  BlockDims dm{W->num_experts, W->hidden, W->top_k, W->gate.out, 0, false};
+  BlockDims dm{W->num_experts, W->hidden, W->top_k, W->gate.out, 0, false, W->pool};
   Carver c(nullptr);
   carve_experts(c, T, dm);
   return c.size();
@@ -544,7 +557,7 @@ size_t vx_moe_block_workspace(int32_t T, const vx_moe_weights* W) {
   if (!W || T < 0) return 0;
   const bool shared = W->shared_gate.w != nullptr;
   BlockDims dm{W->num_experts, W->hidden, W->top_k, W->gate.out, shared ? W->shared_gate.out : 0,
-               shared};
+               shared, W->pool};
   Carver c(nullptr);
   c.take<uint16_t>(int64_t(T) * dm.E);   // logits
   c.take<int32_t>(int64_t(T) * dm.k);    // inds

@@ -2,9 +2,12 @@
 //
 // Same arithmetic as the MLX-layout kernel (vx_gemv_mma.cu: mma.sync
 // m16n8k16 with the block-diagonal B, nibbles unpacked to 128+q by one lop3,
-// MLX's qmv formula per group folded into the epilogue), but the weights come
-// from a pool re-tiled once at load time into the order the warp consumes
-// them.  One record = one warp's 128-input chunk of one row tile:
+// MLX's qmv formula per group folded into the epilogue), but every operand
+// arrives by bulk copy from records laid out in the order the warp consumes
+// them.
+//
+// Weight records (the pool, re-tiled once at load time).  One record = one
+// warp's 128-input chunk of one row tile:
 //
 //   [p][m][h][lane] 16 B   packed words: lane (g = lane/4, c = lane%4) gets
 //                          row 16m + g + 8h of the tile, words 4c..4c+3
@@ -13,19 +16,24 @@
 //
 // (p: projection - gate and up interleaved for the gate/up pass; m: 16-row
 // m-tile).  1280 bytes per (p, m): 1024 of weights, 256 of scales and biases,
-// the same bytes as the MLX layout.  A warp streams a row tile's records,
-// which are contiguous, with ONE bulk copy per chunk (issued by lane 0,
-// completed on the stage's mbarrier) instead of a TMA box plus eight small
-// scale copies per lane.  The pipeline runs across the warp's tasks: the
-// copies of the next task start while the current one is still being
-// consumed, so short reductions (the down projection has 4 chunks) do not
-// pay the pipeline fill per task.
+// the same bytes as the MLX layout.  Expert e's records start at e * stride,
+// the counterpart of the reference's fixed-stride expert records
+// (models/flashnext/slab_pack.py:1-25, expert_pool.py:1-22).
 //
-// Records out of range (rows >= out, groups >= in/32) hold zero words, scales
-// and biases, so they add exactly zero; no bounds checks in the inner loop.
-// The pool is the counterpart of the reference's fixed-stride expert records
-// (models/flashnext/slab_pack.py:1-25, expert_pool.py:1-22): expert e's
-// records start at e * expert_stride.
+// Activation records (written per call): per (chunk, sorted position) the
+// chunk's 128 inputs in lane order plus the group sums (kActRecord bytes).
+// An item's positions are consecutive, so lane 0 brings a chunk's weights
+// and all of the item's activations with two bulk copies onto one mbarrier;
+// no other lane issues copies or computes addresses.
+//
+// Items hold up to four tokens: B operand 0 carries tokens 0-1, B operand 1
+// tokens 2-3 (only for items with more than two), both multiplied against
+// the same unpacked weight fragments.  The pipeline runs across the warp's
+// tasks, so the copies of the next task start while the current one is
+// being consumed.  Records out of range (rows >= out, groups >= in/32) hold
+// zeros and add exactly zero.
+#include <type_traits>
+
 #include "vx_async.cuh"
 #include "vx_common.cuh"
 #include "vx_launch.h"
@@ -34,7 +42,7 @@ namespace vx {
 
 constexpr int kTiledThreads = 256;
 constexpr int kTiledWarps = kTiledThreads / 32;
-constexpr int kTiledStages = 4;
+constexpr int kTiledStages = 3;
 
 struct TiledTask {
   int e, p0, cnt, row0, N, K;
@@ -54,14 +62,35 @@ VX_DEVICE bool decode_task(const TiledArgs& a, int t, TiledTask& k) {
   return k.row0 < k.N;
 }
 
+// Lane 0 arms the stage's mbarrier for both copies and issues them; the
+// other lanes execute nothing (predicated inside one asm block, no branch).
+VX_DEVICE void issue_stage(bool leader, uint32_t bar, uint32_t dst_w, const void* src_w, uint32_t nw,
+                           uint64_t pol_w, uint32_t dst_x, const void* src_x, uint32_t nx,
+                           uint64_t pol_x) {
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "setp.ne.b32 p, %0, 0;\n"
+      "@p fence.proxy.async.shared::cta;\n"
+      "@p mbarrier.arrive.expect_tx.shared::cta.b64 _, [%1], %2;\n"
+      "@p cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%3], [%4], %5, "
+      "[%1], %6;\n"
+      "@p cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%7], [%8], %9, "
+      "[%1], %10;\n"
+      "}\n" ::"r"(int(leader)),
+      "r"(bar), "r"(nw + nx), "r"(dst_w), "l"(src_w), "r"(nw), "l"(pol_w), "r"(dst_x), "l"(src_x), "r"(nx),
+      "l"(pol_x)
+      : "memory");
+}
+
 template <bool GATEUP, int MT, bool XMMA, int STAGES>
 __global__ void __launch_bounds__(kTiledThreads, 2) gemv_tiled_kernel(const __grid_constant__ TiledArgs a) {
   constexpr int NP = GATEUP ? 2 : 1;
   constexpr int kRec = NP * MT * kTileRecordUnit;
   constexpr int kWBytes = NP * MT * 1024;
-  constexpr int kXOff = kRec;                 // x: [i][b-lane g][16 B]
-  constexpr int kXsOff = kRec + 512;          // sum(x) pairs [lane]
-  constexpr int kStage = (kRec + 512 + (XMMA ? 0 : 256) + 127) & ~127;
+  constexpr int kXOff = kRec;                       // [token][kActRecord]
+  constexpr int kStage = kRec + kTiledItemChunk * kActRecord;
+  static_assert(kStage % 128 == 0, "stage size");
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) uint64_t bars[kTiledWarps][STAGES];
   __shared__ __align__(16) uint32_t zero16[4];
@@ -75,35 +104,30 @@ __global__ void __launch_bounds__(kTiledThreads, 2) gemv_tiled_kernel(const __gr
   const uint32_t ring = smem_u32(smem) + warp * STAGES * kStage;
   const uint32_t bar0 = smem_u32(&bars[warp][0]);
   const uint32_t zaddr = smem_u32(zero16);
-  const bool blane = (g & 3) == c;   // carries token (g >> 2) on group c
+  const bool blane = (g & 3) == c;   // carries token (g >> 2) of its pair on group c
   const int tb = g >> 2, ts = c >> 1;
   const int n_items = *a.n_items;
   const int total = n_items * a.tiles_per_item;
   const int nw = gridDim.x * kTiledWarps;
-  const uint64_t pol = policy_evict_first();
+  const uint64_t pol_w = policy_evict_first();
+  const uint64_t pol_x = policy_evict_last();
+  const int64_t act_pitch = a.act_rows * kActRecord;   // bytes per chunk of activations
 
   // ---- producer cursor: task ti, chunk ci ----
   int ti = blockIdx.x * kTiledWarps + warp, ci = 0;
-  int inch = 0, iG = 0;   // chunks and groups of the task being issued
+  int inch = 0;
+  uint32_t ixbytes = 0;
   const unsigned char* irec = nullptr;
-  const uint16_t* ix = a.x;
-  const float* ixs = a.xsum;
-  bool ixv = false, ixsv = false;
+  const unsigned char* iact = nullptr;
   auto seek = [&]() {   // first valid task at or after ti
     for (; ti < total; ti += nw) {
       TiledTask k;
       if (!decode_task<MT>(a, ti, k)) continue;
       const int rb = k.row0 / (16 * MT);
       inch = (k.K + 127) >> 7;
-      iG = k.K >> 5;
       irec = (k.sh ? a.rec_s : a.rec_b + int64_t(k.e) * a.stride_b) + int64_t(rb) * inch * kRec;
-      ixv = blane && tb < k.cnt;
-      ixsv = ts < k.cnt;
-      int64_t rx = 0, rs = 0;
-      if (ixv) rx = a.src_rows ? __ldg(a.src_rows + k.p0 + tb) : k.p0 + tb;
-      if (!XMMA && ixsv) rs = a.src_rows ? __ldg(a.src_rows + k.p0 + ts) : k.p0 + ts;
-      ix = a.x + rx * a.ldx + c * 32;
-      if (!XMMA) ixs = a.xsum + rs * a.ldxs + 2 * (c & 1);
+      iact = a.act + int64_t(k.p0) * kActRecord;
+      ixbytes = uint32_t(k.cnt) * kActRecord;
       return;
     }
   };
@@ -112,16 +136,8 @@ __global__ void __launch_bounds__(kTiledThreads, 2) gemv_tiled_kernel(const __gr
   bool timed_out = false;
   auto issue = [&]() {
     const uint32_t st = ring + st_issue * kStage;
-    if (lane == 0) {
-      const uint32_t bar = bar0 + 8 * st_issue;
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      mbar_expect(bar, kRec);
-      bulk_load(st, irec + int64_t(ci) * kRec, kRec, bar, pol);
-    }
-    const int nbytes = (ixv && 4 * ci + c < iG) ? 16 : 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) cp16_if(st + kXOff + (i * 8 + g) * 16, ix + ci * 128 + 8 * i, nbytes, blane);
-    if (!XMMA) cp8(st + kXsOff + lane * 8, ixs + ci * 4, ixsv && 4 * ci + 2 * (c & 1) < iG);
+    issue_stage(lane == 0, bar0 + 8 * st_issue, st, irec + int64_t(ci) * kRec, kRec, pol_w, st + kXOff,
+                iact + int64_t(ci) * act_pitch, ixbytes, pol_x);
     st_issue = st_issue == STAGES - 1 ? 0 : st_issue + 1;
     if (++ci == inch) {
       ci = 0;
@@ -132,53 +148,61 @@ __global__ void __launch_bounds__(kTiledThreads, 2) gemv_tiled_kernel(const __gr
 
   seek();
 #pragma unroll
-  for (int s = 0; s < STAGES - 1; ++s) {
+  for (int s = 0; s < STAGES - 1; ++s)
     if (ti < total) issue();
-    cp_commit();
-  }
 
   // ---- consumer: tasks in the same order ----
-  for (int t = blockIdx.x * kTiledWarps + warp; t < total; t += nw) {
-    TiledTask k;
-    if (!decode_task<MT>(a, t, k)) continue;   // warp-uniform
-    float acc[NP][MT][2];
+  auto run = [&](const TiledTask& k, auto nq_tag) {
+    constexpr int NQ = decltype(nq_tag)::value;   // B operands (token pairs)
+    float acc[NP][MT][NQ][2];
 #pragma unroll
     for (int p = 0; p < NP; ++p)
 #pragma unroll
-      for (int m = 0; m < MT; ++m) acc[p][m][0] = acc[p][m][1] = 0.f;
-
+      for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int q = 0; q < NQ; ++q) acc[p][m][q][0] = acc[p][m][q][1] = 0.f;
+    // B lanes of a present token read its activations; the others read zeros
+    uint32_t xa[NQ], xsa[NQ];
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+      const bool live = blane && 2 * q + tb < k.cnt;
+      xa[q] = live ? kXOff + (2 * q + tb) * kActRecord + c * 16 : 0xFFFFFFFFu;
+      xsa[q] = kXOff + (2 * q + ts) * kActRecord + kActXsum + (c & 1) * 8;
+    }
     const int nch = (k.K + 127) >> 7;
     for (int ch = 0; ch < nch; ++ch) {
       if (ti < total) issue();
-      cp_commit();
-      cp_wait<STAGES - 1>();
       const uint32_t st = ring + st_use * kStage;
       if (!mbar_wait(bar0 + 8 * st_use, (parity_bits >> st_use) & 1u)) timed_out = true;
       parity_bits ^= 1u << st_use;
 
-      uint32_t bq[16];
-      const uint32_t xa = blane ? st + kXOff + g * 16 : zaddr;
-      const uint32_t xstep = blane ? 8 * 16 : 0;
+      uint32_t bq[NQ][16];
+      float xs[NQ][2];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint4 v = lds128(xa + i * xstep);
-        bq[4 * i + 0] = v.x;
-        bq[4 * i + 1] = v.y;
-        bq[4 * i + 2] = v.z;
-        bq[4 * i + 3] = v.w;
-      }
-      float xs0, xs1;
-      if (XMMA) {
-        float d[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int q = 0; q < NQ; ++q) {
+        const bool live = xa[q] != 0xFFFFFFFFu;
+        const uint32_t base = live ? st + xa[q] : zaddr;
+        const uint32_t step = live ? 64 : 0;
 #pragma unroll
-        for (int mm = 0; mm < 8; ++mm)
-          mma16816(d, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u, bq[2 * mm], bq[2 * mm + 1]);
-        xs0 = d[0];
-        xs1 = d[1];
-      } else {
-        const uint2 v = lds64(st + kXsOff + lane * 8);
-        xs0 = __uint_as_float(v.x);
-        xs1 = __uint_as_float(v.y);
+        for (int i = 0; i < 4; ++i) {
+          const uint4 v = lds128(base + i * step);
+          bq[q][4 * i + 0] = v.x;
+          bq[q][4 * i + 1] = v.y;
+          bq[q][4 * i + 2] = v.z;
+          bq[q][4 * i + 3] = v.w;
+        }
+        if (XMMA) {
+          float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int mm = 0; mm < 8; ++mm)
+            mma16816(d, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u, bq[q][2 * mm], bq[q][2 * mm + 1]);
+          xs[q][0] = d[0];
+          xs[q][1] = d[1];
+        } else {
+          const uint2 v = lds64(st + xsa[q]);
+          xs[q][0] = __uint_as_float(v.x);
+          xs[q][1] = __uint_as_float(v.y);
+        }
       }
 #pragma unroll
       for (int p = 0; p < NP; ++p) {
@@ -188,18 +212,25 @@ __global__ void __launch_bounds__(kTiledThreads, 2) gemv_tiled_kernel(const __gr
           const uint4 wg = lds128(wrow), w8 = lds128(wrow + 512);
           const uint32_t ag[4] = {wg.x, wg.y, wg.z, wg.w};
           const uint32_t a8[4] = {w8.x, w8.y, w8.z, w8.w};
-          float d[4] = {0.f, 0.f, 0.f, 0.f}, e2[4] = {0.f, 0.f, 0.f, 0.f};
+          float d[NQ][4], e2[NQ][4];
+#pragma unroll
+          for (int q = 0; q < NQ; ++q)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) d[q][i] = e2[q][i] = 0.f;
 #pragma unroll
           for (int mm = 0; mm < 8; mm += 2) {
             const int wi = mm >> 1;
-            mma16816(d, nib_pair128(ag[wi]), nib_pair128(a8[wi]), nib_pair128(ag[wi] >> 4),
-                     nib_pair128(a8[wi] >> 4), bq[2 * mm], bq[2 * mm + 1]);
-            mma16816(e2, nib_pair128(ag[wi] >> 8), nib_pair128(a8[wi] >> 8),
-                     nib_pair128(ag[wi] >> 12), nib_pair128(a8[wi] >> 12), bq[2 * mm + 2],
-                     bq[2 * mm + 3]);
-          }
+            const uint32_t f0 = nib_pair128(ag[wi]), f1 = nib_pair128(a8[wi]);
+            const uint32_t f2 = nib_pair128(ag[wi] >> 4), f3 = nib_pair128(a8[wi] >> 4);
+            const uint32_t h0 = nib_pair128(ag[wi] >> 8), h1 = nib_pair128(a8[wi] >> 8);
+            const uint32_t h2 = nib_pair128(ag[wi] >> 12), h3 = nib_pair128(a8[wi] >> 12);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) d[i] += e2[i];
+            for (int q = 0; q < NQ; ++q) {
+              // two independent accumulator chains (even / odd MMAs)
+              mma16816(d[q], f0, f1, f2, f3, bq[q][2 * mm], bq[q][2 * mm + 1]);
+              mma16816(e2[q], h0, h1, h2, h3, bq[q][2 * mm + 2], bq[q][2 * mm + 3]);
+            }
+          }
           const uint4 sb = lds128(st + kWBytes + (p * MT + m) * 256 + (g * 2 + (c & 1)) * 16);
           const uint32_t sw[4] = {sb.x, sb.y, sb.z, sb.w};
 #pragma unroll
@@ -211,12 +242,15 @@ __global__ void __launch_bounds__(kTiledThreads, 2) gemv_tiled_kernel(const __gr
             // bias - 128*scale: the lop3 operands carry q + 128.
             const float c0 = fmaf(-128.f, s0, b0);
             const float c1 = fmaf(-128.f, s1, b1);
-            float v = acc[p][m][h];
-            v = fmaf(s0, d[2 * h], v);
-            v = fmaf(c0, xs0, v);
-            v = fmaf(s1, d[2 * h + 1], v);
-            v = fmaf(c1, xs1, v);
-            acc[p][m][h] = v;
+#pragma unroll
+            for (int q = 0; q < NQ; ++q) {
+              float v = acc[p][m][q][h];
+              v = fmaf(s0, d[q][2 * h] + e2[q][2 * h], v);
+              v = fmaf(c0, xs[q][0], v);
+              v = fmaf(s1, d[q][2 * h + 1] + e2[q][2 * h + 1], v);
+              v = fmaf(c1, xs[q][1], v);
+              acc[p][m][q][h] = v;
+            }
           }
         }
       }
@@ -224,16 +258,21 @@ __global__ void __launch_bounds__(kTiledThreads, 2) gemv_tiled_kernel(const __gr
       st_use = st_use == STAGES - 1 ? 0 : st_use + 1;
     }
 
+    // lanes c and c^1 hold the two group halves of the same (row, token)
 #pragma unroll
     for (int p = 0; p < NP; ++p)
 #pragma unroll
       for (int m = 0; m < MT; ++m)
 #pragma unroll
-        for (int h = 0; h < 2; ++h) acc[p][m][h] += __shfl_xor_sync(0xFFFFFFFFu, acc[p][m][h], 1);
-    const int tok = c >> 1;
-    if ((c & 1) == 0 && tok < k.cnt) {
-      const int pos = k.p0 + tok;
-      const int64_t dst = a.dst_rows ? __ldg(a.dst_rows + pos) : pos;
+        for (int q = 0; q < NQ; ++q)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) acc[p][m][q][h] += __shfl_xor_sync(0xFFFFFFFFu, acc[p][m][q][h], 1);
+    if (c & 1) return;
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+      const int tok = 2 * q + (c >> 1);
+      if (tok >= k.cnt) continue;
+      const int64_t pos = k.p0 + tok;
 #pragma unroll
       for (int m = 0; m < MT; ++m)
 #pragma unroll
@@ -241,16 +280,83 @@ __global__ void __launch_bounds__(kTiledThreads, 2) gemv_tiled_kernel(const __gr
           const int row = k.row0 + 16 * m + g + 8 * h;
           if (row >= k.N) continue;
           if (GATEUP) {
-            const float v = silu_mul_bf16(bf16r(acc[0][m][h]), bf16r(acc[NP - 1][m][h]));
-            a.out[dst * a.ldo + b_order_col(row)] = f32_to_bf16(v);
+            // h is the down projection's input: store it as an activation record
+            const float v = silu_mul_bf16(bf16r(acc[0][m][q][h]), bf16r(acc[NP - 1][m][q][h]));
+            const int e8 = row & 7;
+            const int slot = e8 < 4 ? 2 * e8 : 2 * (e8 - 4) + 1;
+            const int64_t off = (row >> 7) * act_pitch + pos * kActRecord +
+                                ((((row >> 3) & 3) * 4 + ((row >> 5) & 3)) * 16) + slot * 2;
+            *reinterpret_cast<uint16_t*>(a.hrec + off) = f32_to_bf16(v);
           } else {
-            a.out[dst * a.ldo + row] = f32_to_bf16(acc[0][m][h]);
+            a.out[pos * a.ldo + row] = f32_to_bf16(acc[0][m][q][h]);
           }
         }
     }
+  };
+
+  for (int t = blockIdx.x * kTiledWarps + warp; t < total; t += nw) {
+    TiledTask k;
+    if (!decode_task<MT>(a, t, k)) continue;   // warp-uniform
+    if (k.cnt > 2)
+      run(k, std::integral_constant<int, 2>());
+    else
+      run(k, std::integral_constant<int, 1>());
   }
-  cp_wait<0>();
   if (timed_out && a.err) atomicOr(a.err, 0x100);
+}
+
+// ---- activation records ------------------------------------------------------
+
+// One thread per 8-input block of a (position, chunk): reads the token's x,
+// writes the block in B order at lane-order slot (i*4 + c) and, for the first
+// block of each group, the group sum - computed exactly as the MLX-layout
+// path computes it (left-to-right over 8 inputs, then (s0+s1)+(s2+s3)), so the
+// two paths stay bit-identical.
+__global__ void act_records_kernel(const uint16_t* __restrict__ x, int64_t ldx, int K,
+                                   const int32_t* __restrict__ src_rows, const int32_t* __restrict__ n_rows,
+                                   int64_t rows, unsigned char* __restrict__ act) {
+  const int nch = (K + 127) / 128;
+  const int nb = nch * 16;   // 8-input blocks per position, chunk padding included
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t n = rows * nb;
+  const int64_t limit = n_rows ? int64_t(*n_rows) : rows;
+  const int64_t p = i < n ? i / nb : 0;
+  const int blk = i < n ? int(i - p * nb) : 0;
+  const bool live = i < n && p < limit;
+  const bool inside = live && blk * 8 < K;
+  uint4 v = make_uint4(0, 0, 0, 0);
+  if (inside) {
+    const int64_t r = src_rows ? int64_t(__ldg(src_rows + p)) : p;
+    v = *reinterpret_cast<const uint4*>(x + r * ldx + blk * 8);
+  }
+  float s = 0.f;
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    s += __uint_as_float(w[j] << 16);
+    s += __uint_as_float(w[j] & 0xFFFF0000u);
+  }
+  s += __shfl_xor_sync(0xFFFFFFFFu, s, 1);
+  s += __shfl_xor_sync(0xFFFFFFFFu, s, 2);
+  if (!live) return;
+  const int ch = blk >> 4, c = (blk >> 2) & 3, ib = blk & 3;
+  unsigned char* rec = act + (int64_t(ch) * rows + p) * kActRecord;
+  uint4 o;
+  o.x = prmt(v.x, v.z, 0x5410);   // (x0, x4)
+  o.y = prmt(v.x, v.z, 0x7632);   // (x1, x5)
+  o.z = prmt(v.y, v.w, 0x5410);   // (x2, x6)
+  o.w = prmt(v.y, v.w, 0x7632);   // (x3, x7)
+  *reinterpret_cast<uint4*>(rec + (ib * 4 + c) * 16) = o;
+  if (ib == 0) *reinterpret_cast<float*>(rec + kActXsum + c * 4) = inside ? s : 0.f;
+}
+
+cudaError_t launch_act_records(const uint16_t* x, int64_t ldx, int K, const int32_t* src_rows,
+                               const int32_t* n_rows, int64_t rows, unsigned char* act,
+                               cudaStream_t st) {
+  const int64_t n = rows * ((K + 127) / 128) * 16;
+  if (n == 0) return cudaSuccess;
+  act_records_kernel<<<int((n + 255) / 256), 256, 0, st>>>(x, ldx, K, src_rows, n_rows, rows, act);
+  return cudaGetLastError();
 }
 
 // ---- pool packing -----------------------------------------------------------
@@ -335,8 +441,7 @@ cudaError_t launch_tile_pack(const vx_q4& a, const vx_q4& b, int nproj, int tile
 template <bool GATEUP, int MT, bool XMMA>
 static cudaError_t launch_tiled_t(TiledArgs a, int max_items, int max_out, cudaStream_t st) {
   constexpr int NP = GATEUP ? 2 : 1;
-  constexpr int kRec = NP * MT * kTileRecordUnit;
-  constexpr int kStage = (kRec + 512 + (XMMA ? 0 : 256) + 127) & ~127;
+  constexpr int kStage = NP * MT * kTileRecordUnit + kTiledItemChunk * kActRecord;
   a.tiles_per_item = (max_out + 16 * MT - 1) / (16 * MT);
   const size_t smem = size_t(kTiledWarps) * kTiledStages * kStage;
   auto kern = gemv_tiled_kernel<GATEUP, MT, XMMA, kTiledStages>;
@@ -351,20 +456,16 @@ static cudaError_t launch_tiled_t(TiledArgs a, int max_items, int max_out, cudaS
   return cudaGetLastError();
 }
 
+// gate/up: activation records carry the group sums; the single projection
+// (down) sums its input h on the tensor pipe.
 cudaError_t launch_gemv_tiled(bool gateup, int tile_rows, const TiledArgs& a, int max_items,
                               int max_out, cudaStream_t st) {
-  const bool xmma = a.xsum == nullptr;
   if (gateup) {
     if (tile_rows != 16) return cudaErrorInvalidValue;
-    return xmma ? launch_tiled_t<true, 1, true>(a, max_items, max_out, st)
-                : launch_tiled_t<true, 1, false>(a, max_items, max_out, st);
+    return launch_tiled_t<true, 1, false>(a, max_items, max_out, st);
   }
-  if (tile_rows == 32)
-    return xmma ? launch_tiled_t<false, 2, true>(a, max_items, max_out, st)
-                : launch_tiled_t<false, 2, false>(a, max_items, max_out, st);
-  if (tile_rows == 16)
-    return xmma ? launch_tiled_t<false, 1, true>(a, max_items, max_out, st)
-                : launch_tiled_t<false, 1, false>(a, max_items, max_out, st);
+  if (tile_rows == 32) return launch_tiled_t<false, 2, true>(a, max_items, max_out, st);
+  if (tile_rows == 16) return launch_tiled_t<false, 1, true>(a, max_items, max_out, st);
   return cudaErrorInvalidValue;
 }
 

@@ -47,6 +47,18 @@ cudaError_t launch_gemv_mma(bool gateup, const MmaArgs& a, int max_items, int ma
 // 128-input chunk: 1024 of packed words + 256 of scales and biases.
 constexpr int kTileRecordUnit = 1280;
 
+// Tokens per work item of the tiled GEMV: two B operands of two tokens each
+// share every unpacked weight fragment.
+constexpr int kTiledItemChunk = 4;
+
+// Activation records of the tiled GEMV: per (128-input chunk, position) 320
+// bytes - the chunk's 128 bf16 inputs in lane order [i][c] (8 inputs each,
+// B order inside), then the four group sums as float32, then padding.  An
+// item's positions are consecutive, so one bulk copy brings all its tokens.
+// The 320-byte pitch puts the two tokens a B operand reads on disjoint banks.
+constexpr int kActRecord = 320;
+constexpr int kActXsum = 256;
+
 struct TiledArgs {
   int32_t* err;                 // bit 8 set when a pipeline wait ran out (may be null)
   const unsigned char* rec_b;   // routed experts' records
@@ -55,18 +67,24 @@ struct TiledArgs {
   int N_b, N_s;                 // output rows of the routed / shared projection
   int K_b, K_s;                 // inputs of the routed / shared projection
   int E;
-  const int32_t* items;         // [n][3] expert, first position, count
+  const int32_t* items;         // [n][3] expert, first position, count (<= kTiledItemChunk)
   const int32_t* n_items;
-  const int32_t* src_rows;
-  const int32_t* dst_rows;
-  const uint16_t* x;            // activations in B order
-  int64_t ldx;
-  const float* xsum;            // null: sum(x) on the tensor pipe
-  int64_t ldxs;
-  uint16_t* out;
+  const unsigned char* act;     // activation records [chunk][act_rows][kActRecord]
+  int64_t act_rows;             // positions per chunk of act (and of hrec)
+  unsigned char* hrec;          // gate/up: h written as activation records (no sums)
+  uint16_t* out;                // projection: plain rows [position][ldo]
   int64_t ldo;
   int tiles_per_item;           // set by the launcher
 };
+
+// x rows (token src_rows[p] for position p < *n_rows, or p when src_rows is
+// null) -> activation records with group sums; chunk padding is zero.
+cudaError_t launch_act_records(const uint16_t* x, int64_t ldx, int K, const int32_t* src_rows,
+                               const int32_t* n_rows, int64_t rows, unsigned char* act,
+                               cudaStream_t st);
+inline int64_t act_record_bytes(int K, int64_t rows) {
+  return int64_t((K + 127) / 128) * rows * kActRecord;
+}
 
 int64_t tile_pool_bytes(int64_t experts, int out, int in, int nproj, int tile_rows);
 cudaError_t launch_tile_pack(const vx_q4& a, const vx_q4& b, int nproj, int tile_rows, void* out,
