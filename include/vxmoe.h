@@ -97,7 +97,15 @@ typedef struct vx_moe_weights {
   int32_t hidden;
   int32_t top_k;
   const vx_moe_pool* pool;    /* may be NULL */
+  /* Expert pipeline: VX_PATH_AUTO picks the grouped GEMV for decode-sized
+   * batches and the tcgen05 grouped GEMM once the batch averages at least
+   * four routed positions per expert (T*top_k >= 4*num_experts). */
+  int32_t expert_path;
 } vx_moe_weights;
+
+#define VX_PATH_AUTO 0
+#define VX_PATH_GEMV 1
+#define VX_PATH_GEMM 2
 
 /* Library identification and error text. */
 const char* vx_version(void);

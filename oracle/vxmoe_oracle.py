@@ -366,6 +366,32 @@ def expert_mlp_bf16(x, gate: Q4Bank, up: Q4Bank, down: Q4Bank, group_size=GROUP_
     return g, u, h, y
 
 
+def dequantize_bf16(bank: Q4Bank, group_size=GROUP_SIZE) -> np.ndarray:
+    """Weights as MLX's quantized-matmul kernels stage them for large batches:
+    ``bf16(scale*q + bias)``, one rounding of the exact value (the float32
+    product ``scale*q`` is exact; the sum with the bias then rounds once)."""
+    return bf16_round(dequantize(bank.w, bank.scales, bank.biases, group_size))
+
+
+def qmm_bf16(x, bank: Q4Bank, group_size=GROUP_SIZE) -> np.ndarray:
+    """The prefill-path projection (MLX ``gather_qmm`` on sorted, batched
+    rows, expert_cache.py:2017-2037): bf16 dequantised tile, products summed
+    in high precision, bf16 out.  The float64 sum stands in for the kernel's
+    float32 tensor-core accumulation, whose order is the hardware's."""
+    w = dequantize_bf16(bank, group_size).astype(np.float64)
+    return bf16_round((f32(x).astype(np.float64) @ w.T).astype(np.float32))
+
+
+def expert_mlp_qmm(x, gate: Q4Bank, up: Q4Bank, down: Q4Bank, group_size=GROUP_SIZE):
+    """One expert on the prefill path: bf16-dequantised gate/up and down
+    tiles, bf16 SwiGLU between.  Returns (g, u, h, y)."""
+    g = qmm_bf16(x, gate, group_size)
+    u = qmm_bf16(x, up, group_size)
+    h = silu_mul_bf16(g, u)
+    y = qmm_bf16(h, down, group_size)
+    return g, u, h, y
+
+
 def shared_parts(x, p: MoEParams):
     """``shared = shared_expert(x)``, ``sg = sigmoid(shared_expert_gate(x))``
     in bf16 (``adaptive_topk.py:264-265``)."""

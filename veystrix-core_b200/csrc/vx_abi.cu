@@ -2,6 +2,7 @@
 // workspace carving and the launch sequence of each entry point.  No entry
 // point allocates device memory or synchronises the host.
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
@@ -64,6 +65,7 @@ struct BlockDims {
   int E, d, k, I, Is;
   bool shared;
   const vx_moe_pool* pool = nullptr;
+  int path = VX_PATH_AUTO;   // the weights' expert_path
 };
 
 static int check_tiles(const vx_q4_tiles& t, int experts, int out, int in, int nproj) {
@@ -109,7 +111,8 @@ static int check_weights(const vx_moe_weights* W, bool need_router, BlockDims* d
     if (need_router && (s = check_q4(&W->shared_expert_gate, 1, 1, d))) return s;
   }
   if (W->pool && (s = check_pool(W->pool, E, d, I, Is, shared))) return s;
-  *dm = {E, d, k, I, Is, shared, W->pool};
+  if (W->expert_path < VX_PATH_AUTO || W->expert_path > VX_PATH_GEMM) return VX_EINVAL_SHAPE;
+  *dm = {E, d, k, I, Is, shared, W->pool, W->expert_path};
   return VX_OK;
 }
 
@@ -124,8 +127,32 @@ struct ExpertScratch {
   int max_items;
 };
 
+// Which expert pipeline runs a batch.  Decode-sized batches (a few tokens per
+// expert) stream the weights through the GEMV - from the tiled pool when the
+// weights carry one; prefill-sized batches (on average at least four routed
+// positions per expert) take the tcgen05 GEMM.  The weights' expert_path
+// forces one side; so does VXMOE_EXPERT_PATH=gemv|gemm when it is AUTO.
+enum ExpertPath { kPathGemvMlx = 0, kPathGemvTiled = 1, kPathGemm = 2 };
+
+static int path_override() {
+  static int v = -1;
+  if (v < 0) {
+    const char* s = getenv("VXMOE_EXPERT_PATH");
+    v = (s && strcmp(s, "gemv") == 0) ? 1 : (s && strcmp(s, "gemm") == 0) ? 2 : 0;
+  }
+  return v;
+}
+
+static ExpertPath expert_path(int T, const BlockDims& dm) {
+  const int o = dm.path != VX_PATH_AUTO ? dm.path : path_override();
+  const bool gemm = o == VX_PATH_GEMM || (o == VX_PATH_AUTO && int64_t(T) * dm.k >= 4 * int64_t(dm.E));
+  if (gemm) return kPathGemm;
+  return dm.pool ? kPathGemvTiled : kPathGemvMlx;
+}
+
 static ExpertScratch carve_experts(Carver& c, int T, const BlockDims& dm) {
   const int64_t P = int64_t(T) * dm.k, Ts = dm.shared ? T : 0;
+  const ExpertPath path = expert_path(T, dm);
   ExpertScratch s;
   s.order = c.take<int32_t>(P);
   s.inverse = c.take<int32_t>(P);
@@ -143,7 +170,10 @@ static ExpertScratch carve_experts(Carver& c, int T, const BlockDims& dm) {
   s.h = s.xb = nullptr;
   s.xs = nullptr;
   s.act = s.hrec = nullptr;
-  if (dm.pool) {
+  if (path == kPathGemm) {
+    s.h = c.take<uint16_t>((P + Ts) * s.ldh);
+    s.xb = c.take<uint16_t>((P + Ts) * dm.d);   // x gathered into sorted order
+  } else if (path == kPathGemvTiled) {
     s.act = c.take<unsigned char>(act_record_bytes(dm.d, P + Ts));
     s.hrec = c.take<unsigned char>(act_record_bytes(int(s.ldh), P + Ts));
   } else {
@@ -161,11 +191,86 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
   const int Ts = dm.shared ? T : 0;
   cudaError_t e = cudaMemsetAsync(s.err, 0, 2 * sizeof(int32_t), st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
+  const ExpertPath path = expert_path(T, dm);
+  const int chunk = path == kPathGemm ? (dm.pool ? kPoolGemmItemChunk : kGemmItemChunk)
+                    : path == kPathGemvTiled ? kTiledItemChunk : kItemChunk;
   e = launch_permute(routes, P, dm.E, Ts, dm.k, nullptr, s.order, s.inverse, s.offsets, s.active,
-                     s.n_active, s.src_rows, s.err, dm.pool ? kTiledItemChunk : kItemChunk, s.items,
-                     s.n_items, st);
+                     s.n_active, s.src_rows, s.err, chunk, s.items, s.n_items, st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
-  if (dm.pool) {
+  if (path == kPathGemm) {
+    e = launch_gather_border(x, dm.d, dm.d, s.src_rows, s.offsets + dm.E + 1, P + Ts, s.xb, st);
+    if (e != cudaSuccess) return vx_cuda_fail(e);
+    profile_mark(st, "permute");
+    if (dm.pool) {
+      // persistent kernel over the tiled pool's records
+      const vx_moe_pool& pl = *dm.pool;
+      PoolGemmArgs a{};
+      a.err = s.err + 1;
+      a.rec_b = static_cast<const unsigned char*>(pl.gate_up.records);
+      a.stride_b = tile_pool_bytes(1, dm.I, dm.d, 2, pl.gate_up.tile_rows);
+      a.rec_s = dm.shared ? static_cast<const unsigned char*>(pl.shared_gate_up.records) : nullptr;
+      a.N_b = dm.I;
+      a.N_s = dm.Is;
+      a.K_b = a.K_s = dm.d;
+      a.tile_rows = pl.gate_up.tile_rows;
+      a.E = dm.E;
+      a.items = s.items;
+      a.n_items = s.n_items;
+      a.out = s.h;
+      a.ldo = s.ldh;
+      e = launch_gemm_pool(true, a, s.xb, P + Ts, dm.d, s.max_items, st);
+      if (e != cudaSuccess) return vx_cuda_fail(e);
+      profile_mark(st, "gate_up_swiglu");
+      PoolGemmArgs b{};
+      b.err = s.err + 1;
+      b.rec_b = static_cast<const unsigned char*>(pl.down.records);
+      b.stride_b = tile_pool_bytes(1, dm.d, dm.I, 1, pl.down.tile_rows);
+      b.rec_s = dm.shared ? static_cast<const unsigned char*>(pl.shared_down.records) : nullptr;
+      b.N_b = b.N_s = dm.d;
+      b.K_b = dm.I;
+      b.K_s = dm.Is;
+      b.tile_rows = pl.down.tile_rows;
+      b.E = dm.E;
+      b.items = s.items;
+      b.n_items = s.n_items;
+      b.out = s.yd;
+      b.ldo = dm.d;
+      e = launch_gemm_pool(false, b, s.h, P + Ts, s.ldh, s.max_items, st);
+      if (e != cudaSuccess) return vx_cuda_fail(e);
+      profile_mark(st, "down");
+      return VX_OK;
+    }
+    GemmArgs a{};
+    a.err = s.err + 1;
+    a.b0 = W->gate;
+    a.b1 = W->up;
+    if (dm.shared) {
+      a.s0 = W->shared_gate;
+      a.s1 = W->shared_up;
+    }
+    a.E = dm.E;
+    a.items = s.items;
+    a.n_items = s.n_items;
+    a.out = s.h;
+    a.ldo = s.ldh;
+    e = launch_gemm_tc(true, a, s.xb, P + Ts, dm.d, s.max_items, st);
+    if (e != cudaSuccess) return vx_cuda_fail(e);
+    profile_mark(st, "gate_up_swiglu");
+    GemmArgs b{};
+    b.err = s.err + 1;
+    b.b0 = W->down;
+    if (dm.shared) b.s0 = W->shared_down;
+    b.E = dm.E;
+    b.items = s.items;
+    b.n_items = s.n_items;
+    b.out = s.yd;
+    b.ldo = dm.d;
+    e = launch_gemm_tc(false, b, s.h, P + Ts, s.ldh, s.max_items, st);
+    if (e != cudaSuccess) return vx_cuda_fail(e);
+    profile_mark(st, "down");
+    return VX_OK;
+  }
+  if (path == kPathGemvTiled) {
     // activation records of the sorted positions (valid count: offsets[E+1])
     e = launch_act_records(x, dm.d, dm.d, s.src_rows, s.offsets + dm.E + 1, P + Ts, s.act, st);
     if (e == cudaSuccess && (dm.I % 128 || dm.Is % 128))   // zero chunk padding of h
@@ -176,7 +281,7 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
   if (e != cudaSuccess) return vx_cuda_fail(e);
   profile_mark(st, "permute");
 
-  if (dm.pool) {
+  if (path == kPathGemvTiled) {
     const vx_moe_pool& pl = *dm.pool;
     TiledArgs a{};
     a.err = s.err + 1;
@@ -489,7 +594,8 @@ int vx_permute(const int32_t* ids, int64_t P, int32_t E, int32_t* order, int32_t
 
 size_t vx_moe_experts_workspace(int32_t T, const vx_moe_weights* W) {
   if (!W || T < 0) return 0;
-  BlockDims dm{W->num_experts, W->hidden, W->top_k, W->gate.out, 0, false, W->pool};
+  BlockDims dm{W->num_experts, W->hidden, W->top_k, W->gate.out, 0, false, W->pool,
+               W->expert_path};
   Carver c(nullptr);
   carve_experts(c, T, dm);
   return c.size();
@@ -557,7 +663,7 @@ size_t vx_moe_block_workspace(int32_t T, const vx_moe_weights* W) {
   if (!W || T < 0) return 0;
   const bool shared = W->shared_gate.w != nullptr;
   BlockDims dm{W->num_experts, W->hidden, W->top_k, W->gate.out, shared ? W->shared_gate.out : 0,
-               shared, W->pool};
+               shared, W->pool, W->expert_path};
   Carver c(nullptr);
   c.take<uint16_t>(int64_t(T) * dm.E);   // logits
   c.take<int32_t>(int64_t(T) * dm.k);    // inds

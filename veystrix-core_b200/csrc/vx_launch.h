@@ -86,6 +86,56 @@ inline int64_t act_record_bytes(int K, int64_t rows) {
   return int64_t((K + 127) / 128) * rows * kActRecord;
 }
 
+// Grouped expert GEMM on tcgen05 (prefill).  Items of up to kGemmItemChunk
+// positions; B operand rows in B order ([rows][ld] bf16).
+constexpr int kGemmItemChunk = 128;
+
+struct GemmArgs {
+  CUtensorMap tm[2][4];      // [routed, shared][box rows 16, 32, 64, 128] (set by the launcher)
+  int32_t* err;              // bit 9 set when a pipeline wait ran out (may be null)
+  vx_q4 b0, b1;              // routed banks (b1: up in gate/up mode)
+  vx_q4 s0, s1;              // shared expert banks (expert id E)
+  int E;
+  const int32_t* items;      // [n][3] expert, first position, count (<= kGemmItemChunk)
+  const int32_t* n_items;
+  uint16_t* out;             // gate/up: h rows in B order; projection: plain rows
+  int64_t ldo;
+  int row_tiles;             // set by the launcher
+};
+
+cudaError_t launch_gemm_tc(bool gateup, GemmArgs a, const uint16_t* x, int64_t rows, int64_t ldx,
+                           int max_items, cudaStream_t st);
+
+// bf16 rows [rows][ld] as a 2-D tensor [rows][K] (columns >= K read as zero),
+// box 64 columns (128 bytes, 128-byte swizzle) x box_rows rows.
+cudaError_t encode_rows(CUtensorMap* m, const uint16_t* p, int64_t rows, int K, int64_t ld, int box_rows);
+
+// The persistent tcgen05 GEMM over the tiled pool: items of up to
+// kPoolGemmItemChunk positions, weights and scales from the pool's records.
+constexpr int kPoolGemmItemChunk = 64;
+
+struct PoolGemmArgs {
+  CUtensorMap tm[2][3];         // [routed, shared][box rows 16, 32, 64] (set by the launcher)
+  int32_t* err;                 // bit 9 set when a pipeline wait ran out (may be null)
+  const unsigned char* rec_b;   // routed records, stride_b bytes per expert
+  int64_t stride_b;
+  const unsigned char* rec_s;   // shared records (expert id E), may be null
+  int N_b, N_s, K_b, K_s;       // outputs and inputs, routed / shared
+  int tile_rows;                // rows per record (16 or 32)
+  int E;
+  const int32_t* items;         // [n][3] expert, first position, count (<= kPoolGemmItemChunk)
+  const int32_t* n_items;
+  uint16_t* out;                // gate/up: h rows in B order; projection: plain rows
+  int64_t ldo;
+  int row_tiles;                // 128-row tiles per item (set by the launcher)
+  int max_tasks;                // upper bound of item x row-tile tasks (set by the launcher)
+};
+
+cudaError_t launch_gemm_pool(bool gateup, PoolGemmArgs a, const uint16_t* x, int64_t rows, int64_t ldx,
+                             int max_items, cudaStream_t st);
+cudaError_t launch_gather_border(const uint16_t* x, int64_t ldx, int K, const int32_t* src_rows,
+                                 const int32_t* n_rows, int64_t rows, uint16_t* out, cudaStream_t st);
+
 int64_t tile_pool_bytes(int64_t experts, int out, int in, int nproj, int tile_rows);
 cudaError_t launch_tile_pack(const vx_q4& a, const vx_q4& b, int nproj, int tile_rows, void* out,
                              cudaStream_t st);

@@ -57,7 +57,11 @@ class VxMoEWeights(ctypes.Structure):
         ("router_w", c_void_p),
         ("num_experts", c_int32), ("hidden", c_int32), ("top_k", c_int32),
         ("pool", ctypes.POINTER(VxMoEPool)),
+        ("expert_path", c_int32),
     ]
+
+
+PATH_AUTO, PATH_GEMV, PATH_GEMM = 0, 1, 2
 
 
 P = c_void_p

@@ -25,7 +25,7 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
-from . import ops
+from . import _lib, ops
 
 
 class CudaBackend:
@@ -49,11 +49,14 @@ class CudaBackend:
     def experts_partial(self, xr, ids, scores):
         return ops.moe_experts_partial(xr, ids, scores, self.w)
 
-    def shared(self, x):
+    def shared(self, x, num_experts):
         if self.shared_w is None:
             return None
-        routes = torch.zeros((x.shape[0], 1), dtype=torch.int32, device=x.device)
-        return ops.moe_experts(x, routes, self.shared_w)[:, 0, :]
+        T = x.shape[0]
+        routes = torch.zeros((T, 1), dtype=torch.int32, device=x.device)
+        # the pipeline the single-GPU block would give its shared rows
+        path = _lib.PATH_GEMM if T * self.w.top_k >= 4 * num_experts else _lib.PATH_GEMV
+        return ops.moe_experts(x, routes, self.shared_w, path=path)[:, 0, :]
 
 
 def shard_weights(w: "ops.MoEWeights", rank: int, world: int) -> "ops.MoEWeights":
@@ -123,7 +126,7 @@ class ExpertParallelMoE:
         part = self.backend.experts_partial(xr, rids, rsc)         # float32 [R, d]
         back = torch.empty((S, d), dtype=torch.float32, device=dev)
         self._a2a(back, part.contiguous(), sc, rc)
-        shared = self.backend.shared(x)
+        shared = self.backend.shared(x, self.E)
         slots = torch.zeros((T, P, d), dtype=torch.float32, device=dev)
         slots[send_tok, send_dst] = back
         routed = slots[:, 0, :]

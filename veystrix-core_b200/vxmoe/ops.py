@@ -195,6 +195,9 @@ class MoEWeights:
         if check_router and self.router_w is not None and tuple(self.router_w.shape) != (E, d):
             raise ValueError(f"router weight shape {tuple(self.router_w.shape)} != {(E, d)}")
         self.pool: Optional[TiledPool] = None
+        # expert pipeline: _lib.PATH_AUTO (GEMV for decode-sized batches,
+        # tcgen05 GEMM from four routed positions per expert), PATH_GEMV, PATH_GEMM
+        self.expert_path = _lib.PATH_AUTO
 
     def pack(self, down_rows: int = 32) -> "MoEWeights":
         """Re-tile the experts into the resident pool the decode kernels
@@ -235,6 +238,7 @@ class MoEWeights:
         s.num_experts, s.hidden, s.top_k = self.num_experts, self.hidden, self.top_k
         if self.pool is not None:
             s.pool = ctypes.pointer(self.pool.vx())
+        s.expert_path = int(self.expert_path)
         return s
 
     def nbytes_per_expert(self) -> int:
@@ -523,11 +527,12 @@ def permute(ids: torch.Tensor, num_experts: int) -> Permutation:
 
 
 def moe_experts(x: torch.Tensor, routes, weights: MoEWeights, scores=None, shared_y=None,
-                shared=None, shared_gate=None) -> torch.Tensor:
+                shared=None, shared_gate=None, path: Optional[int] = None) -> torch.Tensor:
     """Routed experts for given routes (the executor contract,
     ``metal_runtime.py:799-974``).  With ``scores`` returns [T, d]: the
     float32 score-weighted combine of bf16 slot outputs plus the shared part;
-    without, returns the per-slot outputs [T, k, d]."""
+    without, returns the per-slot outputs [T, k, d].  ``path`` overrides the
+    weights' expert pipeline for this call (``_lib.PATH_*``)."""
     x = _bf16(x, "x")
     d = weights.hidden
     x2 = x.reshape(-1, d)
@@ -545,6 +550,8 @@ def moe_experts(x: torch.Tensor, routes, weights: MoEWeights, scores=None, share
     shg = None if shared_gate is None else _bf16(shared_gate.to(torch.bfloat16), "shared_gate").reshape(T)
     st = weights.vx(with_shared=False)
     st.top_k = k
+    if path is not None:
+        st.expert_path = int(path)
     lib = _lib.load()
     ws = _WS.get(lib.vx_moe_experts_workspace(T, ctypes.byref(st)), dev)
     out = torch.empty((T, d) if sc is not None else (T, k, d), dtype=torch.bfloat16, device=dev)
