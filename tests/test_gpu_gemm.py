@@ -84,14 +84,18 @@ def test_gemm_block_matches_float64_reference(packed):
 
 def test_gemm_block_pool_kernel_matches_array_kernel():
     """The persistent kernel over the tiled pool and the kernel reading the MLX
-    arrays dequantise and accumulate identically: the same bits."""
+    arrays dequantise identically; the pool kernel sums the down projection
+    in two interleaved accumulators (even and odd 64-input blocks), so the
+    float32 sums may round differently: within one bf16 ulp."""
     import vxmoe
+    from helpers import ulp_diff_bf16
     p = O.make_params(seed=43, experts=16, hidden=256, inter=128, shared_inter=64, top_k=4)
     x = bf16_t(O.make_x(44, 32, p.hidden))
     a = vxmoe.moe_block(x, weights_from_oracle(p))
     b = vxmoe.moe_block(x, weights_from_oracle(p).pack())
     torch.cuda.synchronize()
-    np.testing.assert_array_equal(a.view(torch.int16).cpu().numpy(), b.view(torch.int16).cpu().numpy())
+    d = ulp_diff_bf16(np32(a), np32(b))
+    assert d.max() <= 1 and float(np.mean(d == 0)) > 0.97
 
 
 @pytest.mark.slow

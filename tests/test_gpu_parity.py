@@ -218,7 +218,8 @@ def test_router_full_production(prod_params):
 # ---------------------------------------------------------------- permutation
 
 @pytest.mark.parametrize("P,E,skew", [(0, 8, False), (1, 8, False), (10, 512, False),
-                                      (640, 512, False), (4096, 64, True), (65536, 512, True)])
+                                      (640, 512, False), (4096, 64, True), (65536, 512, True),
+                                      (20480, 512, False), (100003, 64, False)])
 def test_permute_bit_exact(P, E, skew):
     import vxmoe
     rng = np.random.default_rng(P + E)
@@ -233,6 +234,24 @@ def test_permute_bit_exact(P, E, skew):
     np.testing.assert_array_equal(perm.inverse.cpu().numpy(), inv)
     np.testing.assert_array_equal(perm.offsets.cpu().numpy(), offsets)
     assert int(perm.errors.item()) == 0
+
+
+def test_permute_large_drops_out_of_range_ids():
+    """Prefill-sized input (the multi-CTA permutation): invalid ids are
+    counted, get inverse -1 and leave the order of the others stable."""
+    import vxmoe
+    rng = np.random.default_rng(77)
+    ids = rng.integers(0, 256, 40000).astype(np.int32)
+    bad = rng.random(40000) < 0.01
+    ids[bad] = np.where(rng.random(int(bad.sum())) < 0.5, -1, 256)
+    perm = vxmoe.permute(torch.from_numpy(ids).to(DEV), 256)
+    good = np.nonzero(~bad)[0]
+    order = good[np.argsort(ids[good], kind="stable")]
+    np.testing.assert_array_equal(perm.order.cpu().numpy()[:good.size], order)
+    inv = perm.inverse.cpu().numpy()
+    assert (inv[bad] == -1).all()
+    np.testing.assert_array_equal(inv[order], np.arange(good.size))
+    assert int(perm.errors.item()) == int(bad.sum())
 
 
 def test_permute_counts_out_of_range_ids():

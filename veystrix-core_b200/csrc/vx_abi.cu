@@ -120,6 +120,7 @@ static int check_weights(const vx_moe_weights* W, bool need_router, BlockDims* d
 // the shared expert's T items).
 struct ExpertScratch {
   int32_t *order, *inverse, *offsets, *active, *n_active, *src_rows, *err, *items, *n_items;
+  int32_t* blk;              // per-slice counts of the multi-CTA permutation (prefill sizes)
   uint16_t *h, *yd, *xb;     // xb: x in B order (MLX-layout path)
   float* xs;                 // per-group sum(x) of the T input rows (MLX-layout path)
   unsigned char *act, *hrec; // activation records of x and of h (tiled-pool path)
@@ -164,6 +165,7 @@ static ExpertScratch carve_experts(Carver& c, int T, const BlockDims& dm) {
   s.max_items = max_items_bound(P, dm.E, int(Ts));
   s.items = c.take<int32_t>(3 * int64_t(s.max_items));
   s.n_items = c.take<int32_t>(1);
+  s.blk = c.take<int32_t>(permute_scratch_ints(P, dm.E));
   s.ldh = std::max(dm.I, dm.Is);
   s.yd = c.take<uint16_t>((P + Ts) * dm.d);
   s.ldxs = xsum_stride(dm.d);
@@ -195,7 +197,7 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
   const int chunk = path == kPathGemm ? (dm.pool ? kPoolGemmItemChunk : kGemmItemChunk)
                     : path == kPathGemvTiled ? kTiledItemChunk : kItemChunk;
   e = launch_permute(routes, P, dm.E, Ts, dm.k, nullptr, s.order, s.inverse, s.offsets, s.active,
-                     s.n_active, s.src_rows, s.err, chunk, s.items, s.n_items, st);
+                     s.n_active, s.src_rows, s.err, chunk, s.items, s.n_items, s.blk, st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
   if (path == kPathGemm) {
     e = launch_gather_border(x, dm.d, dm.d, s.src_rows, s.offsets + dm.E + 1, P + Ts, s.xb, st);
@@ -489,7 +491,7 @@ int vx_gather_qmm(const uint16_t* x, int64_t x_rows, const vx_q4* w, const int32
   if (e == cudaSuccess) e = launch_gather_items(lhs, rhs, B, M, x_rows, keys, src_map, st);
   if (e == cudaSuccess)
     e = launch_permute(keys, n, E, 0, 1, src_map, order, inverse, offsets, active, n_active, src_rows,
-                       err, kItemChunk, items, n_items, st);
+                       err, kItemChunk, items, n_items, nullptr, st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
   MmaArgs a{};
   a.b0 = *w;
@@ -573,6 +575,7 @@ size_t vx_permute_workspace(int64_t P, int32_t E) {
   Carver c(nullptr);
   c.take<int32_t>(E + 1);
   c.take<int32_t>(1);
+  c.take<int32_t>(permute_scratch_ints(P, E));   // per-slice counts (large P)
   return c.size();
 }
 
@@ -586,9 +589,10 @@ int vx_permute(const int32_t* ids, int64_t P, int32_t E, int32_t* order, int32_t
   Carver c(workspace);
   int32_t* active = c.take<int32_t>(E + 1);
   int32_t* n_active = c.take<int32_t>(1);
+  int32_t* blk = c.take<int32_t>(permute_scratch_ints(P, E));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = launch_permute(ids, P, E, -1, 1, nullptr, order, inverse, offsets, active, n_active,
-                                 nullptr, error_count, kItemChunk, nullptr, nullptr, st);
+                                 nullptr, error_count, kItemChunk, nullptr, nullptr, blk, st);
   return e == cudaSuccess ? VX_OK : vx_cuda_fail(e);
 }
 

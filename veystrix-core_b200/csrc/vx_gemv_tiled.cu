@@ -83,6 +83,30 @@ VX_DEVICE void issue_stage(bool leader, uint32_t bar, uint32_t dst_w, const void
       : "memory");
 }
 
+// Lane 0 arms the stage's mbarrier for the activation copy alone and issues
+// it (the weights travel by per-lane cp.async, see below).
+VX_DEVICE void issue_act(bool leader, uint32_t bar, uint32_t dst_x, const void* src_x, uint32_t nx,
+                         uint64_t pol_x) {
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "setp.ne.b32 p, %0, 0;\n"
+      "@p fence.proxy.async.shared::cta;\n"
+      "@p mbarrier.arrive.expect_tx.shared::cta.b64 _, [%1], %2;\n"
+      "@p cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%3], [%4], %2, "
+      "[%1], %5;\n"
+      "}\n" ::"r"(int(leader)),
+      "r"(bar), "r"(nx), "r"(dst_x), "l"(src_x), "l"(pol_x)
+      : "memory");
+}
+
+// The weight records travel through the load/store units (each lane copies
+// 16-byte pieces with cp.async) while the small activation records use the
+// bulk-copy engine: one SM's bulk-copy (TMA) engine alone sustains about 14
+// bytes per cycle - about 4 TB/s over the chip - below what HBM delivers,
+// so the heavy stream goes the other way.
+constexpr bool kWeightsByLsu = true;
+
 template <bool GATEUP, int MT, bool XMMA, int STAGES>
 __global__ void __launch_bounds__(kTiledThreads, 2) gemv_tiled_kernel(const __grid_constant__ TiledArgs a) {
   constexpr int NP = GATEUP ? 2 : 1;
@@ -136,8 +160,16 @@ __global__ void __launch_bounds__(kTiledThreads, 2) gemv_tiled_kernel(const __gr
   bool timed_out = false;
   auto issue = [&]() {
     const uint32_t st = ring + st_issue * kStage;
-    issue_stage(lane == 0, bar0 + 8 * st_issue, st, irec + int64_t(ci) * kRec, kRec, pol_w, st + kXOff,
-                iact + int64_t(ci) * act_pitch, ixbytes, pol_x);
+    if (kWeightsByLsu) {
+      const unsigned char* src = irec + int64_t(ci) * kRec + lane * 16;
+#pragma unroll
+      for (int j = 0; j < (kRec + 511) / 512; ++j)
+        cp16_if(st + j * 512 + lane * 16, src + j * 512, 16, j * 512 + lane * 16 < kRec);
+      issue_act(lane == 0, bar0 + 8 * st_issue, st + kXOff, iact + int64_t(ci) * act_pitch, ixbytes, pol_x);
+    } else {
+      issue_stage(lane == 0, bar0 + 8 * st_issue, st, irec + int64_t(ci) * kRec, kRec, pol_w, st + kXOff,
+                  iact + int64_t(ci) * act_pitch, ixbytes, pol_x);
+    }
     st_issue = st_issue == STAGES - 1 ? 0 : st_issue + 1;
     if (++ci == inch) {
       ci = 0;
@@ -148,8 +180,10 @@ __global__ void __launch_bounds__(kTiledThreads, 2) gemv_tiled_kernel(const __gr
 
   seek();
 #pragma unroll
-  for (int s = 0; s < STAGES - 1; ++s)
+  for (int s = 0; s < STAGES - 1; ++s) {
     if (ti < total) issue();
+    cp_commit();   // one cp.async group per unit, empty ones included
+  }
 
   // ---- consumer: tasks in the same order ----
   auto run = [&](const TiledTask& k, auto nq_tag) {
@@ -172,7 +206,12 @@ __global__ void __launch_bounds__(kTiledThreads, 2) gemv_tiled_kernel(const __gr
     const int nch = (k.K + 127) >> 7;
     for (int ch = 0; ch < nch; ++ch) {
       if (ti < total) issue();
+      cp_commit();
       const uint32_t st = ring + st_use * kStage;
+      if (kWeightsByLsu) {
+        cp_wait<STAGES - 1>();   // this unit's weight pieces (every lane's)
+        __syncwarp();
+      }
       if (!mbar_wait(bar0 + 8 * st_use, (parity_bits >> st_use) & 1u)) timed_out = true;
       parity_bits ^= 1u << st_use;
 
@@ -302,6 +341,7 @@ __global__ void __launch_bounds__(kTiledThreads, 2) gemv_tiled_kernel(const __gr
     else
       run(k, std::integral_constant<int, 1>());
   }
+  cp_wait<0>();
   if (timed_out && a.err) atomicOr(a.err, 0x100);
 }
 

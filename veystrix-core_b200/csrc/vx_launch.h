@@ -152,11 +152,14 @@ inline int max_items_bound(int64_t P, int E, int Ts) {
 
 int sm_count();
 
+// Stable sort by expert.  blk: scratch of permute_scratch_ints(P, E) ints
+// (null or zero-sized: the one-CTA variant regardless of P).
 cudaError_t launch_permute(const int32_t* ids, int64_t P, int E, int shared_items, int k_div,
                            const int32_t* src_map, int32_t* order, int32_t* inverse,
                            int32_t* offsets, int32_t* active, int32_t* n_active,
                            int32_t* src_rows, int32_t* err, int item_chunk, int32_t* items,
-                           int32_t* n_items, cudaStream_t st);
+                           int32_t* n_items, int32_t* blk, cudaStream_t st);
+int64_t permute_scratch_ints(int64_t P, int E);
 
 cudaError_t launch_router_logits(const uint16_t* x, int T, const uint16_t* wg, int E, int K,
                                  uint16_t* logits, cudaStream_t st);

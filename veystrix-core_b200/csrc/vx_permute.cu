@@ -2,12 +2,19 @@
 // _gather_sort/_scatter_unsort (called at models/flashnext/expert_cache.py:
 // 2017-2037), which is a stable argsort of the flat expert ids.
 //
-// One CTA: a counting pass (shared-memory histogram), an exclusive scan into
-// run offsets, then a stable scatter in chunks of blockDim items.  Inside a
-// chunk, __match_any_sync groups lanes by expert; the rank of an item is its
-// rank among equal lanes of its warp, plus the items of lower warps in the
-// chunk with the same expert, plus the items of earlier chunks.  The result
-// depends only on the ids, never on scheduling.
+// Three phases: a counting pass (shared-memory histogram), an exclusive scan
+// into run offsets (plus the active-expert list and the work-item table of
+// the grouped kernels), then a stable scatter in chunks of blockDim items.
+// Inside a chunk, __match_any_sync groups lanes by expert; the rank of an item
+// is its rank among equal lanes of its warp, plus the items of lower warps in
+// the chunk with the same expert, plus the items placed before the chunk.
+// The result depends only on the ids, never on scheduling.
+//
+// Decode-sized inputs run all three phases in one CTA.  Prefill-sized inputs
+// (more than kPermMultiMin ids) split the ids into slices of kPermSlice: one
+// CTA per slice counts, one CTA scans the per-slice counts into per-slice
+// starting positions (slice order = flat order, so the sort stays stable),
+// and one CTA per slice scatters.
 #include "vx_common.cuh"
 #include "vx_launch.h"
 
@@ -42,36 +49,27 @@ __device__ int block_exclusive_scan(int v, int* warp_tot) {
   return r;
 }
 
-// ids [P]; expert E (if shared_items > 0) is appended with shared_items items
-// whose x rows are 0..shared_items-1.  shared_items < 0 means offsets has
-// only E+1 entries.
-__global__ void __launch_bounds__(kPermThreads) permute_kernel(
-    const int32_t* __restrict__ ids, int P, int E, int shared_items, int k_div,
-    const int32_t* __restrict__ src_map, int32_t* __restrict__ order,
-    int32_t* __restrict__ inverse, int32_t* __restrict__ offsets, int32_t* __restrict__ active,
-    int32_t* __restrict__ n_active, int32_t* __restrict__ src_rows, int32_t* __restrict__ err,
-    int item_chunk, int32_t* __restrict__ items, int32_t* __restrict__ n_items) {
-  extern __shared__ int smem[];
-  int* counts = smem;                         // [E]
-  int* base = counts + E;                     // [E]  run start
-  int* running = base + E;                    // [E]  items placed so far
-  int* hist = running + E;                    // [kPermWarps][E]
-  __shared__ int warp_tot[32];
-  __shared__ int s_bad;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-
-  for (int e = tid; e < E; e += kPermThreads) counts[e] = running[e] = 0;
-  for (int i = tid; i < kPermWarps * E; i += kPermThreads) hist[i] = 0;
-  if (tid == 0) s_bad = 0;
-  __syncthreads();
-  for (int i = tid; i < P; i += kPermThreads) {
+// Histogram of ids[lo, hi) into counts[E] (shared, zeroed by the caller);
+// returns the number of ids outside [0, E) (block-wide, valid on all threads
+// after the call).
+__device__ int perm_count(const int32_t* ids, int64_t lo, int64_t hi, int E, int* counts, int* s_bad) {
+  for (int64_t i = lo + threadIdx.x; i < hi; i += kPermThreads) {
     const int id = ids[i];
     if (id >= 0 && id < E) atomicAdd(&counts[id], 1);
-    else atomicAdd(&s_bad, 1);
+    else atomicAdd(s_bad, 1);
   }
   __syncthreads();
+  return *s_bad;
+}
 
-  // Exclusive scan of counts and of the "has items" flags, E <= 4 per thread.
+// From counts[E] (shared): base[e] = offsets[e] (run starts), the active
+// list, offsets[E] (and offsets[E+1] with the shared run), the shared run's
+// src_rows, and the work-item table.  Returns the number of routed items.
+__device__ int perm_offsets(int E, int shared_items, const int* counts, int* base, int* warp_tot,
+                            int32_t* offsets, int32_t* active, int32_t* n_active, int32_t* src_rows,
+                            int item_chunk, int32_t* items, int32_t* n_items) {
+  const int tid = threadIdx.x;
+  __shared__ int tot_c, tot_a, tot_i;
   int carry = 0, acarry = 0;
   for (int e0 = 0; e0 < E; e0 += kPermThreads) {
     const int e = e0 + tid;
@@ -84,9 +82,10 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(
       offsets[e] = carry + ex;
       if (f) active[acarry + ax] = e;
     }
-    // totals of this slice
-    __shared__ int tot_c, tot_a;
-    if (tid == kPermThreads - 1) { tot_c = ex + c; tot_a = ax + f; }
+    if (tid == kPermThreads - 1) {
+      tot_c = ex + c;
+      tot_a = ax + f;
+    }
     __syncthreads();
     carry += tot_c;
     acarry += tot_a;
@@ -99,11 +98,9 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(
     int na = acarry;
     if (shared_items > 0) active[na++] = E;
     *n_active = na;
-    if (err && s_bad) atomicAdd(err, s_bad);
   }
-  for (int t = tid; t < shared_items; t += kPermThreads) {
+  for (int t = tid; t < shared_items; t += kPermThreads)
     if (src_rows) src_rows[carry + t] = t;
-  }
 
   // Work items for the grouped kernels: each expert's run cut into chunks of
   // at most item_chunk positions, in expert order: {expert, first, count}.
@@ -126,7 +123,6 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(
         it[1] = first + j * item_chunk;
         it[2] = min(item_chunk, n - j * item_chunk);
       }
-      __shared__ int tot_i;
       if (tid == kPermThreads - 1) tot_i = ex + nch;
       __syncthreads();
       icarry += tot_i;
@@ -134,12 +130,19 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(
     }
     if (tid == 0) *n_items = icarry;
   }
+  return carry;
+}
 
-  // Stable scatter.
-  for (int c0 = 0; c0 < P; c0 += kPermThreads) {
-    const int i = c0 + tid;
+// Stable scatter of ids[lo, hi): running[e] (shared) holds the next position
+// of expert e; hist is [kPermWarps][E] shared scratch, zeroed.
+__device__ void perm_scatter(const int32_t* ids, int64_t lo, int64_t hi, int E, int k_div,
+                             const int32_t* src_map, int* running, int* hist, int32_t* order,
+                             int32_t* inverse, int32_t* src_rows) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int64_t c0 = lo; c0 < hi; c0 += kPermThreads) {
+    const int64_t i = c0 + tid;
     int key = -1;
-    if (i < P) {
+    if (i < hi) {
       key = ids[i];
       if (key < 0 || key >= E) {
         key = -1;
@@ -154,10 +157,10 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(
     if (key >= 0) {
       int before = running[key];
       for (int w = 0; w < warp; ++w) before += hist[w * E + key];
-      const int pos = base[key] + before + rank;
-      order[pos] = i;
+      const int pos = before + rank;
+      order[pos] = int32_t(i);
       inverse[i] = pos;
-      if (src_rows) src_rows[pos] = src_map ? src_map[i] : i / k_div;
+      if (src_rows) src_rows[pos] = src_map ? src_map[i] : int32_t(i / k_div);
     }
     __syncthreads();
     if (key >= 0 && leader) {
@@ -168,20 +171,133 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(
   }
 }
 
+// ids [P]; expert E (if shared_items > 0) is appended with shared_items items
+// whose x rows are 0..shared_items-1.  shared_items < 0 means offsets has
+// only E+1 entries.
+__global__ void __launch_bounds__(kPermThreads) permute_kernel(
+    const int32_t* __restrict__ ids, int P, int E, int shared_items, int k_div,
+    const int32_t* __restrict__ src_map, int32_t* __restrict__ order,
+    int32_t* __restrict__ inverse, int32_t* __restrict__ offsets, int32_t* __restrict__ active,
+    int32_t* __restrict__ n_active, int32_t* __restrict__ src_rows, int32_t* __restrict__ err,
+    int item_chunk, int32_t* __restrict__ items, int32_t* __restrict__ n_items) {
+  extern __shared__ int smem[];
+  int* counts = smem;                         // [E]
+  int* base = counts + E;                     // [E]  run start
+  int* hist = base + E;                       // [kPermWarps][E]
+  __shared__ int warp_tot[32];
+  __shared__ int s_bad;
+  const int tid = threadIdx.x;
+  for (int e = tid; e < E; e += kPermThreads) counts[e] = 0;
+  for (int i = tid; i < kPermWarps * E; i += kPermThreads) hist[i] = 0;
+  if (tid == 0) s_bad = 0;
+  __syncthreads();
+  const int bad = perm_count(ids, 0, P, E, counts, &s_bad);
+  if (tid == 0 && err && bad) atomicAdd(err, bad);
+  perm_offsets(E, shared_items, counts, base, warp_tot, offsets, active, n_active, src_rows, item_chunk,
+               items, n_items);
+  __syncthreads();
+  perm_scatter(ids, 0, P, E, k_div, src_map, base, hist, order, inverse, src_rows);
+}
+
+// ---- prefill-sized inputs: slices of kPermSlice ids -------------------------
+
+constexpr int kPermSlice = 8192;
+constexpr int64_t kPermMultiMin = 16384;
+
+int64_t permute_scratch_ints(int64_t P, int E) {
+  if (P <= kPermMultiMin) return 0;
+  return ((P + kPermSlice - 1) / kPermSlice) * int64_t(E);
+}
+
+__global__ void __launch_bounds__(kPermThreads) permute_count_kernel(const int32_t* __restrict__ ids,
+                                                                     int64_t P, int E, int32_t* __restrict__ blk,
+                                                                     int32_t* __restrict__ err) {
+  extern __shared__ int counts[];
+  __shared__ int s_bad;
+  for (int e = threadIdx.x; e < E; e += kPermThreads) counts[e] = 0;
+  if (threadIdx.x == 0) s_bad = 0;
+  __syncthreads();
+  const int64_t lo = int64_t(blockIdx.x) * kPermSlice;
+  const int64_t hi = lo + kPermSlice < P ? lo + kPermSlice : P;
+  const int bad = perm_count(ids, lo, hi, E, counts, &s_bad);
+  for (int e = threadIdx.x; e < E; e += kPermThreads) blk[int64_t(blockIdx.x) * E + e] = counts[e];
+  if (threadIdx.x == 0 && err && bad) atomicAdd(err, bad);
+}
+
+// One CTA: totals per expert, offsets and items, then each slice's starting
+// position per expert (earlier slices first).
+__global__ void __launch_bounds__(kPermThreads) permute_scan_kernel(
+    int nb, int E, int shared_items, int32_t* __restrict__ blk, int32_t* __restrict__ offsets,
+    int32_t* __restrict__ active, int32_t* __restrict__ n_active, int32_t* __restrict__ src_rows,
+    int item_chunk, int32_t* __restrict__ items, int32_t* __restrict__ n_items) {
+  extern __shared__ int smem[];
+  int* counts = smem;           // [E]
+  int* base = counts + E;       // [E]
+  __shared__ int warp_tot[32];
+  for (int e = threadIdx.x; e < E; e += kPermThreads) {
+    int run = 0;
+    for (int b = 0; b < nb; ++b) {
+      const int c = blk[int64_t(b) * E + e];
+      blk[int64_t(b) * E + e] = run;      // start of slice b inside expert e's run
+      run += c;
+    }
+    counts[e] = run;
+  }
+  __syncthreads();
+  perm_offsets(E, shared_items, counts, base, warp_tot, offsets, active, n_active, src_rows, item_chunk,
+               items, n_items);
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += kPermThreads)
+    for (int b = 0; b < nb; ++b) blk[int64_t(b) * E + e] += base[e];
+}
+
+__global__ void __launch_bounds__(kPermThreads) permute_scatter_kernel(
+    const int32_t* __restrict__ ids, int64_t P, int E, int k_div, const int32_t* __restrict__ src_map,
+    const int32_t* __restrict__ blk, int32_t* __restrict__ order, int32_t* __restrict__ inverse,
+    int32_t* __restrict__ src_rows) {
+  extern __shared__ int smem[];
+  int* running = smem;          // [E]
+  int* hist = running + E;      // [kPermWarps][E]
+  for (int e = threadIdx.x; e < E; e += kPermThreads) running[e] = blk[int64_t(blockIdx.x) * E + e];
+  for (int i = threadIdx.x; i < kPermWarps * E; i += kPermThreads) hist[i] = 0;
+  __syncthreads();
+  const int64_t lo = int64_t(blockIdx.x) * kPermSlice;
+  const int64_t hi = lo + kPermSlice < P ? lo + kPermSlice : P;
+  perm_scatter(ids, lo, hi, E, k_div, src_map, running, hist, order, inverse, src_rows);
+}
+
+static cudaError_t set_smem(const void* fn, size_t smem) {
+  if (smem <= 48 * 1024) return cudaSuccess;
+  return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+}
+
 cudaError_t launch_permute(const int32_t* ids, int64_t P, int E, int shared_items, int k_div,
                            const int32_t* src_map, int32_t* order, int32_t* inverse,
                            int32_t* offsets, int32_t* active, int32_t* n_active,
                            int32_t* src_rows, int32_t* err, int item_chunk, int32_t* items,
-                           int32_t* n_items, cudaStream_t st) {
-  const size_t smem = size_t(E) * (3 + kPermWarps) * sizeof(int);
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         int(smem));
+                           int32_t* n_items, int32_t* blk, cudaStream_t st) {
+  if (P <= kPermMultiMin || blk == nullptr) {
+    const size_t smem = size_t(E) * (2 + kPermWarps) * sizeof(int);
+    cudaError_t e = set_smem(reinterpret_cast<const void*>(permute_kernel), smem);
     if (e != cudaSuccess) return e;
+    permute_kernel<<<1, kPermThreads, smem, st>>>(ids, int(P), E, shared_items, k_div, src_map, order,
+                                                  inverse, offsets, active, n_active, src_rows, err,
+                                                  item_chunk, items, n_items);
+    return cudaGetLastError();
   }
-  permute_kernel<<<1, kPermThreads, smem, st>>>(ids, int(P), E, shared_items, k_div, src_map, order,
-                                                inverse, offsets, active, n_active, src_rows, err,
-                                                item_chunk, items, n_items);
+  const int nb = int((P + kPermSlice - 1) / kPermSlice);
+  permute_count_kernel<<<nb, kPermThreads, size_t(E) * sizeof(int), st>>>(ids, P, E, blk, err);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  permute_scan_kernel<<<1, kPermThreads, size_t(E) * 2 * sizeof(int), st>>>(
+      nb, E, shared_items, blk, offsets, active, n_active, src_rows, item_chunk, items, n_items);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const size_t smem = size_t(E) * (1 + kPermWarps) * sizeof(int);
+  e = set_smem(reinterpret_cast<const void*>(permute_scatter_kernel), smem);
+  if (e != cudaSuccess) return e;
+  permute_scatter_kernel<<<nb, kPermThreads, smem, st>>>(ids, P, E, k_div, src_map, blk, order, inverse,
+                                                          src_rows);
   return cudaGetLastError();
 }
 
