@@ -48,6 +48,8 @@ def parse():
     ap.add_argument("--tokens", type=int, default=64)
     ap.add_argument("--pools", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="launch the block's kernels one by one instead of replaying a CUDA graph")
     ap.add_argument("--layout", default="tiled", choices=("tiled", "mlx"),
                     help="expert weights as the tiled resident pool (default) or the MLX arrays")
     return ap.parse_args()
@@ -75,8 +77,8 @@ def stage_bytes(stage, U, T):
         return (U + 1) * 2 * PROJ_BYTES + T * HIDDEN * 2 + (P + T) * INTER * 2
     if stage == "down":
         return (U + 1) * PROJ_BYTES + (P + T) * INTER * 2 + (P + T) * HIDDEN * 2
-    if stage == "router_logits":
-        return ROUTER_BYTES + T * HIDDEN * 2 + T * EXPERTS * 2
+    if stage == "router":
+        return ROUTER_BYTES + SHARED_GATE_BYTES + T * HIDDEN * 2 + T * EXPERTS * 2
     return None
 
 
@@ -196,6 +198,8 @@ def config_dict(args, world):
         "parallelism": (f"ep{world}: {EXPERTS // world} experts per GPU, NCCL all-to-all "
                         f"dispatch/combine" if world > 1 else "single GPU, all experts resident"),
         "l2": f"inputs larger than L2: {args.pools} rotating weight pools of {EXPERTS} experts",
+        "launch": ("one CUDA graph per weight pool (x copied into the graph's input buffer each step)"
+                   if world == 1 and not args.no_graph else "kernels launched one by one"),
         "weight_layout": ("tiled resident pool (packed once at load)" if args.layout == "tiled"
                           else "MLX arrays"),
     }
@@ -233,7 +237,7 @@ def main():
     K, W = args.steps, max(3, args.warmup)
     g = torch.Generator(device=dev)
     gr = torch.Generator(device=dev)
-    pools, layers = [], []
+    pools, layers, plain = [], [], []
     for i in range(args.pools):
         g.manual_seed(1000 * rank + i)
         gr.manual_seed(5000 + i)          # router and shared expert: the same on every rank
@@ -243,7 +247,9 @@ def main():
             if args.layout == "tiled":
                 w.pack()
             pools.append(w)
-            layers.append(lambda x, w=w: vxmoe.moe_block(x, w))
+            plain.append(lambda x, w=w: vxmoe.moe_block(x, w))
+            # one CUDA graph per weight pool: the block's launches replay as one
+            layers.append(plain[-1] if args.no_graph else vxmoe.GraphedBlock(w, T))
         else:
             # expert parallel: this rank holds experts [rank*E/N, (rank+1)*E/N)
             from vxmoe.ep import ExpertParallelMoE
@@ -254,11 +260,14 @@ def main():
                 w.pack()
             pools.append(w)
             layers.append(ExpertParallelMoE(w, EXPERTS))
+            plain.append(layers[-1])
     g.manual_seed(7 + rank)
     nx = K + W
     xs = (torch.randn((nx, T, HIDDEN), device=dev, generator=g)).to(torch.bfloat16)
     torch.cuda.synchronize()
-    launches_per_step = 8 if world == 1 else 13
+    # our kernels per step: router, permute, activation records, gate/up, down, combine
+    # (EP adds the shared expert's own pass)
+    launches_per_step = 6 if world == 1 else 11
 
     def step(i):
         return layers[i % len(layers)](xs[i])
@@ -332,7 +341,7 @@ def main():
     # per-kernel durations: the same steps again with stage events
     _lib.profile_enable(True)
     for i in range(K):
-        step(W + i)
+        plain[(W + i) % len(plain)](xs[W + i])
     stages = _lib.profile_read()
     _lib.profile_enable(False)
     barrier()

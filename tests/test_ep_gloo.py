@@ -56,7 +56,7 @@ class OracleBackend:
         return torch.from_numpy(shared).to(torch.bfloat16)
 
 
-def _worker(rank, world, port, q, fail_rank):
+def _worker(rank, world, port, q, fail_rank, mode="capacity"):
     try:
         import torch.distributed as dist
         from vxmoe.ep import ExpertParallelMoE
@@ -71,6 +71,8 @@ def _worker(rank, world, port, q, fail_rank):
             top_k = K
 
         ep = ExpertParallelMoE(_Shard(), E, backend=backend)
+        if mode == "counts":
+            ep.capacity_max_tokens = 0          # force the count-based exchange
         x = O.make_x(100 + rank, 6, D)
         y = ep(torch.from_numpy(x).to(torch.bfloat16))
         q.put((rank, "ok", y.float().numpy(), x, ep.last_stats))
@@ -80,10 +82,10 @@ def _worker(rank, world, port, q, fail_rank):
         q.put((rank, "error", repr(exc), traceback.format_exc(), None))
 
 
-def _run(world, port, fail_rank=-1, timeout=120):
+def _run(world, port, fail_rank=-1, timeout=120, mode="capacity"):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, fail_rank)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, fail_rank, mode)) for r in range(world)]
     for pr in procs:
         pr.start()
     out = {}
@@ -97,17 +99,27 @@ def _run(world, port, fail_rank=-1, timeout=120):
     return out
 
 
-def test_ep_two_ranks_matches_single_process_oracle():
-    out = _run(2, 29631)
+@pytest.mark.parametrize("mode,port", [("capacity", 29631), ("counts", 29636)])
+def test_ep_two_ranks_matches_single_process_oracle(mode, port):
+    out = _run(2, port, mode=mode)
     p = O.make_params(seed=3, experts=E, hidden=D, inter=I, shared_inter=I, top_k=K)
     for rank in range(2):
         status, y, x, stats = out[rank]
         assert status == "ok", x
+        assert stats["mode"] == mode
         ref = O.moe_block(x, p).y
         assert O.normwise_error(y, ref) < 1e-2
         assert np.mean(O.bf16_bits(y) == O.bf16_bits(ref)) > 0.95
-        assert sum(stats["send_counts"]) == stats["sent_rows"]
-        assert stats["sent_rows"] <= 6 * 2          # one row per (token, destination)
+        if mode == "counts":
+            assert sum(stats["send_counts"]) == stats["sent_rows"]
+            assert stats["sent_rows"] <= 6 * 2      # one row per (token, destination)
+
+
+def test_ep_exchange_modes_agree_bit_for_bit():
+    a = _run(2, 29646, mode="capacity")
+    b = _run(2, 29651, mode="counts")
+    for rank in range(2):
+        np.testing.assert_array_equal(O.bf16_bits(a[rank][1]), O.bf16_bits(b[rank][1]))
 
 
 def test_ep_failing_rank_does_not_hang_its_peer():

@@ -524,25 +524,23 @@ int vx_softmax_topk(const uint16_t* logits, int32_t T, int32_t E, int32_t k, int
 size_t vx_router_workspace(int32_t T, const vx_moe_weights* W) {
   if (!W || T < 0) return 0;
   Carver c(nullptr);
-  c.take<uint16_t>(int64_t(T) * W->num_experts);
+  c.take<uint16_t>(int64_t(T) * W->num_experts);   // logits (when the caller passes none)
+  c.take<int32_t>((int64_t(T) + 7) / 8);           // arrival counters of the fused router
   return c.size();
 }
 
+// One launch: logits, top-k and renorm by the last CTA of each token block,
+// and the shared-expert gate (vx_router.cu router_fused_kernel).
 static int router_impl(const uint16_t* x, int T, const vx_moe_weights* W, const BlockDims& dm,
                        uint16_t* logits, int32_t* inds, uint16_t* weights, uint16_t* sg,
-                       cudaStream_t st) {
+                       int32_t* counters, cudaStream_t st) {
   profile_mark(st, "");
-  cudaError_t e = launch_router_logits(x, T, W->router_w, dm.E, dm.d, logits, st);
+  const bool gate = sg && W->shared_expert_gate.w;
+  cudaError_t e = launch_router_fused(x, T, W->router_w, dm.E, dm.d, dm.k,
+                                      gate ? &W->shared_expert_gate : nullptr, logits, inds, weights,
+                                      gate ? sg : nullptr, counters, st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
-  profile_mark(st, "router_logits");
-  e = launch_softmax_topk(logits, T, dm.E, dm.k, inds, nullptr, weights, nullptr, st);
-  if (e != cudaSuccess) return vx_cuda_fail(e);
-  profile_mark(st, "softmax_topk");
-  if (sg && W->shared_expert_gate.w) {
-    e = launch_shared_gate(x, T, W->shared_expert_gate, sg, st);
-    if (e != cudaSuccess) return vx_cuda_fail(e);
-    profile_mark(st, "shared_gate");
-  }
+  profile_mark(st, "router");
   return VX_OK;
 }
 
@@ -563,12 +561,12 @@ int vx_router(const uint16_t* x, int32_t T, const vx_moe_weights* W, uint16_t* l
   if (T < 0) return VX_EINVAL_SHAPE;
   if (T == 0) return VX_OK;
   if (!x || !inds || !weights || !aligned16(x)) return VX_EINVAL_SHAPE;
-  if (!logits) {
-    if (!workspace || workspace_bytes < vx_router_workspace(T, W)) return VX_EWORKSPACE;
-    Carver c(workspace);
-    logits = c.take<uint16_t>(int64_t(T) * dm.E);
-  }
-  return router_impl(x, T, W, dm, logits, inds, weights, sg, static_cast<cudaStream_t>(stream));
+  if (!workspace || workspace_bytes < vx_router_workspace(T, W)) return VX_EWORKSPACE;
+  Carver c(workspace);
+  uint16_t* lg = c.take<uint16_t>(int64_t(T) * dm.E);
+  int32_t* counters = c.take<int32_t>((int64_t(T) + 7) / 8);
+  if (!logits) logits = lg;
+  return router_impl(x, T, W, dm, logits, inds, weights, sg, counters, static_cast<cudaStream_t>(stream));
 }
 
 size_t vx_permute_workspace(int64_t P, int32_t E) {
@@ -673,6 +671,7 @@ size_t vx_moe_block_workspace(int32_t T, const vx_moe_weights* W) {
   c.take<int32_t>(int64_t(T) * dm.k);    // inds
   c.take<uint16_t>(int64_t(T) * dm.k);   // weights
   c.take<uint16_t>(T);                   // sg
+  c.take<int32_t>((int64_t(T) + 7) / 8);  // router arrival counters
   carve_experts(c, T, dm);
   return c.size();
 }
@@ -692,10 +691,11 @@ int vx_moe_block(const uint16_t* x, int32_t T, const vx_moe_weights* W, uint16_t
   int32_t* inds_ws = c.take<int32_t>(int64_t(T) * dm.k);
   uint16_t* w_ws = c.take<uint16_t>(int64_t(T) * dm.k);
   uint16_t* sg = c.take<uint16_t>(T);
+  int32_t* counters = c.take<int32_t>((int64_t(T) + 7) / 8);
   ExpertScratch es = carve_experts(c, T, dm);
   if (!inds) inds = inds_ws;
   if (!weights) weights = w_ws;
-  s = router_impl(x, T, W, dm, logits, inds, weights, dm.shared ? sg : nullptr, st);
+  s = router_impl(x, T, W, dm, logits, inds, weights, dm.shared ? sg : nullptr, counters, st);
   if (s) return s;
   s = run_experts(x, T, inds, W, dm, es, st);
   if (s) return s;

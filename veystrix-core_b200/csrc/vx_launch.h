@@ -168,6 +168,11 @@ cudaError_t launch_shared_gate(const uint16_t* x, int T, const vx_q4& seg, uint1
 cudaError_t launch_softmax_topk(const uint16_t* logits, int T, int E, int k, int32_t* inds,
                                 uint16_t* scores, uint16_t* weights, uint16_t* mass,
                                 cudaStream_t st);
+// Logits, top-k/renorm and (seg != null) the shared-expert gate in one
+// launch; counters: (T+7)/8 ints of scratch (zeroed by the launcher).
+cudaError_t launch_router_fused(const uint16_t* x, int T, const uint16_t* wg, int E, int K, int k,
+                                const vx_q4* seg, uint16_t* logits, int32_t* inds, uint16_t* weights,
+                                uint16_t* sg, int32_t* counters, cudaStream_t st);
 
 // Combine modes for the shared part.
 enum SharedMode { kSharedNone = 0, kSharedInternal = 1, kSharedY = 2, kSharedParts = 3 };

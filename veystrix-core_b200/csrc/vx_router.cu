@@ -11,6 +11,8 @@
 // The kernel ranks by the bf16 logit, then the lower expert id.  Softmax is
 // monotone, so this is always a valid top-k of the probabilities and it does
 // not depend on how exp rounds.
+#include <type_traits>
+
 #include "vx_common.cuh"
 #include "vx_launch.h"
 
@@ -111,24 +113,20 @@ cudaError_t launch_shared_gate(const uint16_t* x, int T, const vx_q4& seg, uint1
 }
 
 // ---- softmax + top-k + renorm: one warp per token --------------------------
-constexpr int kMaxK = 16;
+// Register-only: lane r keeps the r-th selection.  The selection sum runs in
+// slot order on every lane, as the reference's mass reduction does.
+constexpr int kMaxK = 32;
 
-template <int PER>
-__global__ void __launch_bounds__(256) softmax_topk_kernel(const uint16_t* __restrict__ logits,
-                                                           int T, int E, int k,
-                                                           int32_t* __restrict__ inds,
-                                                           uint16_t* __restrict__ scores,
-                                                           uint16_t* __restrict__ weights,
-                                                           uint16_t* __restrict__ mass) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x * 8 + warp;
-  if (t >= T) return;
-  const uint16_t* lr = logits + int64_t(t) * E;
+template <int PER, bool COHERENT>
+__device__ __forceinline__ void topk_row(const uint16_t* lr, int E, int k, int32_t* inds, uint16_t* scores,
+                                         uint16_t* weights, uint16_t* mass) {
+  const int lane = threadIdx.x & 31;
   float l[PER];
 #pragma unroll
   for (int j = 0; j < PER; ++j) {
     const int e = lane + 32 * j;
-    l[j] = e < E ? bf16_to_f32(lr[e]) : -INFINITY;
+    // logits written by other CTAs of the same launch are read past L1
+    l[j] = e < E ? bf16_to_f32(COHERENT ? __ldcg(lr + e) : lr[e]) : -INFINITY;
   }
   float m = -INFINITY;
 #pragma unroll
@@ -145,8 +143,8 @@ __global__ void __launch_bounds__(256) softmax_topk_kernel(const uint16_t* __res
   const float inv = __fdiv_rn(1.0f, s);
 
   uint32_t taken = 0;
-  int sel_i[kMaxK];
-  float sel_p[kMaxK];
+  int my_i = 0;
+  float my_p = 0.f, tot = 0.f;
   for (int r = 0; r < k; ++r) {
     float bv = -INFINITY;
     int bi = 0x7FFFFFFF;
@@ -174,43 +172,167 @@ __global__ void __launch_bounds__(256) softmax_topk_kernel(const uint16_t* __res
       if (j == jj) mine = ex[j];
     const float ew = __shfl_sync(0xFFFFFFFFu, mine, owner);
     if (lane == owner) taken |= 1u << jj;
-    if (r < kMaxK) {
-      sel_i[r] = bi;
-      sel_p[r] = bf16r(__fmul_rn(ew, inv));
+    const float pr = bf16r(__fmul_rn(ew, inv));
+    tot = __fadd_rn(tot, pr);
+    if (lane == r) {
+      my_i = bi;
+      my_p = pr;
     }
   }
   // mass and renorm (blend 1.0): norm = mass + 1.0*(sum - mass), in bf16.
-  float tot = 0.f;
-  for (int r = 0; r < k; ++r) tot = __fadd_rn(tot, sel_p[r]);
   const float msum = bf16r(tot);
-  const float sel_sum = msum;
-  const float diff = bf16r(__fsub_rn(sel_sum, msum));
+  const float diff = bf16r(__fsub_rn(msum, msum));
   const float norm = bf16r(__fadd_rn(msum, bf16r(diff)));
-  for (int r = lane; r < k; r += 32) {
-    float p = 0.f;
-    int id = 0;
-    for (int q = 0; q < k; ++q)
-      if (q == r) {
-        p = sel_p[q];
-        id = sel_i[q];
-      }
-    inds[int64_t(t) * k + r] = id;
-    if (scores) scores[int64_t(t) * k + r] = f32_to_bf16(p);
-    weights[int64_t(t) * k + r] = f32_to_bf16(bf16r(__fdiv_rn(p, norm)));
+  if (lane < k) {
+    inds[lane] = my_i;
+    if (scores) scores[lane] = f32_to_bf16(my_p);
+    weights[lane] = f32_to_bf16(bf16r(__fdiv_rn(my_p, norm)));
   }
-  if (mass && lane == 0) mass[t] = f32_to_bf16(msum);
+  if (mass && lane == 0) *mass = f32_to_bf16(msum);
+}
+
+template <int PER>
+__global__ void __launch_bounds__(256) softmax_topk_kernel(const uint16_t* __restrict__ logits,
+                                                           int T, int E, int k,
+                                                           int32_t* __restrict__ inds,
+                                                           uint16_t* __restrict__ scores,
+                                                           uint16_t* __restrict__ weights,
+                                                           uint16_t* __restrict__ mass) {
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t >= T) return;
+  topk_row<PER, false>(logits + int64_t(t) * E, E, k, inds + int64_t(t) * k,
+                       scores ? scores + int64_t(t) * k : nullptr, weights + int64_t(t) * k,
+                       mass ? mass + t : nullptr);
+}
+
+template <class F>
+static void per_width(int E, F&& f) {
+  const int per = (E + 31) / 32;
+  if (per <= 4) f(std::integral_constant<int, 4>());
+  else if (per <= 8) f(std::integral_constant<int, 8>());
+  else if (per <= 16) f(std::integral_constant<int, 16>());
+  else f(std::integral_constant<int, 32>());
 }
 
 cudaError_t launch_softmax_topk(const uint16_t* logits, int T, int E, int k, int32_t* inds,
                                 uint16_t* scores, uint16_t* weights, uint16_t* mass,
                                 cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  const int per = (E + 31) / 32;
+  if (k > kMaxK) return cudaErrorInvalidValue;
   const int grid = (T + 7) / 8;
-  if (per <= 4) softmax_topk_kernel<4><<<grid, 256, 0, st>>>(logits, T, E, k, inds, scores, weights, mass);
-  else if (per <= 8) softmax_topk_kernel<8><<<grid, 256, 0, st>>>(logits, T, E, k, inds, scores, weights, mass);
-  else if (per <= 16) softmax_topk_kernel<16><<<grid, 256, 0, st>>>(logits, T, E, k, inds, scores, weights, mass);
-  else softmax_topk_kernel<32><<<grid, 256, 0, st>>>(logits, T, E, k, inds, scores, weights, mass);
+  per_width(E, [&](auto per) {
+    softmax_topk_kernel<decltype(per)::value><<<grid, 256, 0, st>>>(logits, T, E, k, inds, scores, weights, mass);
+  });
+  return cudaGetLastError();
+}
+
+// ---- the fused router: logits, then top-k by the last CTA of each token
+// block, and the shared-expert gate in an extra CTA column ----------------
+// CTA (eb, tb), eb < nEB: the 16 x 8 logits tile of router_logits_kernel,
+// then an arrival on the token block's counter; the CTA that arrives last
+// (after its __threadfence, so every tile is visible) runs softmax/top-k for
+// the block's 8 tokens (one warp each) and resets the counter.  CTA eb == nEB
+// computes sigmoid(shared_expert_gate(x)) for the 8 tokens.  The counters
+// (one per token block) must be zero at launch.
+template <int PER>
+__global__ void __launch_bounds__(32 * kRouterSlices) router_fused_kernel(
+    const uint16_t* __restrict__ x, int T, const uint16_t* __restrict__ wg, int E, int K, int k, vx_q4 seg,
+    uint16_t* __restrict__ logits, int32_t* __restrict__ inds, uint16_t* __restrict__ weights,
+    uint16_t* __restrict__ sg, int32_t* __restrict__ counters) {
+  const int nEB = (E + 15) / 16;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = blockIdx.y * 8;
+  if (int(blockIdx.x) == nEB) {
+    // shared expert gate: warp w -> token t0 + w
+    const int t = t0 + warp;
+    if (!sg || !seg.w || t >= T) return;
+    const int G = K / 32;
+    const uint16_t* xr = x + int64_t(t) * K;
+    float acc = 0.f;
+    for (int g = lane; g < G; g += 32) {
+      const uint4 w = __ldg(reinterpret_cast<const uint4*>(seg.w) + g);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+      float q = 0.f, xs = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint4 xv = __ldg(reinterpret_cast<const uint4*>(xr + g * 32 + c * 8));
+        const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+        for (int n = 0; n < 8; ++n) {
+          const float v = __uint_as_float((n & 1) ? (xw[n >> 1] & 0xFFFF0000u) : (xw[n >> 1] << 16));
+          q = fmaf(float(nibble(ws[c], n)), v, q);
+          xs += v;
+        }
+      }
+      acc += fmaf(bf16_to_f32(seg.scales[g]), q, bf16_to_f32(seg.biases[g]) * xs);
+    }
+    acc = warp_sum<32>(acc);
+    if (lane == 0) sg[t] = f32_to_bf16(sigmoid_bf16(bf16r(acc)));
+    return;
+  }
+  __shared__ float red[kRouterSlices][32][4];
+  __shared__ int s_last;
+  const int g = lane >> 2, c = lane & 3;
+  const int e0 = blockIdx.x * 16;
+  const int ea = e0 + g, eb = e0 + g + 8, tx = t0 + g;
+  const uint16_t* ra = wg + int64_t(ea < E ? ea : 0) * K;
+  const uint16_t* rb = wg + int64_t(eb < E ? eb : 0) * K;
+  const uint16_t* rx = x + int64_t(tx < T ? tx : 0) * K;
+  const int steps = K / 32;
+  const int per = (steps + kRouterSlices - 1) / kRouterSlices;
+  const int s0 = warp * per, s1 = min(steps, s0 + per);
+  float d[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int s = s0; s < s1; ++s) {
+    const int kk = s * 32 + c * 8;
+    const uint4 wa = ea < E ? ldg_nc(ra + kk) : make_uint4(0, 0, 0, 0);
+    const uint4 wb = eb < E ? ldg_nc(rb + kk) : make_uint4(0, 0, 0, 0);
+    const uint4 xb = tx < T ? __ldg(reinterpret_cast<const uint4*>(rx + kk)) : make_uint4(0, 0, 0, 0);
+    mma16816(d, wa.x, wb.x, wa.y, wb.y, xb.x, xb.y);
+    mma16816(d, wa.z, wb.z, wa.w, wb.w, xb.z, xb.w);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) red[warp][lane][i] = d[i];
+  __syncthreads();
+  if (warp == 0) {
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int w = 0; w < kRouterSlices; ++w)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] += red[w][lane][i];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = (i < 2) ? ea : eb;
+      const int t = t0 + 2 * c + (i & 1);
+      if (e < E && t < T) logits[int64_t(t) * E + e] = f32_to_bf16(v[i]);
+    }
+    __threadfence();   // this tile before the arrival
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(counters + blockIdx.y, 1) == nEB - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();     // every tile of the token block is visible
+  const int t = t0 + warp;
+  if (t < T)
+    topk_row<PER, true>(logits + int64_t(t) * E, E, k, inds + int64_t(t) * k, nullptr, weights + int64_t(t) * k,
+                        nullptr);
+  if (threadIdx.x == 0) counters[blockIdx.y] = 0;
+}
+
+cudaError_t launch_router_fused(const uint16_t* x, int T, const uint16_t* wg, int E, int K, int k,
+                                const vx_q4* seg, uint16_t* logits, int32_t* inds, uint16_t* weights,
+                                uint16_t* sg, int32_t* counters, cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  if (k > kMaxK) return cudaErrorInvalidValue;
+  const int nTB = (T + 7) / 8, nEB = (E + 15) / 16;
+  cudaError_t e = cudaMemsetAsync(counters, 0, size_t(nTB) * sizeof(int32_t), st);
+  if (e != cudaSuccess) return e;
+  vx_q4 q{};
+  if (seg) q = *seg;
+  dim3 grid(nEB + 1, nTB);
+  per_width(E, [&](auto per) {
+    router_fused_kernel<decltype(per)::value><<<grid, 32 * kRouterSlices, 0, st>>>(x, T, wg, E, K, k, q, logits,
+                                                                                  inds, weights, sg, counters);
+  });
   return cudaGetLastError();
 }
 

@@ -12,7 +12,8 @@ ABI of include/vxmoe.h).  Public surfaces follow the reference:
 """
 from .ops import (  # noqa: F401
     GROUP_SIZE, BITS, MoEWeights, Q4Projection, dequantize, gather_qmm, moe_block, moe_experts,
-    moe_experts_partial, permute, quantized_matmul, rms_norm, route, router, softmax_topk, swiglu,
+    GraphedBlock, moe_experts_partial, permute, quantized_matmul, rms_norm, route, router, softmax_topk,
+    swiglu,
 )
 from .executor import (  # noqa: F401
     MoEExecutor, Executor, build_executor, create_executor, probe_capabilities, weighted_combine,

@@ -96,7 +96,53 @@ class ExpertParallelMoE:
     def _a2a(self, out, inp, out_splits, in_splits):
         dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
 
+    # Decode-sized batches take the fixed-capacity exchange: every rank sends
+    # every destination a block of T rows (token order; rows of tokens with no
+    # expert there carry ids -1 and cost no expert work), so no counts travel
+    # to the host and the step is graph-capturable.  Larger batches exchange
+    # only the rows that are needed, after a count all-to-all.
+    capacity_max_tokens = 256
+
     def __call__(self, x):
+        if int(x.shape[0]) <= self.capacity_max_tokens:
+            return self._call_capacity(x)
+        return self._call_counts(x)
+
+    def _call_capacity(self, x):
+        T, d = int(x.shape[0]), int(x.shape[1])
+        P, El, k = self.world, self.El, self.k
+        dev = x.device
+        inds, wts, sg = self.backend.route(x, self.E)
+        inds = inds.reshape(T, k).to(torch.int64)
+        dest = inds // El                                           # [T, k]
+        # per destination p: token t's slot ids local to p (-1 elsewhere)
+        ranks = torch.arange(P, device=dev).view(P, 1, 1)
+        ids = torch.where(dest.unsqueeze(0) == ranks, inds.unsqueeze(0) - ranks * El,
+                          torch.full((P, T, k), -1, dtype=torch.int64, device=dev))
+        meta = torch.cat([ids.to(torch.float32),
+                          wts.reshape(1, T, k).expand(P, T, k).to(torch.float32)], 2)   # [P, T, 2k]
+        xs = x.unsqueeze(0).expand(P, T, d).contiguous()
+        xr = torch.empty_like(xs)
+        mr = torch.empty_like(meta)
+        self._a2a(xr, xs, None, None)
+        self._a2a(mr, meta.contiguous(), None, None)
+        rids = mr[..., :k].reshape(P * T, k).to(torch.int32).contiguous()
+        rsc = mr[..., k:].reshape(P * T, k).to(torch.bfloat16).contiguous()
+        part = self.backend.experts_partial(xr.reshape(P * T, d), rids, rsc)   # float32 [P*T, d]
+        back = torch.empty((P, T, d), dtype=torch.float32, device=dev)
+        self._a2a(back, part.reshape(P, T, d).contiguous(), None, None)
+        shared = self.backend.shared(x, self.E)
+        routed = back[0]
+        for p in range(1, P):                                       # rank order, float32
+            routed = routed + back[p]
+        y = routed.to(torch.bfloat16)
+        if shared is not None:
+            sy = (sg.reshape(T, 1).float() * shared.float()).to(torch.bfloat16)
+            y = (y.float() + sy.float()).to(torch.bfloat16)
+        self.last_stats = {"mode": "capacity", "rows_per_peer": T}
+        return y
+
+    def _call_counts(self, x):
         T, d = int(x.shape[0]), int(x.shape[1])
         P, El, k = self.world, self.El, self.k
         dev = x.device
@@ -136,5 +182,5 @@ class ExpertParallelMoE:
         if shared is not None:
             sy = (sg.reshape(T, 1).float() * shared.float()).to(torch.bfloat16)
             y = (y.float() + sy.float()).to(torch.bfloat16)
-        self.last_stats = {"sent_rows": S, "received_rows": R, "send_counts": sc}
+        self.last_stats = {"mode": "counts", "sent_rows": S, "received_rows": R, "send_counts": sc}
         return y

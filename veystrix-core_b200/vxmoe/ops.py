@@ -492,9 +492,11 @@ def route(x: torch.Tensor, router_w: torch.Tensor, top_k: int,
     if shared_expert_gate is not None:
         st.shared_expert_gate = shared_expert_gate.vx()
     st.num_experts, st.hidden, st.top_k = E, d, k
-    _lib.check(_lib.load().vx_router(x2.data_ptr(), T, ctypes.byref(st), logits.data_ptr(),
-                                      inds.data_ptr(), w.data_ptr(), _ptr(sg), None, 0,
-                                      _stream(dev)), "router")
+    lib = _lib.load()
+    ws = _WS.get(lib.vx_router_workspace(T, ctypes.byref(st)), dev)
+    _lib.check(lib.vx_router(x2.data_ptr(), T, ctypes.byref(st), logits.data_ptr(),
+                             inds.data_ptr(), w.data_ptr(), _ptr(sg), ws.data_ptr(), ws.numel(),
+                             _stream(dev)), "router")
     lead = x.shape[:-1]
     return RouterOut(logits.reshape(*lead, E), inds.reshape(*lead, k), w.reshape(*lead, k),
                      None if sg is None else sg.reshape(*lead, 1))
@@ -610,6 +612,34 @@ def moe_block(x: torch.Tensor, weights: MoEWeights, return_routing: bool = False
     if return_routing:
         return y, inds.reshape(*x.shape[:-1], k), w.reshape(*x.shape[:-1], k)
     return y
+
+
+class GraphedBlock:
+    """``moe_block`` for a fixed batch size captured once into a CUDA graph:
+    a call copies x into the graph's input buffer and replays the block
+    (router through combine, every launch of it) as one graph launch.  The
+    library's entry points never synchronise the host or allocate, so the
+    whole block captures; the output tensor belongs to the graph and is
+    overwritten by the next call."""
+
+    def __init__(self, weights: MoEWeights, tokens: int):
+        dev = weights.device
+        self.weights = weights
+        self.x = torch.zeros((int(tokens), weights.hidden), dtype=torch.bfloat16, device=dev)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            moe_block(self.x, weights)            # kernel attributes, workspace
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.y = moe_block(self.x, weights)
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        self.x.copy_(x, non_blocking=True)
+        self.graph.replay()
+        return self.y
 
 
 def rms_norm(x: torch.Tensor, gain: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
