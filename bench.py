@@ -48,6 +48,9 @@ def parse():
     ap.add_argument("--tokens", type=int, default=64)
     ap.add_argument("--pools", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=1,
+                    help="> 1: BASELINE config 3, a decode stack of this many distinct layers "
+                         "(h += MoE(RMSNorm(h)), mixers identity)")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch the block's kernels one by one instead of replaying a CUDA graph")
     ap.add_argument("--layout", default="tiled", choices=("tiled", "mlx"),
@@ -210,8 +213,132 @@ def config_dict(args, world):
 # --------------------------------------------------------------------------
 
 
+def main_stack(args):
+    """a decode stack of `args.layers` distinct MoE layers
+    (each with its own random weights, packed into the tiled pool), the
+    residual stream h += MoE(RMSNorm(h)) with gain 1.0 and eps 1e-6, mixers
+    replaced by identity.  A step is one pass of T tokens through every layer,
+    captured as one CUDA graph (the stack is launch-bound at T=1 otherwise)."""
+    import torch
+    import vxmoe
+    from vxmoe import _lib
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    T, L = args.tokens, args.layers
+    K, W = args.steps, max(3, args.warmup)
+    g = torch.Generator(device=dev)
+    layers = []
+    for i in range(L):
+        g.manual_seed(100 + i)
+        layers.append(vxmoe.MoEWeights.random(EXPERTS, HIDDEN, INTER, SHARED_INTER, TOPK, device=dev,
+                                              generator=g).pack())
+    gain = torch.ones(HIDDEN, dtype=torch.bfloat16, device=dev)
+    g.manual_seed(7)
+    xs = torch.randn((K + W, T, HIDDEN), device=dev, generator=g).to(torch.bfloat16)
+
+    def stack(h):
+        for w in layers:
+            h = h + vxmoe.moe_block(vxmoe.rms_norm(h, gain, 1e-6), w)
+        return h
+
+    h_in = torch.zeros((T, HIDDEN), dtype=torch.bfloat16, device=dev)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        stack(h_in)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        h_out = stack(h_in)
+
+    def step(x):
+        h_in.copy_(x, non_blocking=True)
+        graph.replay()
+        return h_out
+
+    stream = torch.cuda.current_stream(dev)
+    for i in range(W):
+        step(xs[i])
+    torch.cuda.synchronize()
+    sampler = ClockSampler(dev.index)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(K):
+        step(xs[W + i])
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    hx = xs[W:W + K].cpu().pin_memory()
+    hy = torch.empty((K, T, HIDDEN), dtype=torch.bfloat16).pin_memory()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for i in range(K):
+        hy[i].copy_(step(hx[i].to(dev, non_blocking=True)), non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    clocks = sampler.stop()
+
+    # routing statistics and stage times: one step without the graph
+    h = xs[W].clone()
+    Us = []
+    _lib.profile_enable(True)
+    for w in layers:
+        n = vxmoe.rms_norm(h, gain, 1e-6)
+        y, inds, _ = vxmoe.moe_block(n, w, return_routing=True)
+        Us.append(int(torch.unique(inds).numel()))
+        h = h + y
+    stages = _lib.profile_read()
+    _lib.profile_enable(False)
+    torch.cuda.synchronize()
+
+    hbm_gbs, _, peak_kind = peaks()
+    step_bytes = sum(layer_bytes(U, T) for U in Us)
+    achieved = step_bytes / (ms / K / 1000.0) / 1e9
+    dom = max(stages, key=lambda k: stages[k][1]) if stages else None
+    roof = None
+    if dom is not None:
+        b = stage_bytes(dom, sum(Us) / len(Us), T)
+        ach = b / (stages[dom][1] / 1000.0) / 1e9 if b else None
+        roof = {"kernel": dom, "bound": "hbm", "achieved": round(ach, 1) if ach else None,
+                "peak": hbm_gbs, "unit": "GB/s", "frac": round(ach / hbm_gbs, 4) if ach else None,
+                "traffic": None, "peak_kind": peak_kind, "algorithmic_bytes_per_launch": int(b) if b else None,
+                "avg_launch_ms": round(stages[dom][1], 5)}
+    cpu = None
+    if not args.no_cpu_baseline:
+        v, cores, kind, sample, _ = cpu_oracle_time(10, 1, budget_s=10.0, tokens=T)
+        cpu = {"value": round(v / L, 4), "unit": "tokens/s", "cores": cores, "kind": kind,
+               "sample": sample + f"; one layer timed, tokens/s divided by {L} layers"}
+    line = {
+        "metric": METRIC, "value": round(K * T / (ms / 1000.0), 2), "unit": "tokens/s", "n_gpus": 1,
+        "steps": K, "warmup": W, "ms_per_step": round(ms / K, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": (f"BASELINE config 3: {L}-layer routed-MoE decode stack, batch {T}, "
+                                "RMSNorm (gain 1, eps 1e-6) + MoE block + residual per layer, mixers identity; "
+                                "d=2048, 512 experts top-10 + shared, I=512, Q4 affine g32"),
+                   "global_batch": T, "layers": L, "experts": EXPERTS, "hidden": HIDDEN,
+                   "intermediate": INTER, "top_k": TOPK, "parallelism": "single GPU, every layer resident",
+                   "l2": f"{L} distinct layers ({L} x 1.0 GB of experts, plus the tiled pool) >> L2",
+                   "launch": "the whole stack as one CUDA graph"},
+        "hbm": {"achieved_gbs": round(achieved, 1), "frac_of_8tbps": round(achieved / NOMINAL_HBM_GBS, 4),
+                "frac_of_measured": round(achieved / hbm_gbs, 4), "bytes_per_step": int(step_bytes),
+                "distinct_experts_mean": round(sum(Us) / len(Us), 1)},
+        "roofline": roof,
+        "stages_ms": {k: round(v[1], 5) for k, v in stages.items()},
+        "e2e": {"value": round(K * T / (e2e_ms / 1000.0), 2), "unit": "tokens/s",
+                "h2d_bytes_per_step": T * HIDDEN * 2, "d2h_bytes_per_step": T * HIDDEN * 2},
+        "cpu_baseline": cpu,
+        "clocks": clocks,
+        "gpu_launches": 7 * L * K,   # per layer: RMSNorm + the block's six kernels
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
+    if args.layers > 1 and args.impl != "reference":
+        return main_stack(args)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
