@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=1,
                     help="> 1: BASELINE config 3, a decode stack of this many distinct layers "
                          "(h += MoE(RMSNorm(h)), mixers identity)")
+    ap.add_argument("--ep-transport", default="p2p", choices=("p2p", "collective"),
+                    help="expert-parallel exchange: peer stores over NVLink or NCCL all-to-all")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch the block's kernels one by one instead of replaying a CUDA graph")
     ap.add_argument("--layout", default="tiled", choices=("tiled", "mlx"),
@@ -198,11 +200,14 @@ def config_dict(args, world):
                      % args.tokens),
         "global_batch": args.tokens * world, "tokens_per_gpu": args.tokens,
         "experts": EXPERTS, "hidden": HIDDEN, "intermediate": INTER, "top_k": TOPK,
-        "parallelism": (f"ep{world}: {EXPERTS // world} experts per GPU, NCCL all-to-all "
-                        f"dispatch/combine" if world > 1 else "single GPU, all experts resident"),
+        "parallelism": ((f"ep{world}: {EXPERTS // world} experts per GPU, dispatch/combine as "
+                         + ("peer stores over NVLink (CUDA IPC buffers, flag-ordered)"
+                            if args.ep_transport == "p2p" else "NCCL all-to-all"))
+                        if world > 1 else "single GPU, all experts resident"),
         "l2": f"inputs larger than L2: {args.pools} rotating weight pools of {EXPERTS} experts",
         "launch": ("one CUDA graph per weight pool (x copied into the graph's input buffer each step)"
-                   if world == 1 and not args.no_graph else "kernels launched one by one"),
+                   if not args.no_graph and (world == 1 or args.ep_transport == "p2p")
+                   else "kernels launched one by one"),
         "weight_layout": ("tiled resident pool (packed once at load)" if args.layout == "tiled"
                           else "MLX arrays"),
     }
@@ -379,22 +384,25 @@ def main():
             layers.append(plain[-1] if args.no_graph else vxmoe.GraphedBlock(w, T))
         else:
             # expert parallel: this rank holds experts [rank*E/N, (rank+1)*E/N)
-            from vxmoe.ep import ExpertParallelMoE
+            from vxmoe.ep import ExpertParallelMoE, GraphedExpertParallel
             w = vxmoe.MoEWeights.random(EXPERTS // world, HIDDEN, INTER, SHARED_INTER, TOPK,
                                         device=dev, generator=g, router_experts=EXPERTS,
                                         router_generator=gr)
             if args.layout == "tiled":
                 w.pack()
             pools.append(w)
-            layers.append(ExpertParallelMoE(w, EXPERTS))
-            plain.append(layers[-1])
+            ep = ExpertParallelMoE(w, EXPERTS, transport=args.ep_transport)
+            plain.append(ep)
+            graphed = args.ep_transport == "p2p" and not args.no_graph
+            layers.append(GraphedExpertParallel(ep, T) if graphed else ep)
     g.manual_seed(7 + rank)
     nx = K + W
     xs = (torch.randn((nx, T, HIDDEN), device=dev, generator=g)).to(torch.bfloat16)
     torch.cuda.synchronize()
-    # our kernels per step: router, permute, activation records, gate/up, down, combine
-    # (EP adds the shared expert's own pass)
-    launches_per_step = 6 if world == 1 else 11
+    # our kernels per step: router, permute, activation records, gate/up, down, combine;
+    # EP adds the shared expert's own pass (permute .. unpermute) and, on the peer
+    # transport, dispatch, the dispatch wait and the combine
+    launches_per_step = 6 if world == 1 else (14 if args.ep_transport == "p2p" else 11)
 
     def step(i):
         return layers[i % len(layers)](xs[i])
@@ -473,9 +481,18 @@ def main():
     _lib.profile_enable(False)
     barrier()
 
+    ep_timeouts = 0
     if dist is not None:
+        from vxmoe import ep as ep_mod
+        for ex in ep_mod._EXCHANGES.values():
+            ep_timeouts |= ex.errors()
+        layers.clear()
+        plain.clear()
+        ep_mod.close_exchanges()
         dist.barrier()
         dist.destroy_process_group()
+    if ep_timeouts:
+        raise RuntimeError(f"rank {rank}: an expert-parallel wait ran out (bits {ep_timeouts})")
     if rank != 0:
         return
 

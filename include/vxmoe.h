@@ -226,6 +226,64 @@ int vx_moe_block(const uint16_t* x, int32_t T, const vx_moe_weights* W,
 int vx_moe_block_noalloc(const uint16_t* x, int32_t T, const vx_moe_weights* W,
                          uint16_t* y, int32_t* inds, uint16_t* weights, void* stream);
 
+/* ---- Expert parallelism over NVLink peer memory ----------------------- */
+
+/* The reference serves the block on one Apple GPU and has no exchange; these
+ * entry points are the B200 scale-out of the same block: the routed experts
+ * split into contiguous shards of num_experts/world per rank, one process per
+ * GPU, every rank's exchange buffer mapped into every rank (CUDA IPC).  One
+ * step, every rank with the same T <= tokens_cap tokens:
+ *   vx_router (own tokens) -> vx_ep_dispatch -> vx_ep_experts (the rank's
+ *   shard) -> [shared expert, own tokens] -> vx_ep_combine
+ * Dispatch stores each token's row once into every rank that owns one of its
+ * experts (peer stores over NVLink) with slot ids local to that rank; the
+ * experts call waits for every rank's dispatch, runs the grouped pipeline and
+ * stores each row's float32 partial sum straight into its home rank; the
+ * combine waits for every rank's partials and adds them in rank order,
+ * rounds once and adds bf16(shared_gate * shared), the float32-then-bf16
+ * contract of the single-GPU combine (metal_runtime.py:315-334).
+ * Waits are bounded: one that runs out sets a bit of *err and returns.
+ * Nothing synchronises the host, so the step captures into a CUDA graph. */
+#define VX_EP_MAX_RANKS 8
+#define VX_EP_IPC_HANDLE_BYTES 64
+
+typedef struct vx_ep_comm {
+  void* buffers[VX_EP_MAX_RANKS]; /* every rank's exchange buffer as mapped here, own at [rank] */
+  int32_t rank, world;
+  int32_t tokens_cap;             /* tokens per rank and step, at most */
+  int32_t hidden, top_k;
+  int32_t num_experts;            /* routed experts over all ranks */
+  int32_t* err;                   /* device word or NULL: bit 0 dispatch wait ran out, bit 1 combine */
+  uint64_t wait_ns;               /* bound of every wait in ns (0: 20 s) */
+} vx_ep_comm;
+
+/* Bytes of one rank's exchange buffer.  The caller allocates it on its GPU,
+ * zeroes it, and lets no rank dispatch before every rank has zeroed its own
+ * (a host barrier); one buffer serves any number of layers run in the same
+ * order on every rank. */
+size_t vx_ep_buffer_bytes(int32_t world, int32_t tokens_cap, int32_t hidden, int32_t top_k);
+
+/* CUDA IPC of an exchange buffer: handle (VX_EP_IPC_HANDLE_BYTES) and offset
+ * of `buffer` inside its allocation; a peer process opens them into its own
+ * mapping and closes that mapping when done. */
+int vx_ep_ipc_handle(const void* buffer, void* handle, uint64_t* offset);
+int vx_ep_ipc_open(const void* handle, uint64_t offset, void** buffer);
+int vx_ep_ipc_close(void* buffer, uint64_t offset);
+
+/* inds/weights [T, k]: the router's global expert ids and slot weights. */
+int vx_ep_dispatch(const vx_ep_comm* comm, const uint16_t* x, int32_t T, const int32_t* inds,
+                   const uint16_t* weights, void* stream);
+
+/* W: this rank's shard (num_experts/world routed experts, no shared expert). */
+size_t vx_ep_experts_workspace(const vx_ep_comm* comm, int32_t T, const vx_moe_weights* W);
+int vx_ep_experts(const vx_ep_comm* comm, int32_t T, const vx_moe_weights* W, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
+/* y [T, d] bf16 for this rank's tokens; shared [T, d] and shared_gate [T]
+ * bf16, both or neither. */
+int vx_ep_combine(const vx_ep_comm* comm, int32_t T, const int32_t* inds, const uint16_t* shared,
+                  const uint16_t* shared_gate, uint16_t* y, void* stream);
+
 /* RMSNorm in float32 with a bf16 gain, bf16 out (patch_rmsnorm.py:96-120). */
 int vx_rmsnorm(const uint16_t* x, const uint16_t* gain, int32_t T, int32_t d,
                float eps, uint16_t* y, void* stream);

@@ -707,6 +707,169 @@ int vx_moe_block(const uint16_t* x, int32_t T, const vx_moe_weights* W, uint16_t
   return VX_OK;
 }
 
+// ---- Expert parallelism over peer memory --------------------------------
+
+size_t vx_ep_buffer_bytes(int32_t world, int32_t tokens_cap, int32_t hidden, int32_t top_k) {
+  if (world < 1 || world > VX_EP_MAX_RANKS || tokens_cap < 1 || hidden < 1 || top_k < 1) return 0;
+  return size_t(ep_layout(world, tokens_cap, hidden, top_k).bytes);
+}
+
+static int check_comm(const vx_ep_comm* c, int32_t T, EpArgs* a) {
+  if (!c || c->world < 1 || c->world > VX_EP_MAX_RANKS || c->rank < 0 || c->rank >= c->world)
+    return VX_EINVAL_SHAPE;
+  if (c->hidden < 8 || c->hidden % 8 || c->top_k < 1 || c->top_k > 32 || c->tokens_cap < 1)
+    return VX_EINVAL_SHAPE;
+  if (c->num_experts < c->world || c->num_experts % c->world) return VX_EINVAL_SHAPE;
+  if (T < 0 || T > c->tokens_cap) return VX_EINVAL_SHAPE;
+  const EpLayout L = ep_layout(c->world, c->tokens_cap, c->hidden, c->top_k);
+  for (int p = 0; p < VX_EP_MAX_RANKS; ++p) {
+    a->buf[p] = p < c->world ? static_cast<unsigned char*>(c->buffers[p]) : nullptr;
+    if (p < c->world && (!a->buf[p] || !aligned16(a->buf[p]))) return VX_EINVAL_SHAPE;
+  }
+  a->P = c->world;
+  a->rank = c->rank;
+  a->T = T;
+  a->d = c->hidden;
+  a->k = c->top_k;
+  a->El = c->num_experts / c->world;
+  a->err = c->err;
+  a->wait_ns = c->wait_ns ? c->wait_ns : 20ull * 1000 * 1000 * 1000;
+  a->off_x = L.x;
+  a->off_ids = L.ids;
+  a->off_w = L.w;
+  a->off_back = L.back;
+  return VX_OK;
+}
+
+typedef CUresult (*PfnMemGetAddressRange)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+static PfnMemGetAddressRange mem_range_fn() {
+  static PfnMemGetAddressRange fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PfnMemGetAddressRange>(p);
+  }
+  return fn;
+}
+
+int vx_ep_ipc_handle(const void* buffer, void* handle, uint64_t* offset) {
+  if (!buffer || !handle || !offset) return VX_EINVAL_SHAPE;
+  PfnMemGetAddressRange range = mem_range_fn();
+  if (!range) return VX_EUNSUPPORTED;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(buffer)) != CUDA_SUCCESS) return VX_EINVAL_SHAPE;
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return vx_cuda_fail(e);
+  static_assert(sizeof(h) == VX_EP_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle, &h, sizeof(h));
+  *offset = uint64_t(reinterpret_cast<uintptr_t>(buffer) - uintptr_t(base));
+  return VX_OK;
+}
+
+int vx_ep_ipc_open(const void* handle, uint64_t offset, void** buffer) {
+  if (!handle || !buffer) return VX_EINVAL_SHAPE;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return vx_cuda_fail(e);
+  *buffer = static_cast<char*>(base) + offset;
+  return VX_OK;
+}
+
+int vx_ep_ipc_close(void* buffer, uint64_t offset) {
+  if (!buffer) return VX_EINVAL_SHAPE;
+  cudaError_t e = cudaIpcCloseMemHandle(static_cast<char*>(buffer) - offset);
+  return e == cudaSuccess ? VX_OK : vx_cuda_fail(e);
+}
+
+int vx_ep_dispatch(const vx_ep_comm* comm, const uint16_t* x, int32_t T, const int32_t* inds,
+                   const uint16_t* weights, void* stream) {
+  EpArgs a;
+  int s = check_comm(comm, T, &a);
+  if (s) return s;
+  if (T == 0) return VX_OK;
+  if (!x || !inds || !weights || !aligned16(x)) return VX_EINVAL_SHAPE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = launch_ep_dispatch(a, x, inds, weights, st);
+  if (e != cudaSuccess) return vx_cuda_fail(e);
+  profile_mark(st, "ep_dispatch");
+  return VX_OK;
+}
+
+// The shard's pipeline for the P*T received rows.  An AUTO expert path
+// follows the rows that carry a slot here: T*k of them on average (the P*T*k
+// received slots are spread over P ranks).
+static int ep_dims(const vx_ep_comm* comm, int32_t T, const vx_moe_weights* W, BlockDims* dm) {
+  int s = check_weights(W, false, dm);
+  if (s) return s;
+  if (dm->E * comm->world != comm->num_experts || dm->d != comm->hidden || dm->k != comm->top_k)
+    return VX_EINVAL_SHAPE;
+  dm->shared = false;
+  dm->Is = 0;
+  if (dm->path == VX_PATH_AUTO) {
+    const int o = path_override();
+    dm->path = o ? o : (int64_t(T) * dm->k >= 4 * int64_t(dm->E) ? VX_PATH_GEMM : VX_PATH_GEMV);
+  }
+  return VX_OK;
+}
+
+size_t vx_ep_experts_workspace(const vx_ep_comm* comm, int32_t T, const vx_moe_weights* W) {
+  EpArgs a;
+  BlockDims dm;
+  if (check_comm(comm, T, &a) || ep_dims(comm, T, W, &dm)) return 0;
+  Carver c(nullptr);
+  carve_experts(c, T * comm->world, dm);
+  return c.size();
+}
+
+int vx_ep_experts(const vx_ep_comm* comm, int32_t T, const vx_moe_weights* W, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+  EpArgs a;
+  int s = check_comm(comm, T, &a);
+  if (s) return s;
+  BlockDims dm;
+  s = ep_dims(comm, T, W, &dm);
+  if (s) return s;
+  if (T == 0) return VX_OK;
+  if (!workspace || workspace_bytes < vx_ep_experts_workspace(comm, T, W)) return VX_EWORKSPACE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int rows = T * comm->world;
+  Carver c(workspace);
+  ExpertScratch es = carve_experts(c, rows, dm);
+  cudaError_t e = launch_ep_wait_dispatch(a, st);
+  if (e != cudaSuccess) return vx_cuda_fail(e);
+  profile_mark(st, "ep_wait");
+  unsigned char* own = a.buf[a.rank];
+  s = run_experts(reinterpret_cast<const uint16_t*>(own + a.off_x), rows,
+                  reinterpret_cast<const int32_t*>(own + a.off_ids), W, dm, es, st);
+  if (s) return s;
+  e = launch_ep_send(a, es.yd, dm.d, es.inverse, st);
+  if (e != cudaSuccess) return vx_cuda_fail(e);
+  profile_mark(st, "ep_send");
+  return VX_OK;
+}
+
+int vx_ep_combine(const vx_ep_comm* comm, int32_t T, const int32_t* inds, const uint16_t* shared,
+                  const uint16_t* shared_gate, uint16_t* y, void* stream) {
+  EpArgs a;
+  int s = check_comm(comm, T, &a);
+  if (s) return s;
+  if ((shared == nullptr) != (shared_gate == nullptr)) return VX_EINVAL_SHAPE;
+  if (T == 0) return VX_OK;
+  if (!inds || !y) return VX_EINVAL_SHAPE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = launch_ep_combine(a, inds, shared, shared_gate, y, st);
+  if (e != cudaSuccess) return vx_cuda_fail(e);
+  profile_mark(st, "ep_combine");
+  return VX_OK;
+}
+
 int vx_rmsnorm(const uint16_t* x, const uint16_t* gain, int32_t T, int32_t d, float eps, uint16_t* y,
                void* stream) {
   if (T < 0 || d <= 0) return VX_EINVAL_SHAPE;

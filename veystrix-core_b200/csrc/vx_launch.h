@@ -174,6 +174,38 @@ cudaError_t launch_router_fused(const uint16_t* x, int T, const uint16_t* wg, in
                                 const vx_q4* seg, uint16_t* logits, int32_t* inds, uint16_t* weights,
                                 uint16_t* sg, int32_t* counters, cudaStream_t st);
 
+// Expert-parallel exchange buffer of one rank (vx_ep.cu): a 256-byte header
+// (u32 flag_dispatch[8], flag_combine[8], epoch, tickets[3]), then, for a step
+// of T <= cap tokens per rank, rows i = r*T + t of
+//   x    [P*T][d] bf16    rows received from rank r for this rank's experts
+//   ids  [P*T][k] int32   their slot ids local to this rank (-1: elsewhere)
+//   w    [P*T][k] bf16    their slot weights
+//   back [P*T][d] float32 partial sums of this rank's tokens from rank r
+// (each region sized for cap, 256-byte aligned).
+constexpr int kEpMaxRanks = 8;
+constexpr int64_t kEpHeaderBytes = 256;
+
+struct EpLayout {
+  int64_t x, ids, w, back, bytes;
+};
+EpLayout ep_layout(int P, int cap, int d, int k);
+
+struct EpArgs {
+  unsigned char* buf[kEpMaxRanks];   // every rank's exchange buffer (own at [rank])
+  int P, rank, T, d, k, El;          // El: experts per rank
+  int32_t* err;                      // bit 0: dispatch wait ran out, bit 1: combine wait (may be null)
+  uint64_t wait_ns;                  // bound of every wait
+  int64_t off_x, off_ids, off_w, off_back;
+};
+
+cudaError_t launch_ep_dispatch(const EpArgs& a, const uint16_t* x, const int32_t* inds,
+                               const uint16_t* wts, cudaStream_t st);
+cudaError_t launch_ep_wait_dispatch(const EpArgs& a, cudaStream_t st);
+cudaError_t launch_ep_send(const EpArgs& a, const uint16_t* yd, int64_t ldy, const int32_t* inverse,
+                           cudaStream_t st);
+cudaError_t launch_ep_combine(const EpArgs& a, const int32_t* inds, const uint16_t* shared,
+                              const uint16_t* sg, uint16_t* y, cudaStream_t st);
+
 // Combine modes for the shared part.
 enum SharedMode { kSharedNone = 0, kSharedInternal = 1, kSharedY = 2, kSharedParts = 3 };
 

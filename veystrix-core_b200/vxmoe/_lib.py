@@ -63,6 +63,18 @@ class VxMoEWeights(ctypes.Structure):
 
 PATH_AUTO, PATH_GEMV, PATH_GEMM = 0, 1, 2
 
+EP_MAX_RANKS = 8
+EP_IPC_HANDLE_BYTES = 64
+
+
+class VxEpComm(ctypes.Structure):
+    _fields_ = [
+        ("buffers", c_void_p * EP_MAX_RANKS),
+        ("rank", c_int32), ("world", c_int32), ("tokens_cap", c_int32),
+        ("hidden", c_int32), ("top_k", c_int32), ("num_experts", c_int32),
+        ("err", c_void_p), ("wait_ns", ctypes.c_uint64),
+    ]
+
 
 P = c_void_p
 # name: (restype, argtypes)
@@ -94,6 +106,16 @@ SIGNATURES = {
                                     c_size_t, P]),
     "vx_moe_block_noalloc": (ctypes.c_int, [P, c_int32, ctypes.POINTER(VxMoEWeights), P, P, P,
                                             P]),
+    "vx_ep_buffer_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32]),
+    "vx_ep_ipc_handle": (ctypes.c_int, [P, P, ctypes.POINTER(ctypes.c_uint64)]),
+    "vx_ep_ipc_open": (ctypes.c_int, [P, ctypes.c_uint64, ctypes.POINTER(c_void_p)]),
+    "vx_ep_ipc_close": (ctypes.c_int, [P, ctypes.c_uint64]),
+    "vx_ep_dispatch": (ctypes.c_int, [ctypes.POINTER(VxEpComm), P, c_int32, P, P, P]),
+    "vx_ep_experts_workspace": (c_size_t, [ctypes.POINTER(VxEpComm), c_int32,
+                                           ctypes.POINTER(VxMoEWeights)]),
+    "vx_ep_experts": (ctypes.c_int, [ctypes.POINTER(VxEpComm), c_int32,
+                                     ctypes.POINTER(VxMoEWeights), P, c_size_t, P]),
+    "vx_ep_combine": (ctypes.c_int, [ctypes.POINTER(VxEpComm), c_int32, P, P, P, P, P]),
     "vx_rmsnorm": (ctypes.c_int, [P, P, c_int32, c_int32, c_float, P, P]),
     "vx_profile_enable": (ctypes.c_int, [ctypes.c_int]),
     "vx_profile_read": (ctypes.c_int, [ctypes.c_int, ctypes.c_char_p, ctypes.c_int,
