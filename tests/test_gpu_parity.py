@@ -218,6 +218,8 @@ def test_router_full_production(prod_params):
 # ---------------------------------------------------------------- permutation
 
 @pytest.mark.parametrize("P,E,skew", [(0, 8, False), (1, 8, False), (10, 512, False),
+                                      (200, 512, False), (256, 1024, False), (256, 8, True),
+                                      (257, 512, True), (80, 3, False),
                                       (640, 512, False), (4096, 64, True), (65536, 512, True),
                                       (20480, 512, False), (100003, 64, False)])
 def test_permute_bit_exact(P, E, skew):

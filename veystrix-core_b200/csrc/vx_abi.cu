@@ -34,6 +34,15 @@ int sm_count() {
   return cache[dev];
 }
 
+bool chain_enabled(bool streaming) {
+  static int v = -1;
+  if (v < 0) {
+    const char* s = getenv("VXMOE_PDL");
+    v = (s && strcmp(s, "0") == 0) ? 0 : (s && strcmp(s, "1") == 0) ? 1 : 2;
+  }
+  return v == 1 || (v == 2 && !streaming);
+}
+
 // Carves 256-byte aligned pieces out of a caller workspace.  With a null
 // base it only measures.
 struct Carver {
@@ -187,12 +196,18 @@ static ExpertScratch carve_experts(Carver& c, int T, const BlockDims& dm) {
 }
 
 // permute -> gate/up + SwiGLU -> down, leaving sorted bf16 outputs in s.yd.
+// err_zeroed: the caller cleared s.err earlier on the stream, so no memset
+// node breaks the chain of programmatically serialised kernels.
 static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx_moe_weights* W,
-                       const BlockDims& dm, const ExpertScratch& s, cudaStream_t st) {
+                       const BlockDims& dm, const ExpertScratch& s, cudaStream_t st,
+                       bool err_zeroed = false) {
   const int64_t P = int64_t(T) * dm.k;
   const int Ts = dm.shared ? T : 0;
-  cudaError_t e = cudaMemsetAsync(s.err, 0, 2 * sizeof(int32_t), st);
-  if (e != cudaSuccess) return vx_cuda_fail(e);
+  cudaError_t e = cudaSuccess;
+  if (!err_zeroed) {
+    e = cudaMemsetAsync(s.err, 0, 2 * sizeof(int32_t), st);
+    if (e != cudaSuccess) return vx_cuda_fail(e);
+  }
   const ExpertPath path = expert_path(T, dm);
   const int chunk = path == kPathGemm ? (dm.pool ? kPoolGemmItemChunk : kGemmItemChunk)
                     : path == kPathGemvTiled ? kTiledItemChunk : kItemChunk;
@@ -695,11 +710,13 @@ int vx_moe_block(const uint16_t* x, int32_t T, const vx_moe_weights* W, uint16_t
   ExpertScratch es = carve_experts(c, T, dm);
   if (!inds) inds = inds_ws;
   if (!weights) weights = w_ws;
+  cudaError_t e = cudaMemsetAsync(es.err, 0, 2 * sizeof(int32_t), st);
+  if (e != cudaSuccess) return vx_cuda_fail(e);
   s = router_impl(x, T, W, dm, logits, inds, weights, dm.shared ? sg : nullptr, counters, st);
   if (s) return s;
-  s = run_experts(x, T, inds, W, dm, es, st);
+  s = run_experts(x, T, inds, W, dm, es, st, true);
   if (s) return s;
-  cudaError_t e = launch_combine(es.yd, dm.d, es.inverse, weights, T, dm.k, dm.d,
+  e = launch_combine(es.yd, dm.d, es.inverse, weights, T, dm.k, dm.d,
                                  dm.shared ? kSharedInternal : kSharedNone, es.offsets, dm.E, sg,
                                  nullptr, nullptr, nullptr, y, st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
@@ -842,12 +859,14 @@ int vx_ep_experts(const vx_ep_comm* comm, int32_t T, const vx_moe_weights* W, vo
   const int rows = T * comm->world;
   Carver c(workspace);
   ExpertScratch es = carve_experts(c, rows, dm);
-  cudaError_t e = launch_ep_wait_dispatch(a, st);
+  cudaError_t e = cudaMemsetAsync(es.err, 0, 2 * sizeof(int32_t), st);
+  if (e != cudaSuccess) return vx_cuda_fail(e);
+  e = launch_ep_wait_dispatch(a, st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
   profile_mark(st, "ep_wait");
   unsigned char* own = a.buf[a.rank];
   s = run_experts(reinterpret_cast<const uint16_t*>(own + a.off_x), rows,
-                  reinterpret_cast<const int32_t*>(own + a.off_ids), W, dm, es, st);
+                  reinterpret_cast<const int32_t*>(own + a.off_ids), W, dm, es, st, true);
   if (s) return s;
   e = launch_ep_send(a, es.yd, dm.d, es.inverse, st);
   if (e != cudaSuccess) return vx_cuda_fail(e);

@@ -129,6 +129,25 @@ struct Q4Ptr {
   const uint16_t* b;
 };
 
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch.  The block's kernels follow one another on
+// one stream; each is launched with programmatic stream serialisation
+// (launch_chained), so it may become resident while its predecessor still
+// runs.  chain_begin() first waits until the predecessor grid has completed
+// and its memory is visible (a no-op when the launch had no programmatic
+// edge), then lets the successor launch.  Every chained kernel calls it, or
+// chain_wait(), before touching global memory.  The streaming GEMV/GEMM
+// kernels call chain_wait(): their successors launch only as their CTAs
+// exit, so no waiting CTA takes an SM slot from them.
+// ---------------------------------------------------------------------------
+
+VX_DEVICE void chain_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+VX_DEVICE void chain_begin() {
+  chain_wait();
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 VX_DEVICE Q4Ptr q4_expert(const vx_q4& bank, int e) {
   const int64_t words = int64_t(bank.out) * (bank.in / 8);
   const int64_t groups = int64_t(bank.out) * (bank.in / bank.group_size);

@@ -16,6 +16,7 @@ __global__ void __launch_bounds__(256) combine_kernel(
     const int32_t* __restrict__ offsets, int E, const uint16_t* __restrict__ sg,
     const uint16_t* __restrict__ shared_y, const uint16_t* __restrict__ shared,
     const uint16_t* __restrict__ shared_gate, uint16_t* __restrict__ y) {
+  chain_begin();
   const int t = blockIdx.y;
   const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 2;
   if (c >= d) return;
@@ -63,9 +64,8 @@ cudaError_t launch_combine(const uint16_t* yd, int64_t ldy, const int32_t* inver
                            const uint16_t* shared_gate, uint16_t* y, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
   dim3 grid((d / 2 + 255) / 256, T);
-  combine_kernel<<<grid, 256, 0, st>>>(yd, ldy, inverse, weights, T, k, d, int(mode), offsets, E, sg,
-                                       shared_y, shared, shared_gate, y);
-  return cudaGetLastError();
+  return launch_chained(combine_kernel, grid, dim3(256), 0, st, yd, ldy, inverse, weights, T, k, d,
+                        int(mode), offsets, E, sg, shared_y, shared, shared_gate, y);
 }
 
 // Activations for the grouped GEMV: B order and per-group sums.  One thread
@@ -74,6 +74,7 @@ cudaError_t launch_combine(const uint16_t* yd, int64_t ldy, const int32_t* inver
 // (s0 + s1) + (s2 + s3), each s a left-to-right float32 sum of 8 inputs.
 __global__ void xprep_kernel(const uint16_t* __restrict__ x, int64_t rows, int K,
                              uint16_t* __restrict__ xb, float* __restrict__ xs, int64_t ldxs) {
+  chain_begin();
   const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const int nb = K / 8;
   const int64_t n = rows * nb;
@@ -109,8 +110,8 @@ cudaError_t launch_xprep(const uint16_t* x, int64_t rows, int K, uint16_t* xb, f
                          int64_t ldxs, cudaStream_t st) {
   const int64_t n = rows * (K / 8);
   if (n == 0) return cudaSuccess;
-  xprep_kernel<<<int((n + 255) / 256), 256, 0, st>>>(x, rows, K, xb, xs, ldxs);
-  return cudaGetLastError();
+  return launch_chained(xprep_kernel, dim3(int((n + 255) / 256)), dim3(256), 0, st, x, rows, K, xb, xs,
+                        ldxs);
 }
 
 // Float32 partial combine for expert parallelism: the same slot-order
@@ -119,6 +120,7 @@ cudaError_t launch_xprep(const uint16_t* x, int64_t rows, int K, uint16_t* xb, f
 __global__ void __launch_bounds__(256) combine_partial_kernel(
     const uint16_t* __restrict__ yd, int64_t ldy, const int32_t* __restrict__ inverse,
     const uint16_t* __restrict__ weights, int k, int d, float* __restrict__ out) {
+  chain_begin();
   const int t = blockIdx.y;
   const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 2;
   if (c >= d) return;
@@ -139,14 +141,15 @@ cudaError_t launch_combine_partial(const uint16_t* yd, int64_t ldy, const int32_
                                    cudaStream_t st) {
   if (T == 0) return cudaSuccess;
   dim3 grid((d / 2 + 255) / 256, T);
-  combine_partial_kernel<<<grid, 256, 0, st>>>(yd, ldy, inverse, weights, k, d, out);
-  return cudaGetLastError();
+  return launch_chained(combine_partial_kernel, grid, dim3(256), 0, st, yd, ldy, inverse, weights, k, d,
+                        out);
 }
 
 // out[t, s, :] = yd[inverse[t*k+s], :]  (_scatter_unsort)
 __global__ void unpermute_kernel(const uint16_t* __restrict__ yd, int64_t ldy,
                                  const int32_t* __restrict__ inverse, int k, int d,
                                  uint16_t* __restrict__ out) {
+  chain_begin();
   const int64_t pair = blockIdx.y;
   const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 2;
   if (c >= d) return;
@@ -160,8 +163,7 @@ cudaError_t launch_unpermute(const uint16_t* yd, int64_t ldy, const int32_t* inv
                              int k, int d, uint16_t* out, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
   dim3 grid((d / 2 + 255) / 256, T * k);
-  unpermute_kernel<<<grid, 256, 0, st>>>(yd, ldy, inverse, k, d, out);
-  return cudaGetLastError();
+  return launch_chained(unpermute_kernel, grid, dim3(256), 0, st, yd, ldy, inverse, k, d, out);
 }
 
 // RMSNorm (patch_rmsnorm.py:96-120): y = bf16(x * (1/sqrt(mean(x^2)+eps)) * gain)
@@ -169,6 +171,7 @@ cudaError_t launch_unpermute(const uint16_t* yd, int64_t ldy, const int32_t* inv
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const uint16_t* __restrict__ x,
                                                       const uint16_t* __restrict__ gain, int d,
                                                       float eps, uint16_t* __restrict__ y) {
+  chain_begin();
   const int64_t t = blockIdx.x;
   const uint16_t* xr = x + t * d;
   float s = 0.f;
@@ -193,8 +196,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const uint16_t* __restrict
 cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* gain, int T, int d, float eps,
                            uint16_t* y, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  rmsnorm_kernel<<<T, 256, 0, st>>>(x, gain, d, eps, y);
-  return cudaGetLastError();
+  return launch_chained(rmsnorm_kernel, dim3(T), dim3(256), 0, st, x, gain, d, eps, y);
 }
 
 __global__ void swiglu_kernel(const uint16_t* __restrict__ g, const uint16_t* __restrict__ u,

@@ -72,13 +72,15 @@ VX_DEVICE uint32_t step_epoch(const EpArgs& a) {
   return *reinterpret_cast<volatile uint32_t*>(header(a.buf[a.rank]) + kHdrEpoch) + 1u;
 }
 
-// Publishes this launch's peer stores: every thread fences at system scope,
-// the last CTA to arrive on the ticket raises flag[slot + rank] = e on every
-// rank and re-arms the ticket.
+// Publishes this launch's peer stores: the CTA barrier orders its threads'
+// stores before thread 0's system-scope fence (the grid-barrier pattern of
+// cooperative groups, at system scope), the last CTA to arrive on the ticket
+// fences again and raises flag[slot + rank] = e on every rank with a release
+// store, then re-arms the ticket.
 VX_DEVICE void signal_all(const EpArgs& a, int ticket, int slot, uint32_t e) {
-  __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence_system();
     uint32_t* tk = header(a.buf[a.rank]) + kHdrTicket + ticket;
     const uint32_t n = atomicAdd(tk, 1u);
     if (n == gridDim.x * gridDim.y - 1) {
@@ -93,6 +95,7 @@ VX_DEVICE void signal_all(const EpArgs& a, int ticket, int slot, uint32_t e) {
 __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpArgs a, const uint16_t* __restrict__ x,
                                                           const int32_t* __restrict__ inds,
                                                           const uint16_t* __restrict__ wts) {
+  chain_begin();
   const uint32_t e = step_epoch(a);
   const int t = blockIdx.x / a.P, p = blockIdx.x % a.P;
   unsigned char* dst = a.buf[p];
@@ -119,6 +122,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpArgs a, const uint16
 }
 
 __global__ void ep_wait_dispatch_kernel(EpArgs a) {
+  chain_begin();
   const uint32_t e = step_epoch(a);
   if (threadIdx.x < a.P &&
       !wait_epoch(header(a.buf[a.rank]) + kHdrFlagDispatch + threadIdx.x, e, a.wait_ns) && a.err)
@@ -131,6 +135,7 @@ __global__ void ep_wait_dispatch_kernel(EpArgs a) {
 // Rows with no slot here send nothing.
 __global__ void __launch_bounds__(256) ep_send_kernel(EpArgs a, const uint16_t* __restrict__ yd,
                                                       int64_t ldy, const int32_t* __restrict__ inverse) {
+  chain_begin();
   const uint32_t e = step_epoch(a);
   const int i = blockIdx.x;
   const int r = i / a.T, t = i % a.T;
@@ -169,6 +174,7 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(EpArgs a, const int32_t
                                                          const uint16_t* __restrict__ shared,
                                                          const uint16_t* __restrict__ sg,
                                                          uint16_t* __restrict__ y) {
+  chain_begin();
   const uint32_t e = step_epoch(a);
   uint32_t* hdr = header(a.buf[a.rank]);
   if (threadIdx.x < a.P && !wait_epoch(hdr + kHdrFlagCombine + threadIdx.x, e, a.wait_ns) && a.err)
@@ -238,27 +244,23 @@ EpLayout ep_layout(int P, int cap, int d, int k) {
 cudaError_t launch_ep_dispatch(const EpArgs& a, const uint16_t* x, const int32_t* inds,
                                const uint16_t* wts, cudaStream_t st) {
   if (a.T == 0) return cudaSuccess;
-  ep_dispatch_kernel<<<a.T * a.P, 256, 0, st>>>(a, x, inds, wts);
-  return cudaGetLastError();
+  return launch_chained(ep_dispatch_kernel, dim3(a.T * a.P), dim3(256), 0, st, a, x, inds, wts);
 }
 
 cudaError_t launch_ep_wait_dispatch(const EpArgs& a, cudaStream_t st) {
-  ep_wait_dispatch_kernel<<<1, 32, 0, st>>>(a);
-  return cudaGetLastError();
+  return launch_chained(ep_wait_dispatch_kernel, dim3(1), dim3(32), 0, st, a);
 }
 
 cudaError_t launch_ep_send(const EpArgs& a, const uint16_t* yd, int64_t ldy, const int32_t* inverse,
                            cudaStream_t st) {
   if (a.T == 0) return cudaSuccess;
-  ep_send_kernel<<<a.T * a.P, 256, 0, st>>>(a, yd, ldy, inverse);
-  return cudaGetLastError();
+  return launch_chained(ep_send_kernel, dim3(a.T * a.P), dim3(256), 0, st, a, yd, ldy, inverse);
 }
 
 cudaError_t launch_ep_combine(const EpArgs& a, const int32_t* inds, const uint16_t* shared,
                               const uint16_t* sg, uint16_t* y, cudaStream_t st) {
   if (a.T == 0) return cudaSuccess;
-  ep_combine_kernel<<<a.T, 256, 0, st>>>(a, inds, shared, sg, y);
-  return cudaGetLastError();
+  return launch_chained(ep_combine_kernel, dim3(a.T), dim3(256), 0, st, a, inds, shared, sg, y);
 }
 
 }  // namespace vx

@@ -97,6 +97,7 @@ VX_DEVICE bool pool_task(const PoolGemmArgs& a, int t, PoolTask& k) {
 
 template <bool GATEUP>
 __global__ void __launch_bounds__(kPoolThreads, 1) gemm_pool_kernel(const __grid_constant__ PoolGemmArgs a) {
+  chain_wait();
   using C = PoolCfg<GATEUP>;
   constexpr int AS = C::kAStages, BS = C::kBStages, RS = C::kRecStages, NP = C::NP, APS = C::kAps;
   extern __shared__ unsigned char smem_raw[];
@@ -387,15 +388,12 @@ cudaError_t launch_gemm_pool(bool gateup, PoolGemmArgs a, const uint16_t* x, int
     auto k = gemm_pool_kernel<true>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(PoolCfg<true>::kSmem));
     if (e != cudaSuccess) return e;
-    k<<<grid, kPoolThreads, PoolCfg<true>::kSmem, st>>>(a);
-  } else {
-    auto k = gemm_pool_kernel<false>;
-    cudaError_t e =
-        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(PoolCfg<false>::kSmem));
-    if (e != cudaSuccess) return e;
-    k<<<grid, kPoolThreads, PoolCfg<false>::kSmem, st>>>(a);
+    return launch_streaming(k, dim3(grid), dim3(kPoolThreads), PoolCfg<true>::kSmem, st, a);
   }
-  return cudaGetLastError();
+  auto k = gemm_pool_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(PoolCfg<false>::kSmem));
+  if (e != cudaSuccess) return e;
+  return launch_streaming(k, dim3(grid), dim3(kPoolThreads), PoolCfg<false>::kSmem, st, a);
 }
 
 }  // namespace vx

@@ -51,6 +51,7 @@ struct GemmCfg {
 
 template <bool GATEUP>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_constant__ GemmArgs a) {
+  chain_wait();
   using C = GemmCfg<GATEUP>;
   constexpr int S = C::kStages;
   extern __shared__ unsigned char smem_raw[];
@@ -271,14 +272,12 @@ cudaError_t launch_gemm_tc(bool gateup, GemmArgs a, const uint16_t* x, int64_t r
     auto k = gemm_tc_kernel<true>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(GemmCfg<true>::kSmem));
     if (e != cudaSuccess) return e;
-    k<<<int(grid), kGemmThreads, GemmCfg<true>::kSmem, st>>>(a);
-  } else {
-    auto k = gemm_tc_kernel<false>;
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(GemmCfg<false>::kSmem));
-    if (e != cudaSuccess) return e;
-    k<<<int(grid), kGemmThreads, GemmCfg<false>::kSmem, st>>>(a);
+    return launch_streaming(k, dim3(int(grid)), dim3(kGemmThreads), GemmCfg<true>::kSmem, st, a);
   }
-  return cudaGetLastError();
+  auto k = gemm_tc_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(GemmCfg<false>::kSmem));
+  if (e != cudaSuccess) return e;
+  return launch_streaming(k, dim3(int(grid)), dim3(kGemmThreads), GemmCfg<false>::kSmem, st, a);
 }
 
 // x rows (token src_rows[p] for positions p < *n_rows) -> bf16 rows in B
@@ -286,6 +285,7 @@ cudaError_t launch_gemm_tc(bool gateup, GemmArgs a, const uint16_t* x, int64_t r
 __global__ void gather_border_kernel(const uint16_t* __restrict__ x, int64_t ldx, int K,
                                      const int32_t* __restrict__ src_rows, const int32_t* __restrict__ n_rows,
                                      int64_t rows, uint16_t* __restrict__ out) {
+  chain_begin();
   const int nb = K / 8;
   const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= rows * nb) return;
@@ -306,8 +306,8 @@ cudaError_t launch_gather_border(const uint16_t* x, int64_t ldx, int K, const in
                                  const int32_t* n_rows, int64_t rows, uint16_t* out, cudaStream_t st) {
   const int64_t n = rows * (K / 8);
   if (n == 0) return cudaSuccess;
-  gather_border_kernel<<<int((n + 255) / 256), 256, 0, st>>>(x, ldx, K, src_rows, n_rows, rows, out);
-  return cudaGetLastError();
+  return launch_chained(gather_border_kernel, dim3(int((n + 255) / 256)), dim3(256), 0, st, x, ldx, K,
+                        src_rows, n_rows, rows, out);
 }
 
 }  // namespace vx

@@ -52,6 +52,7 @@ struct Stage {
 
 template <bool GATEUP, int MT, bool XMMA, bool EVEN>
 __global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(const __grid_constant__ MmaArgs a) {
+  chain_wait();
   constexpr int NP = GATEUP ? 2 : 1;
   using S = Stage<NP, MT, XMMA>;
   extern __shared__ __align__(128) unsigned char smem[];
@@ -328,8 +329,7 @@ static cudaError_t launch_mma_t(MmaArgs a, int max_items, int max_out, cudaStrea
   int64_t grid = (warps + kWarps - 1) / kWarps;
   if (grid > cap) grid = cap;
   if (grid <= 0) return cudaSuccess;
-  kern<<<int(grid), kMmaThreads, smem, st>>>(a);
-  return cudaGetLastError();
+  return launch_streaming(kern, dim3(int(grid)), dim3(kMmaThreads), smem, st, a);
 }
 
 template <bool GATEUP, int MT, bool XMMA>

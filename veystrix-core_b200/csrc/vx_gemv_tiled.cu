@@ -109,6 +109,7 @@ constexpr bool kWeightsByLsu = true;
 
 template <bool GATEUP, int MT, bool XMMA, int STAGES>
 __global__ void __launch_bounds__(kTiledThreads, 2) gemv_tiled_kernel(const __grid_constant__ TiledArgs a) {
+  chain_wait();
   constexpr int NP = GATEUP ? 2 : 1;
   constexpr int kRec = NP * MT * kTileRecordUnit;
   constexpr int kWBytes = NP * MT * 1024;
@@ -355,6 +356,7 @@ __global__ void __launch_bounds__(kTiledThreads, 2) gemv_tiled_kernel(const __gr
 __global__ void act_records_kernel(const uint16_t* __restrict__ x, int64_t ldx, int K,
                                    const int32_t* __restrict__ src_rows, const int32_t* __restrict__ n_rows,
                                    int64_t rows, unsigned char* __restrict__ act) {
+  chain_begin();
   const int nch = (K + 127) / 128;
   const int nb = nch * 16;   // 8-input blocks per position, chunk padding included
   const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -395,8 +397,8 @@ cudaError_t launch_act_records(const uint16_t* x, int64_t ldx, int K, const int3
                                cudaStream_t st) {
   const int64_t n = rows * ((K + 127) / 128) * 16;
   if (n == 0) return cudaSuccess;
-  act_records_kernel<<<int((n + 255) / 256), 256, 0, st>>>(x, ldx, K, src_rows, n_rows, rows, act);
-  return cudaGetLastError();
+  return launch_chained(act_records_kernel, dim3(int((n + 255) / 256)), dim3(256), 0, st, x, ldx, K,
+                        src_rows, n_rows, rows, act);
 }
 
 // ---- pool packing -----------------------------------------------------------
@@ -492,8 +494,7 @@ static cudaError_t launch_tiled_t(TiledArgs a, int max_items, int max_out, cudaS
   int64_t grid = (warps + kTiledWarps - 1) / kTiledWarps;
   if (grid > cap) grid = cap;
   if (grid <= 0) return cudaSuccess;
-  kern<<<int(grid), kTiledThreads, smem, st>>>(a);
-  return cudaGetLastError();
+  return launch_streaming(kern, dim3(int(grid)), dim3(kTiledThreads), smem, st, a);
 }
 
 // gate/up: activation records carry the group sums; the single projection

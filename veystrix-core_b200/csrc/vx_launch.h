@@ -9,6 +9,45 @@
 
 namespace vx {
 
+// Whether chained launches carry the programmatic-serialisation attribute:
+// VXMOE_PDL=0 never, 1 every chained launch, 2 (default) only the short
+// glue kernels (router, permutation, records, combine, exchange) - the
+// streaming GEMV/GEMM kernels launch plainly.  The kernels are correct
+// either way.
+bool chain_enabled(bool streaming);
+
+// Launches `kernel` with programmatic stream serialisation, so that the
+// grid may be scheduled while the previous kernel on the stream finishes;
+// the kernel must call chain_begin() or chain_wait() before its first
+// global-memory access.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_chained_as(bool streaming, void (*kernel)(KArgs...), dim3 grid, dim3 block,
+                                     size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = chain_enabled(streaming) ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_chained(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                  cudaStream_t st, Args... args) {
+  return launch_chained_as(false, kernel, grid, block, smem, st, args...);
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_streaming(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                    cudaStream_t st, Args... args) {
+  return launch_chained_as(true, kernel, grid, block, smem, st, args...);
+}
+
 // Tokens per work item of the tensor-pipe GEMV (an expert's run is cut into
 // items of at most this many positions).  The GEMV's block-diagonal B holds
 // two tokens per MMA.

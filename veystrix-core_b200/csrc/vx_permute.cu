@@ -180,6 +180,7 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(
     int32_t* __restrict__ inverse, int32_t* __restrict__ offsets, int32_t* __restrict__ active,
     int32_t* __restrict__ n_active, int32_t* __restrict__ src_rows, int32_t* __restrict__ err,
     int item_chunk, int32_t* __restrict__ items, int32_t* __restrict__ n_items) {
+  chain_begin();
   extern __shared__ int smem[];
   int* counts = smem;                         // [E]
   int* base = counts + E;                     // [E]  run start
@@ -199,6 +200,130 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(
   perm_scatter(ids, 0, P, E, k_div, src_map, base, hist, order, inverse, src_rows);
 }
 
+// ---- decode-sized inputs: at most kPermSmall ids ---------------------------
+// The same outputs as permute_kernel from one 256-thread CTA with no
+// per-expert histogram: an id's position is the number of valid ids below it
+// plus the equal ids before it (a stable counting rank over at most 256
+// ids), the run offsets come from per-expert counts and one block scan, and
+// the active list and work items from run starts found in sorted order.
+
+constexpr int kPermSmall = 256;
+constexpr int kPermSmallMaxE = 1024;
+
+// Exclusive scan of one int per thread over a 256-thread CTA; *total gets
+// the sum (valid on every thread after the call).
+__device__ int scan256(int v, int* warp_tot, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int inc = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+    if (lane >= o) inc += n;
+  }
+  __syncthreads();   // warp_tot free from a previous call
+  if (lane == 31) warp_tot[warp] = inc;
+  __syncthreads();
+  int before = 0, all = 0;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    const int t = warp_tot[w];
+    before += w < warp ? t : 0;
+    all += t;
+  }
+  *total = all;
+  return before + inc - v;
+}
+
+__global__ void __launch_bounds__(256) permute_small_kernel(
+    const int32_t* __restrict__ ids, int P, int E, int shared_items, int k_div,
+    const int32_t* __restrict__ src_map, int32_t* __restrict__ order,
+    int32_t* __restrict__ inverse, int32_t* __restrict__ offsets, int32_t* __restrict__ active,
+    int32_t* __restrict__ n_active, int32_t* __restrict__ src_rows, int32_t* __restrict__ err,
+    int item_chunk, int32_t* __restrict__ items, int32_t* __restrict__ n_items) {
+  chain_begin();
+  __shared__ int s_key[kPermSmall];
+  __shared__ int s_cnt[kPermSmallMaxE];
+  __shared__ int s_off[kPermSmallMaxE];
+  __shared__ int s_sorted[kPermSmall];   // expert of each sorted position
+  __shared__ int warp_tot[8];
+  const int tid = threadIdx.x;
+  for (int e = tid; e < E; e += 256) s_cnt[e] = 0;
+  int key = 0x7FFFFFFF;
+  bool valid = false;
+  if (tid < P) {
+    const int id = ids[tid];
+    valid = id >= 0 && id < E;
+    if (valid) key = id;
+    else inverse[tid] = -1;
+  }
+  s_key[tid] = key;
+  const int bad = __syncthreads_count(tid < P && !valid);
+  if (valid) atomicAdd(&s_cnt[key], 1);
+  __syncthreads();
+
+  // run offsets: each thread scans a contiguous block of E/256 experts
+  const int per = (E + 255) / 256, e0 = tid * per;
+  int local = 0;
+  for (int j = 0; j < per; ++j)
+    if (e0 + j < E) local += s_cnt[e0 + j];
+  int routed;
+  int run = scan256(local, warp_tot, &routed);
+  for (int j = 0; j < per; ++j)
+    if (e0 + j < E) {
+      s_off[e0 + j] = run;
+      offsets[e0 + j] = run;
+      run += s_cnt[e0 + j];
+    }
+  if (tid == 0) {
+    offsets[E] = routed;
+    if (shared_items >= 0) offsets[E + 1] = routed + shared_items;
+    if (err && bad) atomicAdd(err, bad);
+  }
+  __syncthreads();
+
+  // stable position of each valid id
+  if (valid) {
+    int r = s_off[key];
+    for (int j = 0; j < tid; ++j) r += s_key[j] == key;
+    order[r] = tid;
+    inverse[tid] = r;
+    s_sorted[r] = key;
+    if (src_rows) src_rows[r] = src_map ? src_map[tid] : tid / k_div;
+  }
+  __syncthreads();
+
+  // active experts and items, from the runs in sorted order
+  const bool in = tid < routed;
+  const int ek = in ? s_sorted[tid] : 0;
+  const bool starts = in && (tid == 0 || s_sorted[tid - 1] != ek);
+  const bool istart = in && ((tid - s_off[ek]) % item_chunk == 0);
+  int n_act, n_it;
+  const int ai = scan256(starts ? 1 : 0, warp_tot, &n_act);
+  const int ii = scan256(istart ? 1 : 0, warp_tot, &n_it);
+  if (starts) active[ai] = ek;
+  if (items && istart) {
+    int32_t* it = items + 3 * ii;
+    it[0] = ek;
+    it[1] = tid;
+    it[2] = min(item_chunk, s_off[ek] + s_cnt[ek] - tid);
+  }
+  const int sh_items = shared_items > 0 ? (shared_items + item_chunk - 1) / item_chunk : 0;
+  if (tid == 0) {
+    if (shared_items > 0) active[n_act] = E;
+    *n_active = n_act + (shared_items > 0 ? 1 : 0);
+    if (items) *n_items = n_it + sh_items;
+  }
+  if (items)
+    for (int j = tid; j < sh_items; j += 256) {
+      int32_t* it = items + 3 * (n_it + j);
+      it[0] = E;
+      it[1] = routed + j * item_chunk;
+      it[2] = min(item_chunk, shared_items - j * item_chunk);
+    }
+  if (src_rows)
+    for (int t = tid; t < shared_items; t += 256) src_rows[routed + t] = t;
+}
+
 // ---- prefill-sized inputs: slices of kPermSlice ids -------------------------
 
 constexpr int kPermSlice = 8192;
@@ -212,6 +337,7 @@ int64_t permute_scratch_ints(int64_t P, int E) {
 __global__ void __launch_bounds__(kPermThreads) permute_count_kernel(const int32_t* __restrict__ ids,
                                                                      int64_t P, int E, int32_t* __restrict__ blk,
                                                                      int32_t* __restrict__ err) {
+  chain_begin();
   extern __shared__ int counts[];
   __shared__ int s_bad;
   for (int e = threadIdx.x; e < E; e += kPermThreads) counts[e] = 0;
@@ -230,6 +356,7 @@ __global__ void __launch_bounds__(kPermThreads) permute_scan_kernel(
     int nb, int E, int shared_items, int32_t* __restrict__ blk, int32_t* __restrict__ offsets,
     int32_t* __restrict__ active, int32_t* __restrict__ n_active, int32_t* __restrict__ src_rows,
     int item_chunk, int32_t* __restrict__ items, int32_t* __restrict__ n_items) {
+  chain_begin();
   extern __shared__ int smem[];
   int* counts = smem;           // [E]
   int* base = counts + E;       // [E]
@@ -255,6 +382,7 @@ __global__ void __launch_bounds__(kPermThreads) permute_scatter_kernel(
     const int32_t* __restrict__ ids, int64_t P, int E, int k_div, const int32_t* __restrict__ src_map,
     const int32_t* __restrict__ blk, int32_t* __restrict__ order, int32_t* __restrict__ inverse,
     int32_t* __restrict__ src_rows) {
+  chain_begin();
   extern __shared__ int smem[];
   int* running = smem;          // [E]
   int* hist = running + E;      // [kPermWarps][E]
@@ -276,29 +404,31 @@ cudaError_t launch_permute(const int32_t* ids, int64_t P, int E, int shared_item
                            int32_t* offsets, int32_t* active, int32_t* n_active,
                            int32_t* src_rows, int32_t* err, int item_chunk, int32_t* items,
                            int32_t* n_items, int32_t* blk, cudaStream_t st) {
+  if (P <= kPermSmall && E <= kPermSmallMaxE)
+    return launch_chained(permute_small_kernel, dim3(1), dim3(256), 0, st, ids, int(P), E, shared_items, k_div,
+                          src_map, order, inverse, offsets, active, n_active, src_rows, err, item_chunk, items,
+                          n_items);
   if (P <= kPermMultiMin || blk == nullptr) {
     const size_t smem = size_t(E) * (2 + kPermWarps) * sizeof(int);
     cudaError_t e = set_smem(reinterpret_cast<const void*>(permute_kernel), smem);
     if (e != cudaSuccess) return e;
-    permute_kernel<<<1, kPermThreads, smem, st>>>(ids, int(P), E, shared_items, k_div, src_map, order,
-                                                  inverse, offsets, active, n_active, src_rows, err,
-                                                  item_chunk, items, n_items);
-    return cudaGetLastError();
+    return launch_chained(permute_kernel, dim3(1), dim3(kPermThreads), smem, st, ids, int(P), E,
+                          shared_items, k_div, src_map, order, inverse, offsets, active, n_active,
+                          src_rows, err, item_chunk, items, n_items);
   }
   const int nb = int((P + kPermSlice - 1) / kPermSlice);
-  permute_count_kernel<<<nb, kPermThreads, size_t(E) * sizeof(int), st>>>(ids, P, E, blk, err);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_chained(permute_count_kernel, dim3(nb), dim3(kPermThreads),
+                                 size_t(E) * sizeof(int), st, ids, P, E, blk, err);
   if (e != cudaSuccess) return e;
-  permute_scan_kernel<<<1, kPermThreads, size_t(E) * 2 * sizeof(int), st>>>(
-      nb, E, shared_items, blk, offsets, active, n_active, src_rows, item_chunk, items, n_items);
-  e = cudaGetLastError();
+  e = launch_chained(permute_scan_kernel, dim3(1), dim3(kPermThreads), size_t(E) * 2 * sizeof(int), st,
+                     nb, E, shared_items, blk, offsets, active, n_active, src_rows, item_chunk, items,
+                     n_items);
   if (e != cudaSuccess) return e;
   const size_t smem = size_t(E) * (1 + kPermWarps) * sizeof(int);
   e = set_smem(reinterpret_cast<const void*>(permute_scatter_kernel), smem);
   if (e != cudaSuccess) return e;
-  permute_scatter_kernel<<<nb, kPermThreads, smem, st>>>(ids, P, E, k_div, src_map, blk, order, inverse,
-                                                          src_rows);
-  return cudaGetLastError();
+  return launch_chained(permute_scatter_kernel, dim3(nb), dim3(kPermThreads), smem, st, ids, P, E, k_div,
+                        src_map, blk, order, inverse, src_rows);
 }
 
 // Items of a gather_qmm call: item i = b*M + m has key rhs[b] and x row

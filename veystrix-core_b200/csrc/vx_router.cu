@@ -115,70 +115,69 @@ cudaError_t launch_shared_gate(const uint16_t* x, int T, const vx_q4& seg, uint1
 // ---- softmax + top-k + renorm: one warp per token --------------------------
 // Register-only: lane r keeps the r-th selection.  The selection sum runs in
 // slot order on every lane, as the reference's mass reduction does.
+//
+// Selection order: larger logit first, the smaller expert id among equal
+// logits.  Each candidate is one 32-bit key - the bf16 logit mapped to an
+// order-preserving unsigned 16-bit code (-0 folded onto +0, so zeros tie as
+// equal floats do) above 0xFFFF - id - so a round of the selection is one
+// warp-wide unsigned max (redux) plus a lane-local refresh.
 constexpr int kMaxK = 32;
+
+VX_DEVICE uint32_t logit_key(uint16_t b, int e) {
+  if ((b & 0x7FFFu) == 0) b = 0;                                   // -0 -> +0
+  if ((b & 0x7FFFu) > 0x7F80u) return 0u;                          // NaN: never selected
+  const uint32_t ord = (b & 0x8000u) ? (~uint32_t(b) & 0xFFFFu) : (uint32_t(b) | 0x8000u);
+  return (ord << 16) | (0xFFFFu - uint32_t(e));
+}
+
+VX_DEVICE float key_logit(uint32_t key) {
+  const uint32_t ord = key >> 16;
+  const uint32_t b = (ord & 0x8000u) ? (ord & 0x7FFFu) : (~ord & 0xFFFFu);
+  return bf16_to_f32(uint16_t(b));
+}
 
 template <int PER, bool COHERENT>
 __device__ __forceinline__ void topk_row(const uint16_t* lr, int E, int k, int32_t* inds, uint16_t* scores,
                                          uint16_t* weights, uint16_t* mass) {
   const int lane = threadIdx.x & 31;
-  float l[PER];
+  uint32_t key[PER];
+  float m = -INFINITY;
 #pragma unroll
   for (int j = 0; j < PER; ++j) {
     const int e = lane + 32 * j;
     // logits written by other CTAs of the same launch are read past L1
-    l[j] = e < E ? bf16_to_f32(COHERENT ? __ldcg(lr + e) : lr[e]) : -INFINITY;
+    const uint16_t b = e < E ? (COHERENT ? __ldcg(lr + e) : lr[e]) : uint16_t(0);
+    key[j] = e < E ? logit_key(b, e) : 0u;
+    if (e < E) m = fmaxf(m, bf16_to_f32(b));
   }
-  float m = -INFINITY;
-#pragma unroll
-  for (int j = 0; j < PER; ++j) m = fmaxf(m, l[j]);
   m = warp_max(m);
-  float ex[PER];
   float s = 0.f;
 #pragma unroll
-  for (int j = 0; j < PER; ++j) {
-    ex[j] = (lane + 32 * j < E) ? expf(__fsub_rn(l[j], m)) : 0.f;
-    s += ex[j];
-  }
+  for (int j = 0; j < PER; ++j)
+    if (lane + 32 * j < E) s += expf(__fsub_rn(key_logit(key[j]), m));
   s = warp_sum<32>(s);
   const float inv = __fdiv_rn(1.0f, s);
 
-  uint32_t taken = 0;
-  int my_i = 0;
-  float my_p = 0.f, tot = 0.f;
+  uint32_t lm = 0;
+#pragma unroll
+  for (int j = 0; j < PER; ++j) lm = max(lm, key[j]);
+  uint32_t my_key = 0;
   for (int r = 0; r < k; ++r) {
-    float bv = -INFINITY;
-    int bi = 0x7FFFFFFF;
+    const uint32_t g = __reduce_max_sync(0xFFFFFFFFu, lm);
+    if (lane == r) my_key = g;
+    if (lm == g) {   // the owner: drop the selected key, refresh the local max
+      lm = 0;
 #pragma unroll
-    for (int j = 0; j < PER; ++j) {
-      const int e = lane + 32 * j;
-      if (e < E && !((taken >> j) & 1u) && (l[j] > bv || (l[j] == bv && e < bi))) {
-        bv = l[j];
-        bi = e;
+      for (int j = 0; j < PER; ++j) {
+        if (key[j] == g) key[j] = 0;
+        lm = max(lm, key[j]);
       }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
-      const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
-    const int owner = bi & 31, jj = bi >> 5;
-    float mine = 0.f;
-#pragma unroll
-    for (int j = 0; j < PER; ++j)
-      if (j == jj) mine = ex[j];
-    const float ew = __shfl_sync(0xFFFFFFFFu, mine, owner);
-    if (lane == owner) taken |= 1u << jj;
-    const float pr = bf16r(__fmul_rn(ew, inv));
-    tot = __fadd_rn(tot, pr);
-    if (lane == r) {
-      my_i = bi;
-      my_p = pr;
     }
   }
+  const int my_i = int(0xFFFFu - (my_key & 0xFFFFu));
+  const float my_p = bf16r(__fmul_rn(expf(__fsub_rn(key_logit(my_key), m)), inv));
+  float tot = 0.f;
+  for (int r = 0; r < k; ++r) tot = __fadd_rn(tot, __shfl_sync(0xFFFFFFFFu, my_p, r));
   // mass and renorm (blend 1.0): norm = mass + 1.0*(sum - mass), in bf16.
   const float msum = bf16r(tot);
   const float diff = bf16r(__fsub_rn(msum, msum));
@@ -239,6 +238,7 @@ __global__ void __launch_bounds__(32 * kRouterSlices) router_fused_kernel(
     const uint16_t* __restrict__ x, int T, const uint16_t* __restrict__ wg, int E, int K, int k, vx_q4 seg,
     uint16_t* __restrict__ logits, int32_t* __restrict__ inds, uint16_t* __restrict__ weights,
     uint16_t* __restrict__ sg, int32_t* __restrict__ counters) {
+  chain_begin();
   const int nEB = (E + 15) / 16;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = blockIdx.y * 8;
@@ -282,13 +282,28 @@ __global__ void __launch_bounds__(32 * kRouterSlices) router_fused_kernel(
   const int per = (steps + kRouterSlices - 1) / kRouterSlices;
   const int s0 = warp * per, s1 = min(steps, s0 + per);
   float d[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int s = s0; s < s1; ++s) {
-    const int kk = s * 32 + c * 8;
-    const uint4 wa = ea < E ? ldg_nc(ra + kk) : make_uint4(0, 0, 0, 0);
-    const uint4 wb = eb < E ? ldg_nc(rb + kk) : make_uint4(0, 0, 0, 0);
-    const uint4 xb = tx < T ? __ldg(reinterpret_cast<const uint4*>(rx + kk)) : make_uint4(0, 0, 0, 0);
-    mma16816(d, wa.x, wb.x, wa.y, wb.y, xb.x, xb.y);
-    mma16816(d, wa.z, wb.z, wa.w, wb.w, xb.z, xb.w);
+  // All loads of a batch of steps are issued before its MMAs (same MMA
+  // order as one step at a time), so a warp keeps up to 6 KiB in flight and
+  // a CTA fetches its 64 KiB of router rows in about one memory round trip.
+  constexpr int kBatch = 8;
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+  for (int sb = s0; sb < s1; sb += kBatch) {
+    uint4 wa[kBatch], wb[kBatch], xb[kBatch];
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+      const int s = sb + i;
+      const int kk = s * 32 + c * 8;
+      wa[i] = (s < s1 && ea < E) ? ldg_nc(ra + kk) : zero;
+      wb[i] = (s < s1 && eb < E) ? ldg_nc(rb + kk) : zero;
+      xb[i] = (s < s1 && tx < T) ? __ldg(reinterpret_cast<const uint4*>(rx + kk)) : zero;
+    }
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+      if (sb + i < s1) {
+        mma16816(d, wa[i].x, wb[i].x, wa[i].y, wb[i].y, xb[i].x, xb[i].y);
+        mma16816(d, wa[i].z, wb[i].z, wa[i].w, wb[i].w, xb[i].z, xb[i].w);
+      }
+    }
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) red[warp][lane][i] = d[i];
@@ -330,10 +345,10 @@ cudaError_t launch_router_fused(const uint16_t* x, int T, const uint16_t* wg, in
   if (seg) q = *seg;
   dim3 grid(nEB + 1, nTB);
   per_width(E, [&](auto per) {
-    router_fused_kernel<decltype(per)::value><<<grid, 32 * kRouterSlices, 0, st>>>(x, T, wg, E, K, k, q, logits,
-                                                                                  inds, weights, sg, counters);
+    e = launch_chained(router_fused_kernel<decltype(per)::value>, grid, dim3(32 * kRouterSlices), 0, st, x, T,
+                       wg, E, K, k, q, logits, inds, weights, sg, counters);
   });
-  return cudaGetLastError();
+  return e;
 }
 
 }  // namespace vx

@@ -242,6 +242,7 @@ class ExpertParallelMoE:
             raise ValueError(f"unknown transport {transport!r}")
         self.transport = transport
         self.exchange = None
+        self._side = None
         if transport == "p2p":
             self.exchange = peer_exchange(group, self.capacity_max_tokens, shard.hidden, self.k,
                                           self.E, shard.device)
@@ -265,16 +266,26 @@ class ExpertParallelMoE:
         return self._call_counts(x)
 
     def _call_p2p(self, x):
-        """Every rank passes the same number of tokens."""
+        """Every rank passes the same number of tokens.  The shared expert
+        of the rank's own tokens runs on a second stream, beside the
+        exchange and the routed experts."""
         x = x.contiguous()
         T, d = int(x.shape[0]), int(x.shape[1])
         inds, wts, sg = self.backend.route(x, self.E)
         inds = inds.reshape(T, self.k).contiguous()
         wts = wts.reshape(T, self.k).contiguous()
         ex = self.exchange
+        main = torch.cuda.current_stream(x.device)
+        if self._side is None:
+            self._side = torch.cuda.Stream(x.device)
+        self._side.wait_stream(main)
+        with torch.cuda.stream(self._side):
+            shared = self.backend.shared(x, self.E)
         ex.dispatch(x, inds, wts)
         self.backend.experts_p2p(ex, T)
-        shared = self.backend.shared(x, self.E)
+        main.wait_stream(self._side)
+        if shared is not None:
+            shared.record_stream(main)
         y = torch.empty((T, d), dtype=torch.bfloat16, device=x.device)
         gate = sg.reshape(T).contiguous() if shared is not None else None
         ex.combine(T, inds, shared.contiguous() if shared is not None else None, gate, y)
