@@ -73,18 +73,18 @@ VX_DEVICE uint32_t step_epoch(const EpArgs& a) {
 }
 
 // Publishes this launch's peer stores: the CTA barrier orders its threads'
-// stores before thread 0's system-scope fence (the grid-barrier pattern of
-// cooperative groups, at system scope), the last CTA to arrive on the ticket
-// fences again and raises flag[slot + rank] = e on every rank with a release
-// store, then re-arms the ticket.
+// stores before thread 0's acquire-release ticket add at system scope (the
+// release of this CTA's stores); the CTA that arrives last has acquired every
+// other CTA's release and raises flag[slot + rank] = e on every rank with a
+// release store (cumulative, so it covers all of them), then re-arms the
+// ticket.  No full fence: those cost microseconds each.
 VX_DEVICE void signal_all(const EpArgs& a, int ticket, int slot, uint32_t e) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();
     uint32_t* tk = header(a.buf[a.rank]) + kHdrTicket + ticket;
-    const uint32_t n = atomicAdd(tk, 1u);
+    uint32_t n;
+    asm volatile("atom.acq_rel.sys.global.add.u32 %0, [%1], 1;" : "=r"(n) : "l"(tk) : "memory");
     if (n == gridDim.x * gridDim.y - 1) {
-      __threadfence_system();
       for (int p = 0; p < a.P; ++p) st_release_sys(header(a.buf[p]) + slot + a.rank, e);
       atomicExch(tk, 0u);
     }

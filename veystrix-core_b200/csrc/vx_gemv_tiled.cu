@@ -107,8 +107,9 @@ VX_DEVICE void issue_act(bool leader, uint32_t bar, uint32_t dst_x, const void* 
 // so the heavy stream goes the other way.
 constexpr bool kWeightsByLsu = true;
 
-template <bool GATEUP, int MT, bool XMMA, int STAGES>
-__global__ void __launch_bounds__(kTiledThreads, 2) gemv_tiled_kernel(const __grid_constant__ TiledArgs a) {
+template <bool GATEUP, int MT, bool XMMA, int STAGES, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
+    gemv_tiled_kernel(const __grid_constant__ TiledArgs a) {
   chain_wait();
   constexpr int NP = GATEUP ? 2 : 1;
   constexpr int kRec = NP * MT * kTileRecordUnit;
@@ -117,7 +118,7 @@ __global__ void __launch_bounds__(kTiledThreads, 2) gemv_tiled_kernel(const __gr
   constexpr int kStage = kRec + kTiledItemChunk * kActRecord;
   static_assert(kStage % 128 == 0, "stage size");
   extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ __align__(8) uint64_t bars[kTiledWarps][STAGES];
+  __shared__ __align__(8) uint64_t bars[WARPS][STAGES];
   __shared__ __align__(16) uint32_t zero16[4];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
@@ -133,13 +134,13 @@ __global__ void __launch_bounds__(kTiledThreads, 2) gemv_tiled_kernel(const __gr
   const int tb = g >> 2, ts = c >> 1;
   const int n_items = *a.n_items;
   const int total = n_items * a.tiles_per_item;
-  const int nw = gridDim.x * kTiledWarps;
+  const int nw = gridDim.x * WARPS;
   const uint64_t pol_w = policy_evict_first();
   const uint64_t pol_x = policy_evict_last();
   const int64_t act_pitch = a.act_rows * kActRecord;   // bytes per chunk of activations
 
   // ---- producer cursor: task ti, chunk ci ----
-  int ti = blockIdx.x * kTiledWarps + warp, ci = 0;
+  int ti = blockIdx.x * WARPS + warp, ci = 0;
   int inch = 0;
   uint32_t ixbytes = 0;
   const unsigned char* irec = nullptr;
@@ -334,7 +335,7 @@ __global__ void __launch_bounds__(kTiledThreads, 2) gemv_tiled_kernel(const __gr
     }
   };
 
-  for (int t = blockIdx.x * kTiledWarps + warp; t < total; t += nw) {
+  for (int t = blockIdx.x * WARPS + warp; t < total; t += nw) {
     TiledTask k;
     if (!decode_task<MT>(a, t, k)) continue;   // warp-uniform
     if (k.cnt > 2)
@@ -480,21 +481,37 @@ cudaError_t launch_tile_pack(const vx_q4& a, const vx_q4& b, int nproj, int tile
 
 // ---- launcher ----------------------------------------------------------------
 
-template <bool GATEUP, int MT, bool XMMA>
-static cudaError_t launch_tiled_t(TiledArgs a, int max_items, int max_out, cudaStream_t st) {
+template <bool GATEUP, int MT, bool XMMA, int STAGES, int WARPS>
+static cudaError_t launch_tiled_v(TiledArgs a, int64_t tasks, cudaStream_t st) {
   constexpr int NP = GATEUP ? 2 : 1;
   constexpr int kStage = NP * MT * kTileRecordUnit + kTiledItemChunk * kActRecord;
-  a.tiles_per_item = (max_out + 16 * MT - 1) / (16 * MT);
-  const size_t smem = size_t(kTiledWarps) * kTiledStages * kStage;
-  auto kern = gemv_tiled_kernel<GATEUP, MT, XMMA, kTiledStages>;
+  const size_t smem = size_t(WARPS) * STAGES * kStage;
+  auto kern = gemv_tiled_kernel<GATEUP, MT, XMMA, STAGES, WARPS>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (err != cudaSuccess) return err;
-  const int64_t warps = int64_t(max_items) * a.tiles_per_item;
-  const int64_t cap = int64_t(sm_count()) * 2;   // two resident CTAs per SM, persistent
-  int64_t grid = (warps + kTiledWarps - 1) / kTiledWarps;
+  // persistent: two resident CTAs per SM for the 8-warp shape, one otherwise
+  const int64_t cap = int64_t(sm_count()) * (WARPS == 8 ? 2 : 1);
+  int64_t grid = (tasks + WARPS - 1) / WARPS;
   if (grid > cap) grid = cap;
   if (grid <= 0) return cudaSuccess;
-  return launch_streaming(kern, dim3(int(grid)), dim3(kTiledThreads), smem, st, a);
+  return launch_streaming(kern, dim3(int(grid)), dim3(WARPS * 32), smem, st, a);
+}
+
+// Decode-sized batches have too few (item, row tile) tasks to fill the GPU
+// with warps: each warp then walks its task's chunks with a deep pipeline
+// (kDeepStages - 1 chunks in flight instead of kTiledStages - 1) in 4-warp
+// CTAs, one task per warp.
+constexpr int kDeepStages = 8;
+constexpr int kDeepWarps = 4;
+
+template <bool GATEUP, int MT, bool XMMA>
+static cudaError_t launch_tiled_t(TiledArgs a, int max_items, int max_out, cudaStream_t st) {
+  a.tiles_per_item = (max_out + 16 * MT - 1) / (16 * MT);
+  const int64_t tasks = int64_t(max_items) * a.tiles_per_item;
+  // (a task with only a few chunks, as down's 4, gains nothing from the depth)
+  if (tasks <= int64_t(sm_count()) * kDeepWarps && (a.K_b + 127) / 128 >= kDeepStages)
+    return launch_tiled_v<GATEUP, MT, XMMA, kDeepStages, kDeepWarps>(a, tasks, st);
+  return launch_tiled_v<GATEUP, MT, XMMA, kTiledStages, kTiledWarps>(a, tasks, st);
 }
 
 // gate/up: activation records carry the group sums; the single projection

@@ -140,13 +140,47 @@ template <int PER, bool COHERENT>
 __device__ __forceinline__ void topk_row(const uint16_t* lr, int E, int k, int32_t* inds, uint16_t* scores,
                                          uint16_t* weights, uint16_t* mass) {
   const int lane = threadIdx.x & 31;
+  // Lane owns experts lane*PER .. lane*PER+PER-1 and fetches them with one
+  // or a few vector loads, all issued before any is used (a chain of 2-byte
+  // loads waited on one by one cost microseconds).  Logits written by other
+  // CTAs of the same launch are read past L1.
+  const int e0 = lane * PER;
+  uint32_t raw[PER / 2];
+  constexpr int kVec = PER >= 8 ? 8 : 4;   // bf16 per vector load
+  const bool vec = e0 + PER <= E && E % kVec == 0 && (reinterpret_cast<uintptr_t>(lr) & (2 * kVec - 1)) == 0;
+  if (vec) {
+    if constexpr (PER >= 8) {
+      const uint4* p = reinterpret_cast<const uint4*>(lr + e0);
+      uint4 q[PER / 8];
+#pragma unroll
+      for (int v = 0; v < PER / 8; ++v) q[v] = COHERENT ? __ldcg(p + v) : p[v];
+#pragma unroll
+      for (int v = 0; v < PER / 8; ++v) {
+        raw[4 * v] = q[v].x;
+        raw[4 * v + 1] = q[v].y;
+        raw[4 * v + 2] = q[v].z;
+        raw[4 * v + 3] = q[v].w;
+      }
+    } else {
+      const uint2 q = COHERENT ? __ldcg(reinterpret_cast<const uint2*>(lr + e0))
+                               : *reinterpret_cast<const uint2*>(lr + e0);
+      raw[0] = q.x;
+      raw[1] = q.y;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < PER; j += 2) {
+      const uint32_t lo = e0 + j < E ? (COHERENT ? __ldcg(lr + e0 + j) : lr[e0 + j]) : 0u;
+      const uint32_t hi = e0 + j + 1 < E ? (COHERENT ? __ldcg(lr + e0 + j + 1) : lr[e0 + j + 1]) : 0u;
+      raw[j / 2] = lo | (hi << 16);
+    }
+  }
   uint32_t key[PER];
   float m = -INFINITY;
 #pragma unroll
   for (int j = 0; j < PER; ++j) {
-    const int e = lane + 32 * j;
-    // logits written by other CTAs of the same launch are read past L1
-    const uint16_t b = e < E ? (COHERENT ? __ldcg(lr + e) : lr[e]) : uint16_t(0);
+    const int e = e0 + j;
+    const uint16_t b = uint16_t(raw[j / 2] >> (16 * (j & 1)));
     key[j] = e < E ? logit_key(b, e) : 0u;
     if (e < E) m = fmaxf(m, bf16_to_f32(b));
   }
@@ -154,7 +188,7 @@ __device__ __forceinline__ void topk_row(const uint16_t* lr, int E, int k, int32
   float s = 0.f;
 #pragma unroll
   for (int j = 0; j < PER; ++j)
-    if (lane + 32 * j < E) s += expf(__fsub_rn(key_logit(key[j]), m));
+    if (e0 + j < E) s += expf(__fsub_rn(key_logit(key[j]), m));
   s = warp_sum<32>(s);
   const float inv = __fdiv_rn(1.0f, s);
 
@@ -228,8 +262,8 @@ cudaError_t launch_softmax_topk(const uint16_t* logits, int T, int E, int k, int
 // ---- the fused router: logits, then top-k by the last CTA of each token
 // block, and the shared-expert gate in an extra CTA column ----------------
 // CTA (eb, tb), eb < nEB: the 16 x 8 logits tile of router_logits_kernel,
-// then an arrival on the token block's counter; the CTA that arrives last
-// (after its __threadfence, so every tile is visible) runs softmax/top-k for
+// then an acquire-release arrival on the token block's counter; the CTA that
+// arrives last (every tile is then visible to it) runs softmax/top-k for
 // the block's 8 tokens (one warp each) and resets the counter.  CTA eb == nEB
 // computes sigmoid(shared_expert_gate(x)) for the 8 tokens.  The counters
 // (one per token block) must be zero at launch.
@@ -319,13 +353,22 @@ __global__ void __launch_bounds__(32 * kRouterSlices) router_fused_kernel(
       const int t = t0 + 2 * c + (i & 1);
       if (e < E && t < T) logits[int64_t(t) * E + e] = f32_to_bf16(v[i]);
     }
-    __threadfence();   // this tile before the arrival
+  }
+  // Arrival: the barrier orders the tile's stores before thread 0's
+  // acquire-release add (release of this tile; for the last CTA, acquire of
+  // every other tile, passed to its threads by the second barrier).  No
+  // separate fence: a full fence here cost microseconds on the critical path.
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int prev;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+                 : "=r"(prev)
+                 : "l"(counters + blockIdx.y)
+                 : "memory");
+    s_last = prev == nEB - 1;
   }
   __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(counters + blockIdx.y, 1) == nEB - 1;
-  __syncthreads();
   if (!s_last) return;
-  __threadfence();     // every tile of the token block is visible
   const int t = t0 + warp;
   if (t < T)
     topk_row<PER, true>(logits + int64_t(t) * E, E, k, inds + int64_t(t) * k, nullptr, weights + int64_t(t) * k,
