@@ -196,11 +196,18 @@ static ExpertScratch carve_experts(Carver& c, int T, const BlockDims& dm) {
 }
 
 // permute -> gate/up + SwiGLU -> down, leaving sorted bf16 outputs in s.yd.
+// Positions per work item of each pipeline.
+static int item_chunk(ExpertPath path, const BlockDims& dm) {
+  return path == kPathGemm ? (dm.pool ? kPoolGemmItemChunk : kGemmItemChunk)
+         : path == kPathGemvTiled ? kTiledItemChunk : kItemChunk;
+}
+
 // err_zeroed: the caller cleared s.err earlier on the stream, so no memset
-// node breaks the chain of programmatically serialised kernels.
+// node breaks the chain of programmatically serialised kernels.  permuted:
+// the router already sorted the routes into s (decode-sized batches).
 static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx_moe_weights* W,
                        const BlockDims& dm, const ExpertScratch& s, cudaStream_t st,
-                       bool err_zeroed = false) {
+                       bool err_zeroed = false, bool permuted = false) {
   const int64_t P = int64_t(T) * dm.k;
   const int Ts = dm.shared ? T : 0;
   cudaError_t e = cudaSuccess;
@@ -209,11 +216,11 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
     if (e != cudaSuccess) return vx_cuda_fail(e);
   }
   const ExpertPath path = expert_path(T, dm);
-  const int chunk = path == kPathGemm ? (dm.pool ? kPoolGemmItemChunk : kGemmItemChunk)
-                    : path == kPathGemvTiled ? kTiledItemChunk : kItemChunk;
-  e = launch_permute(routes, P, dm.E, Ts, dm.k, nullptr, s.order, s.inverse, s.offsets, s.active,
-                     s.n_active, s.src_rows, s.err, chunk, s.items, s.n_items, s.blk, st);
-  if (e != cudaSuccess) return vx_cuda_fail(e);
+  if (!permuted) {
+    e = launch_permute(routes, P, dm.E, Ts, dm.k, nullptr, s.order, s.inverse, s.offsets, s.active,
+                       s.n_active, s.src_rows, s.err, item_chunk(path, dm), s.items, s.n_items, s.blk, st);
+    if (e != cudaSuccess) return vx_cuda_fail(e);
+  }
   if (path == kPathGemm) {
     e = launch_gather_border(x, dm.d, dm.d, s.src_rows, s.offsets + dm.E + 1, P + Ts, s.xb, st);
     if (e != cudaSuccess) return vx_cuda_fail(e);
@@ -548,12 +555,12 @@ size_t vx_router_workspace(int32_t T, const vx_moe_weights* W) {
 // and the shared-expert gate (vx_router.cu router_fused_kernel).
 static int router_impl(const uint16_t* x, int T, const vx_moe_weights* W, const BlockDims& dm,
                        uint16_t* logits, int32_t* inds, uint16_t* weights, uint16_t* sg,
-                       int32_t* counters, cudaStream_t st) {
+                       int32_t* counters, cudaStream_t st, const PermSmallArgs* perm = nullptr) {
   profile_mark(st, "");
   const bool gate = sg && W->shared_expert_gate.w;
   cudaError_t e = launch_router_fused(x, T, W->router_w, dm.E, dm.d, dm.k,
                                       gate ? &W->shared_expert_gate : nullptr, logits, inds, weights,
-                                      gate ? sg : nullptr, counters, st);
+                                      gate ? sg : nullptr, counters, perm, st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
   profile_mark(st, "router");
   return VX_OK;
@@ -712,9 +719,16 @@ int vx_moe_block(const uint16_t* x, int32_t T, const vx_moe_weights* W, uint16_t
   if (!weights) weights = w_ws;
   cudaError_t e = cudaMemsetAsync(es.err, 0, 2 * sizeof(int32_t), st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
-  s = router_impl(x, T, W, dm, logits, inds, weights, dm.shared ? sg : nullptr, counters, st);
+  // A decode-sized batch (one token block of the router) is sorted by expert
+  // in the router's last CTA.
+  const bool fuse_perm = T <= 8 && int64_t(T) * dm.k <= kPermSmall && dm.E <= kPermSmallMaxE;
+  PermSmallArgs pa{dm.E, dm.shared ? T : 0, dm.k, item_chunk(expert_path(T, dm), dm), nullptr,
+                   es.order, es.inverse, es.offsets, es.active, es.n_active, es.src_rows, es.err,
+                   es.items, es.n_items};
+  s = router_impl(x, T, W, dm, logits, inds, weights, dm.shared ? sg : nullptr, counters, st,
+                  fuse_perm ? &pa : nullptr);
   if (s) return s;
-  s = run_experts(x, T, inds, W, dm, es, st, true);
+  s = run_experts(x, T, inds, W, dm, es, st, true, fuse_perm);
   if (s) return s;
   e = launch_combine(es.yd, dm.d, es.inverse, weights, T, dm.k, dm.d,
                                  dm.shared ? kSharedInternal : kSharedNone, es.offsets, dm.E, sg,

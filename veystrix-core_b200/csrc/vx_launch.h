@@ -200,6 +200,18 @@ cudaError_t launch_permute(const int32_t* ids, int64_t P, int E, int shared_item
                            int32_t* n_items, int32_t* blk, cudaStream_t st);
 int64_t permute_scratch_ints(int64_t P, int E);
 
+// Decode-sized permutations (at most kPermSmall ids, E <= kPermSmallMaxE) run
+// in one 256-thread CTA: the one-CTA permute kernel, or the fused router's
+// last CTA when it is handed these outputs (PermSmallArgs::order non-null).
+constexpr int kPermSmall = 256;
+constexpr int kPermSmallMaxE = 1024;
+
+struct PermSmallArgs {
+  int E, shared_items, k_div, item_chunk;
+  const int32_t* src_map;
+  int32_t *order, *inverse, *offsets, *active, *n_active, *src_rows, *err, *items, *n_items;
+};
+
 cudaError_t launch_router_logits(const uint16_t* x, int T, const uint16_t* wg, int E, int K,
                                  uint16_t* logits, cudaStream_t st);
 cudaError_t launch_shared_gate(const uint16_t* x, int T, const vx_q4& seg, uint16_t* sg,
@@ -207,11 +219,14 @@ cudaError_t launch_shared_gate(const uint16_t* x, int T, const vx_q4& seg, uint1
 cudaError_t launch_softmax_topk(const uint16_t* logits, int T, int E, int k, int32_t* inds,
                                 uint16_t* scores, uint16_t* weights, uint16_t* mass,
                                 cudaStream_t st);
-// Logits, top-k/renorm and (seg != null) the shared-expert gate in one
+// Logits, top-k/renorm, (seg != null) the shared-expert gate and (perm !=
+// null; T <= 8, T*k <= kPermSmall) the expert sort of the routes in one
 // launch; counters: (T+7)/8 ints of scratch (zeroed by the launcher).
+struct PermSmallArgs;
 cudaError_t launch_router_fused(const uint16_t* x, int T, const uint16_t* wg, int E, int K, int k,
                                 const vx_q4* seg, uint16_t* logits, int32_t* inds, uint16_t* weights,
-                                uint16_t* sg, int32_t* counters, cudaStream_t st);
+                                uint16_t* sg, int32_t* counters, const PermSmallArgs* perm,
+                                cudaStream_t st);
 
 // Expert-parallel exchange buffer of one rank (vx_ep.cu): a 256-byte header
 // (u32 flag_dispatch[8], flag_combine[8], epoch, tickets[3]), then, for a step

@@ -15,6 +15,7 @@
 
 #include "vx_common.cuh"
 #include "vx_launch.h"
+#include "vx_perm_small.cuh"
 
 namespace vx {
 
@@ -271,7 +272,7 @@ template <int PER>
 __global__ void __launch_bounds__(32 * kRouterSlices) router_fused_kernel(
     const uint16_t* __restrict__ x, int T, const uint16_t* __restrict__ wg, int E, int K, int k, vx_q4 seg,
     uint16_t* __restrict__ logits, int32_t* __restrict__ inds, uint16_t* __restrict__ weights,
-    uint16_t* __restrict__ sg, int32_t* __restrict__ counters) {
+    uint16_t* __restrict__ sg, int32_t* __restrict__ counters, PermSmallArgs perm) {
   chain_begin();
   const int nEB = (E + 15) / 16;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -373,15 +374,26 @@ __global__ void __launch_bounds__(32 * kRouterSlices) router_fused_kernel(
   if (t < T)
     topk_row<PER, true>(logits + int64_t(t) * E, E, k, inds + int64_t(t) * k, nullptr, weights + int64_t(t) * k,
                         nullptr);
+  if (perm.order) {
+    // decode-sized batch (one token block): this CTA also sorts the routes
+    // by expert, saving the permutation's own launch
+    __syncthreads();   // every token's ids are written
+    perm_small(perm, inds, T * k);
+  }
   if (threadIdx.x == 0) counters[blockIdx.y] = 0;
 }
 
 cudaError_t launch_router_fused(const uint16_t* x, int T, const uint16_t* wg, int E, int K, int k,
                                 const vx_q4* seg, uint16_t* logits, int32_t* inds, uint16_t* weights,
-                                uint16_t* sg, int32_t* counters, cudaStream_t st) {
+                                uint16_t* sg, int32_t* counters, const PermSmallArgs* perm, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
   if (k > kMaxK) return cudaErrorInvalidValue;
   const int nTB = (T + 7) / 8, nEB = (E + 15) / 16;
+  PermSmallArgs pa{};
+  if (perm) {
+    if (nTB != 1 || T * k > kPermSmall || E > kPermSmallMaxE) return cudaErrorInvalidValue;
+    pa = *perm;
+  }
   cudaError_t e = cudaMemsetAsync(counters, 0, size_t(nTB) * sizeof(int32_t), st);
   if (e != cudaSuccess) return e;
   vx_q4 q{};
@@ -389,7 +401,7 @@ cudaError_t launch_router_fused(const uint16_t* x, int T, const uint16_t* wg, in
   dim3 grid(nEB + 1, nTB);
   per_width(E, [&](auto per) {
     e = launch_chained(router_fused_kernel<decltype(per)::value>, grid, dim3(32 * kRouterSlices), 0, st, x, T,
-                       wg, E, K, k, q, logits, inds, weights, sg, counters);
+                       wg, E, K, k, q, logits, inds, weights, sg, counters, pa);
   });
   return e;
 }
