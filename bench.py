@@ -51,6 +51,9 @@ def parse():
     ap.add_argument("--layers", type=int, default=1,
                     help="> 1: BASELINE config 3, a decode stack of this many distinct layers "
                          "(h += MoE(RMSNorm(h)), mixers identity)")
+    ap.add_argument("--c5", action="store_true",
+                    help="BASELINE config 5: 65,536-token prefill through 4 layers with 32 hot experts "
+                         "(strong scaling over --gpus)")
     ap.add_argument("--ep-transport", default="p2p", choices=("p2p", "collective"),
                     help="expert-parallel exchange: peer stores over NVLink or NCCL all-to-all")
     ap.add_argument("--no-graph", action="store_true",
@@ -340,8 +343,170 @@ def main_stack(args):
     print(json.dumps(line), flush=True)
 
 
+C5_TOKENS = 65536      # 8 sequences x 8,192 tokens
+C5_LAYERS = 4
+C5_HOT = 32            # hot experts, +2.0 on their router logits
+LAYER_FLOPS_PER_TOKEN = 2 * TOPK * 3 * HIDDEN * INTER + 2 * 3 * HIDDEN * SHARED_INTER + 2 * EXPERTS * HIDDEN
+
+
+def main_c5(args):
+    """prefill of 8 x 8,192 = 65,536 tokens through 4
+    stacked layers (h += MoE(RMSNorm(h)), distinct weights per layer), with
+    +2.0 added to the router logits of 32 hot experts chosen with seed 0, so
+    expert load is skewed.  The total is fixed (strong scaling): N ranks take
+    65,536/N tokens each; for N > 1 the experts are split over the ranks and
+    the exchange is the NCCL count transport.  Reports the load imbalance
+    (max/mean routed rows per expert at N = 1, per rank for N > 1) and the
+    device time of the all-to-all calls."""
+    import numpy as np
+    import torch
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    import vxmoe
+    from vxmoe.ep import ExpertParallelMoE
+    T, L = C5_TOKENS // world, C5_LAYERS
+    K, W = args.steps, max(3, args.warmup)
+    hot = np.random.default_rng(0).choice(EXPERTS, C5_HOT, replace=False)
+    bias = torch.zeros(EXPERTS, dtype=torch.bfloat16, device=dev)
+    bias[torch.from_numpy(hot).to(dev)] = 2.0
+    g = torch.Generator(device=dev)
+    gr = torch.Generator(device=dev)
+    layers, weights = [], []
+    for i in range(L):
+        g.manual_seed(200 + 97 * i + rank)
+        gr.manual_seed(300 + i)            # router and shared expert: the same on every rank
+        w = vxmoe.MoEWeights.random(EXPERTS // world, HIDDEN, INTER, SHARED_INTER, TOPK, device=dev,
+                                    generator=g, router_experts=EXPERTS, router_generator=gr).pack()
+        w.router_bias = bias
+        weights.append(w)
+        if world == 1:
+            layers.append(lambda x, w=w: vxmoe.moe_block(x, w))
+        else:
+            layers.append(ExpertParallelMoE(w, EXPERTS, transport="collective"))
+    gain = torch.ones(HIDDEN, dtype=torch.bfloat16, device=dev)
+
+    def step(x):
+        h = x
+        for f in layers:
+            h = h + f(vxmoe.rms_norm(h, gain, 1e-6))
+        return h
+
+    g.manual_seed(7 + rank)
+    xs = torch.randn((2, T, HIDDEN), device=dev, generator=g).to(torch.bfloat16)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if dist is None:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    stream = torch.cuda.current_stream(dev)
+    for i in range(W):
+        step(xs[i % 2])
+    barrier()
+    sampler = ClockSampler(dev.index) if rank == 0 else None
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    for i in range(K):
+        step(xs[i % 2])
+    e1.record(stream)
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    clocks = sampler.stop() if sampler else None
+
+    # end to end: pinned host x -> device -> stack -> pinned host y
+    hx = xs.cpu().pin_memory()
+    hy = torch.empty((T, HIDDEN), dtype=torch.bfloat16).pin_memory()
+    dx = torch.empty((T, HIDDEN), dtype=torch.bfloat16, device=dev)
+    barrier()
+    e0.record(stream)
+    for i in range(K):
+        dx.copy_(hx[i % 2], non_blocking=True)
+        hy.copy_(step(dx), non_blocking=True)
+    e1.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+
+    # load statistics and exchange time (outside the timed regions)
+    if world == 1:
+        r = vxmoe.router(vxmoe.rms_norm(xs[0], gain, 1e-6), weights[0])
+        counts = torch.bincount(r.inds.reshape(-1).long(), minlength=EXPERTS).float()
+        imbalance = {"per": "expert", "max_over_mean": round(float(counts.max() / counts.mean()), 3),
+                     "hot_share": round(float(counts[torch.from_numpy(hot).to(dev)].sum() / counts.sum()), 4)}
+        exchange_ms = 0.0
+    else:
+        for f in layers:
+            f.exchange_events = []
+        step(xs[0])
+        exchange_ms = sum(f.exchange_ms() for f in layers)
+        rows = torch.tensor([float(sum(f.last_stats.get("received_rows", 0) for f in layers))], device=dev)
+        allr = [torch.empty_like(rows) for _ in range(world)]
+        dist.all_gather(allr, rows)
+        vals = torch.cat(allr)
+        imbalance = {"per": "rank", "max_over_mean": round(float(vals.max() / vals.mean()), 3),
+                     "received_rows": [int(v) for v in vals.tolist()]}
+        exchange_ms = max_over_ranks(exchange_ms)
+        for f in layers:
+            f.exchange_events = None
+        layers.clear()
+        barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    _, tf_burst, peak_kind = peaks()
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            tf_sus = float(json.load(fh)["bf16_tflops_sustained"])
+    except Exception:
+        tf_sus = tf_burst
+    step_flops = float(LAYER_FLOPS_PER_TOKEN) * C5_TOKENS * L
+    achieved = step_flops / (ms / K / 1000.0) / 1e12 / world     # per GPU
+    line = {
+        "metric": METRIC, "value": round(K * C5_TOKENS / (ms / 1000.0), 1), "unit": "tokens/s",
+        "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": (f"BASELINE config 5: prefill of 8 x 8,192 = {C5_TOKENS} tokens through "
+                                f"{L} stacked layers (h += MoE(RMSNorm(h))), +2.0 on the router logits of "
+                                f"{C5_HOT} hot experts; d=2048, 512 experts top-10 + shared, I=512, Q4 g32"),
+                   "global_batch": C5_TOKENS, "tokens_per_gpu": T, "layers": L,
+                   "parallelism": (f"ep{world}: {EXPERTS // world} experts per GPU, NCCL count "
+                                   "exchange + all-to-all-v" if world > 1 else "single GPU"),
+                   "l2": "inputs larger than L2 (268 MB of activations per layer, 4 distinct layers)"},
+        "layer_tokens_per_s": round(K * C5_TOKENS * L / (ms / 1000.0), 1),
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": tf_sus, "unit": "TFLOP/s",
+                     "frac": round(achieved / tf_sus, 4), "traffic": None, "peak_kind": peak_kind + " sustained",
+                     "algorithmic_flops_per_step": step_flops,
+                     "note": "whole step: routed + shared expert + router MMA flops per GPU over the step time"},
+        "load_imbalance": imbalance,
+        "all_to_all_ms_per_step": round(exchange_ms, 3),
+        "e2e": {"value": round(K * C5_TOKENS / (e2e_ms / 1000.0), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": T * HIDDEN * 2 * world, "d2h_bytes_per_step": T * HIDDEN * 2 * world},
+        "cpu_baseline": None,
+        "clocks": clocks,
+        "gpu_launches": None,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
+    if args.c5 and args.impl != "reference":
+        return main_c5(args)
     if args.layers > 1 and args.impl != "reference":
         return main_stack(args)
     rank = int(os.environ.get("RANK", "0"))

@@ -101,6 +101,10 @@ typedef struct vx_moe_weights {
    * batches and the tcgen05 grouped GEMM once the batch averages at least
    * four routed positions per expert (T*top_k >= 4*num_experts). */
   int32_t expert_path;
+  /* bf16 [E] added to the bf16 router logits before softmax/top-k (rounded
+   * to bf16 again), or NULL.  The skewed-load benchmark configuration adds
+   * +2.0 to the logits of its hot experts this way. */
+  const uint16_t* router_bias;
 } vx_moe_weights;
 
 #define VX_PATH_AUTO 0

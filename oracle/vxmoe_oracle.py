@@ -272,14 +272,19 @@ def renorm(scores, mass, blend: float = 1.0) -> np.ndarray:
     return bf16_round(scores / norm)
 
 
-def router(x, wg, k: int, logits=None) -> RouterOut:
+def router(x, wg, k: int, logits=None, bias=None) -> RouterOut:
     """Router chain of ``adaptive_topk.py:59-65`` plus renorm ``:257-262``.
 
     ``logits`` may be supplied (e.g. the device's own logits) to check the
-    softmax/top-k stage on identical inputs.
+    softmax/top-k stage on identical inputs.  ``bias`` ([E], bf16 values) is
+    added to the bf16 logits before softmax/top-k and the sum rounded to bf16
+    (the skewed-load benchmark's +2.0 on hot experts); supplied logits are
+    taken as already biased.
     """
     if logits is None:
         logits = router_logits(x, wg)
+        if bias is not None:
+            logits = bf16_round(f32(bf16_round(logits)) + f32(bias)[None, :])
     logits = bf16_round(logits)
     probs = softmax_bf16(logits)
     inds = topk_order(logits, k)

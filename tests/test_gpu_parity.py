@@ -190,6 +190,33 @@ def test_softmax_topk_shapes(E, k):
     np.testing.assert_array_equal(out.inds.cpu().numpy(), ref.inds)
 
 
+def test_router_bias_skews_routing(prod_params):
+    """A bf16 logit bias (the skewed-load configuration's +2.0 on 32 hot
+    experts) is added to the bf16 logits before softmax/top-k: logits within
+    one ulp of the biased float64 oracle, ids bit-exact against the oracle on
+    the device's own logits, and most slots go to the hot experts."""
+    import vxmoe
+    p = prod_params
+    w = weights_from_oracle(p)
+    rng = np.random.default_rng(3)
+    hot = rng.choice(512, 32, replace=False)
+    bias = np.zeros(512, np.float32)
+    bias[hot] = 2.0
+    w.router_bias = torch.from_numpy(bias).to(torch.bfloat16).to(DEV)
+    x = O.make_x(6, 32, 2048)
+    r = vxmoe.router(bf16_t(x), w)
+    ref = O.router(x, p.router_w, 10, bias=bias)
+    assert_bf16_close(np32(r.logits), ref.logits, min_exact=0.99, what="biased router logits")
+    own = O.router(None, None, 10, logits=np32(r.logits))
+    np.testing.assert_array_equal(r.inds.cpu().numpy(), own.inds)
+    assert np.isin(r.inds.cpu().numpy(), hot).mean() > 0.5
+    y = vxmoe.moe_block(bf16_t(x), w)      # the block takes the same routes
+    _, inds, _ = vxmoe.moe_block(bf16_t(x), w, return_routing=True)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(inds.cpu().numpy(), r.inds.cpu().numpy())
+    assert torch.isfinite(y.float()).all()
+
+
 def test_router_full_production(prod_params):
     """Device logits within one bf16 ulp of the float64 oracle; ids bit-exact
     against the oracle run on the device's own logits, and equal to the

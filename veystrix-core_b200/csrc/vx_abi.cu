@@ -560,7 +560,7 @@ static int router_impl(const uint16_t* x, int T, const vx_moe_weights* W, const 
   const bool gate = sg && W->shared_expert_gate.w;
   cudaError_t e = launch_router_fused(x, T, W->router_w, dm.E, dm.d, dm.k,
                                       gate ? &W->shared_expert_gate : nullptr, logits, inds, weights,
-                                      gate ? sg : nullptr, counters, perm, st);
+                                      gate ? sg : nullptr, counters, perm, W->router_bias, st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
   profile_mark(st, "router");
   return VX_OK;

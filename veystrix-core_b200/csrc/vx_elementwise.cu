@@ -17,8 +17,8 @@ __global__ void __launch_bounds__(256) combine_kernel(
     const uint16_t* __restrict__ shared_y, const uint16_t* __restrict__ shared,
     const uint16_t* __restrict__ shared_gate, uint16_t* __restrict__ y) {
   chain_begin();
-  const int t = blockIdx.y;
-  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 2;
+  const int t = blockIdx.x;
+  const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 2;   // rows on x: no 65,535 limit
   if (c >= d) return;
   float a0 = 0.f, a1 = 0.f;
   for (int s = 0; s < k; ++s) {
@@ -63,7 +63,7 @@ cudaError_t launch_combine(const uint16_t* yd, int64_t ldy, const int32_t* inver
                            const uint16_t* shared_y, const uint16_t* shared,
                            const uint16_t* shared_gate, uint16_t* y, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  dim3 grid((d / 2 + 255) / 256, T);
+  dim3 grid(T, (d / 2 + 255) / 256);
   return launch_chained(combine_kernel, grid, dim3(256), 0, st, yd, ldy, inverse, weights, T, k, d,
                         int(mode), offsets, E, sg, shared_y, shared, shared_gate, y);
 }
@@ -121,8 +121,8 @@ __global__ void __launch_bounds__(256) combine_partial_kernel(
     const uint16_t* __restrict__ yd, int64_t ldy, const int32_t* __restrict__ inverse,
     const uint16_t* __restrict__ weights, int k, int d, float* __restrict__ out) {
   chain_begin();
-  const int t = blockIdx.y;
-  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 2;
+  const int t = blockIdx.x;
+  const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 2;   // rows on x: no 65,535 limit
   if (c >= d) return;
   float a0 = 0.f, a1 = 0.f;
   for (int s = 0; s < k; ++s) {
@@ -140,7 +140,7 @@ cudaError_t launch_combine_partial(const uint16_t* yd, int64_t ldy, const int32_
                                    const uint16_t* weights, int T, int k, int d, float* out,
                                    cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  dim3 grid((d / 2 + 255) / 256, T);
+  dim3 grid(T, (d / 2 + 255) / 256);
   return launch_chained(combine_partial_kernel, grid, dim3(256), 0, st, yd, ldy, inverse, weights, k, d,
                         out);
 }
@@ -150,8 +150,8 @@ __global__ void unpermute_kernel(const uint16_t* __restrict__ yd, int64_t ldy,
                                  const int32_t* __restrict__ inverse, int k, int d,
                                  uint16_t* __restrict__ out) {
   chain_begin();
-  const int64_t pair = blockIdx.y;
-  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 2;
+  const int64_t pair = blockIdx.x;
+  const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 2;   // rows on x: no 65,535 limit
   if (c >= d) return;
   const int pos = inverse[pair];
   uint32_t v = 0;
@@ -162,7 +162,7 @@ __global__ void unpermute_kernel(const uint16_t* __restrict__ yd, int64_t ldy,
 cudaError_t launch_unpermute(const uint16_t* yd, int64_t ldy, const int32_t* inverse, int T,
                              int k, int d, uint16_t* out, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  dim3 grid((d / 2 + 255) / 256, T * k);
+  dim3 grid(T * k, (d / 2 + 255) / 256);
   return launch_chained(unpermute_kernel, grid, dim3(256), 0, st, yd, ldy, inverse, k, d, out);
 }
 

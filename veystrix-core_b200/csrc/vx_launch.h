@@ -221,12 +221,13 @@ cudaError_t launch_softmax_topk(const uint16_t* logits, int T, int E, int k, int
                                 cudaStream_t st);
 // Logits, top-k/renorm, (seg != null) the shared-expert gate and (perm !=
 // null; T <= 8, T*k <= kPermSmall) the expert sort of the routes in one
-// launch; counters: (T+7)/8 ints of scratch (zeroed by the launcher).
+// launch; bias (bf16 [E] or null) is added to the bf16 logits; counters:
+// (T+7)/8 ints of scratch (zeroed by the launcher).
 struct PermSmallArgs;
 cudaError_t launch_router_fused(const uint16_t* x, int T, const uint16_t* wg, int E, int K, int k,
                                 const vx_q4* seg, uint16_t* logits, int32_t* inds, uint16_t* weights,
                                 uint16_t* sg, int32_t* counters, const PermSmallArgs* perm,
-                                cudaStream_t st);
+                                const uint16_t* bias, cudaStream_t st);
 
 // Expert-parallel exchange buffer of one rank (vx_ep.cu): a 256-byte header
 // (u32 flag_dispatch[8], flag_combine[8], epoch, tickets[3]), then, for a step

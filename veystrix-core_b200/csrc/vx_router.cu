@@ -272,7 +272,8 @@ template <int PER>
 __global__ void __launch_bounds__(32 * kRouterSlices) router_fused_kernel(
     const uint16_t* __restrict__ x, int T, const uint16_t* __restrict__ wg, int E, int K, int k, vx_q4 seg,
     uint16_t* __restrict__ logits, int32_t* __restrict__ inds, uint16_t* __restrict__ weights,
-    uint16_t* __restrict__ sg, int32_t* __restrict__ counters, PermSmallArgs perm) {
+    uint16_t* __restrict__ sg, int32_t* __restrict__ counters, PermSmallArgs perm,
+    const uint16_t* __restrict__ bias) {
   chain_begin();
   const int nEB = (E + 15) / 16;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -352,7 +353,11 @@ __global__ void __launch_bounds__(32 * kRouterSlices) router_fused_kernel(
     for (int i = 0; i < 4; ++i) {
       const int e = (i < 2) ? ea : eb;
       const int t = t0 + 2 * c + (i & 1);
-      if (e < E && t < T) logits[int64_t(t) * E + e] = f32_to_bf16(v[i]);
+      if (e < E && t < T) {
+        float l = bf16r(v[i]);
+        if (bias) l = bf16r(__fadd_rn(l, bf16_to_f32(bias[e])));   // bf16 logits + bf16 bias
+        logits[int64_t(t) * E + e] = f32_to_bf16(l);
+      }
     }
   }
   // Arrival: the barrier orders the tile's stores before thread 0's
@@ -385,7 +390,8 @@ __global__ void __launch_bounds__(32 * kRouterSlices) router_fused_kernel(
 
 cudaError_t launch_router_fused(const uint16_t* x, int T, const uint16_t* wg, int E, int K, int k,
                                 const vx_q4* seg, uint16_t* logits, int32_t* inds, uint16_t* weights,
-                                uint16_t* sg, int32_t* counters, const PermSmallArgs* perm, cudaStream_t st) {
+                                uint16_t* sg, int32_t* counters, const PermSmallArgs* perm,
+                                const uint16_t* bias, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
   if (k > kMaxK) return cudaErrorInvalidValue;
   const int nTB = (T + 7) / 8, nEB = (E + 15) / 16;
@@ -401,7 +407,7 @@ cudaError_t launch_router_fused(const uint16_t* x, int T, const uint16_t* wg, in
   dim3 grid(nEB + 1, nTB);
   per_width(E, [&](auto per) {
     e = launch_chained(router_fused_kernel<decltype(per)::value>, grid, dim3(32 * kRouterSlices), 0, st, x, T,
-                       wg, E, K, k, q, logits, inds, weights, sg, counters, pa);
+                       wg, E, K, k, q, logits, inds, weights, sg, counters, pa, bias);
   });
   return e;
 }

@@ -58,6 +58,7 @@ class VxMoEWeights(ctypes.Structure):
         ("num_experts", c_int32), ("hidden", c_int32), ("top_k", c_int32),
         ("pool", ctypes.POINTER(VxMoEPool)),
         ("expert_path", c_int32),
+        ("router_bias", c_void_p),
     ]
 
 

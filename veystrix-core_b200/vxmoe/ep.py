@@ -183,7 +183,7 @@ class CudaBackend:
                 self.shared_w.pack(shard.pool.down_rows)
 
     def route(self, x, num_experts):
-        r = ops.route(x, self.router_w, self.w.top_k, self.seg)
+        r = ops.route(x, self.router_w, self.w.top_k, self.seg, router_bias=self.w.router_bias)
         return r.inds, r.weights, r.shared_gate
 
     def experts_partial(self, xr, ids, scores):
@@ -213,10 +213,12 @@ def shard_weights(w: "ops.MoEWeights", rank: int, world: int) -> "ops.MoEWeights
     def part(p):
         return ops.Q4Projection(p.weight[sl], p.scales[sl], p.biases[sl])
 
-    return ops.MoEWeights(part(w.gate), part(w.up), part(w.down), router_w=w.router_w,
-                          shared_gate=w.shared_gate, shared_up=w.shared_up,
-                          shared_down=w.shared_down, shared_expert_gate=w.shared_expert_gate,
-                          top_k=w.top_k, device=w.device, check_router=False)
+    out = ops.MoEWeights(part(w.gate), part(w.up), part(w.down), router_w=w.router_w,
+                         shared_gate=w.shared_gate, shared_up=w.shared_up,
+                         shared_down=w.shared_down, shared_expert_gate=w.shared_expert_gate,
+                         top_k=w.top_k, device=w.device, check_router=False)
+    out.router_bias = w.router_bias
+    return out
 
 
 class ExpertParallelMoE:
@@ -247,9 +249,26 @@ class ExpertParallelMoE:
             self.exchange = peer_exchange(group, self.capacity_max_tokens, shard.hidden, self.k,
                                           self.E, shard.device)
         self.last_stats = {}
+        self.exchange_events = None   # a list: record the device time of every all-to-all
 
     def _a2a(self, out, inp, out_splits, in_splits):
+        timed = self.exchange_events is not None and torch.cuda.is_available() and out.is_cuda
+        if timed:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
         dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+        if timed:
+            e1.record()
+            self.exchange_events.append((e0, e1))
+
+    def exchange_ms(self) -> float:
+        """Milliseconds the recorded all-to-all calls took on the device
+        (synchronises); recording is on while ``exchange_events`` is a list."""
+        if not self.exchange_events:
+            return 0.0
+        torch.cuda.synchronize()
+        return float(sum(a.elapsed_time(b) for a, b in self.exchange_events))
 
     # Decode-sized batches take the fixed-capacity exchange: every rank sends
     # every destination a block of T rows (token order; rows of tokens with no

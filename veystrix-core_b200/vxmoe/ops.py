@@ -198,6 +198,9 @@ class MoEWeights:
         # expert pipeline: _lib.PATH_AUTO (GEMV for decode-sized batches,
         # tcgen05 GEMM from four routed positions per expert), PATH_GEMV, PATH_GEMM
         self.expert_path = _lib.PATH_AUTO
+        # bf16 [E] added to the bf16 router logits (None: no bias); the
+        # skewed-load benchmark puts +2.0 on its hot experts this way
+        self.router_bias: Optional[torch.Tensor] = None
 
     def pack(self, down_rows: int = 32) -> "MoEWeights":
         """Re-tile the experts into the resident pool the decode kernels
@@ -239,6 +242,9 @@ class MoEWeights:
         if self.pool is not None:
             s.pool = ctypes.pointer(self.pool.vx())
         s.expert_path = int(self.expert_path)
+        if self.router_bias is not None:   # one value per router row (all experts of the layer)
+            n_router = int(self.router_w.shape[0]) if self.router_w is not None else self.num_experts
+            s.router_bias = _ptr(_bias(self.router_bias, n_router))
         return s
 
     def nbytes_per_expert(self) -> int:
@@ -469,13 +475,26 @@ class RouterOut:
 def router(x: torch.Tensor, weights: MoEWeights) -> RouterOut:
     """Router of the block: bf16 logits, top-k, renormalised weights and the
     shared expert's sigmoid gate."""
-    return route(x, weights.router_w, weights.top_k, weights.shared_expert_gate)
+    return route(x, weights.router_w, weights.top_k, weights.shared_expert_gate,
+                 router_bias=weights.router_bias)
+
+
+def _bias(b: torch.Tensor, E: int) -> torch.Tensor:
+    """The bias tensor itself (its pointer goes to the library, so no copy)."""
+    _require_cuda(b, "router_bias")
+    if b.dtype != torch.bfloat16:
+        raise TypeError(f"router_bias must be bfloat16, got {b.dtype}")
+    if b.numel() != E or not b.is_contiguous():
+        raise ValueError(f"router_bias must be a contiguous vector of {E} values")
+    return b
 
 
 def route(x: torch.Tensor, router_w: torch.Tensor, top_k: int,
-          shared_expert_gate: Optional[Q4Projection] = None) -> RouterOut:
+          shared_expert_gate: Optional[Q4Projection] = None,
+          router_bias: Optional[torch.Tensor] = None) -> RouterOut:
     """The router from its own tensors: bf16 gate [E, d] and, optionally,
-    the Q4 shared-expert gate [1, 1, d/8] (no expert bank needed)."""
+    the Q4 shared-expert gate [1, 1, d/8] and a bf16 logit bias [E] (no
+    expert bank needed)."""
     x = _bf16(x, "x")
     router_w = _bf16(router_w, "router_w")
     E, d = int(router_w.shape[0]), int(router_w.shape[1])
@@ -492,6 +511,8 @@ def route(x: torch.Tensor, router_w: torch.Tensor, top_k: int,
     if shared_expert_gate is not None:
         st.shared_expert_gate = shared_expert_gate.vx()
     st.num_experts, st.hidden, st.top_k = E, d, k
+    if router_bias is not None:
+        st.router_bias = _ptr(_bias(router_bias, E))
     lib = _lib.load()
     ws = _WS.get(lib.vx_router_workspace(T, ctypes.byref(st)), dev)
     _lib.check(lib.vx_router(x2.data_ptr(), T, ctypes.byref(st), logits.data_ptr(),
