@@ -390,7 +390,11 @@ def main_c5(args):
         if world == 1:
             layers.append(lambda x, w=w: vxmoe.moe_block(x, w))
         else:
-            layers.append(ExpertParallelMoE(w, EXPERTS, transport="collective"))
+            # peer transport: fixed blocks of T rows per peer, stored over NVLink by the
+            # kernels; collective: NCCL count exchange + all-to-all-v
+            p2p = args.ep_transport == "p2p"
+            layers.append(ExpertParallelMoE(w, EXPERTS, transport=args.ep_transport,
+                                            capacity=T if p2p else 256))
     gain = torch.ones(HIDDEN, dtype=torch.bfloat16, device=dev)
 
     def step(x):
@@ -454,18 +458,26 @@ def main_c5(args):
             f.exchange_events = []
         step(xs[0])
         exchange_ms = sum(f.exchange_ms() for f in layers)
-        rows = torch.tensor([float(sum(f.last_stats.get("received_rows", 0) for f in layers))], device=dev)
-        allr = [torch.empty_like(rows) for _ in range(world)]
-        dist.all_gather(allr, rows)
-        vals = torch.cat(allr)
+        # routed slots each rank's expert shard receives (first layer, all ranks' tokens)
+        r = vxmoe.route(vxmoe.rms_norm(xs[0], gain, 1e-6), weights[0].router_w, TOPK,
+                        router_bias=bias)
+        vals = torch.bincount(r.inds.reshape(-1).long() // (EXPERTS // world), minlength=world).double()
+        dist.all_reduce(vals)
         imbalance = {"per": "rank", "max_over_mean": round(float(vals.max() / vals.mean()), 3),
-                     "received_rows": [int(v) for v in vals.tolist()]}
+                     "routed_slots": [int(v) for v in vals.tolist()]}
         exchange_ms = max_over_ranks(exchange_ms)
         for f in layers:
             f.exchange_events = None
+        timeouts = 0
+        from vxmoe import ep as ep_mod
+        for ex in ep_mod._EXCHANGES.values():
+            timeouts |= ex.errors()
         layers.clear()
+        ep_mod.close_exchanges()
         barrier()
         dist.destroy_process_group()
+        if timeouts:
+            raise RuntimeError(f"rank {rank}: an expert-parallel wait ran out (bits {timeouts})")
     if rank != 0:
         return
     _, tf_burst, peak_kind = peaks()
@@ -484,8 +496,11 @@ def main_c5(args):
                                 f"{L} stacked layers (h += MoE(RMSNorm(h))), +2.0 on the router logits of "
                                 f"{C5_HOT} hot experts; d=2048, 512 experts top-10 + shared, I=512, Q4 g32"),
                    "global_batch": C5_TOKENS, "tokens_per_gpu": T, "layers": L,
-                   "parallelism": (f"ep{world}: {EXPERTS // world} experts per GPU, NCCL count "
-                                   "exchange + all-to-all-v" if world > 1 else "single GPU"),
+                   "parallelism": ((f"ep{world}: {EXPERTS // world} experts per GPU, " +
+                                    ("blocks of T rows stored into the peers over NVLink by the dispatch "
+                                     "and combine kernels" if args.ep_transport == "p2p"
+                                     else "NCCL count exchange + all-to-all-v"))
+                                   if world > 1 else "single GPU"),
                    "l2": "inputs larger than L2 (268 MB of activations per layer, 4 distinct layers)"},
         "layer_tokens_per_s": round(K * C5_TOKENS * L / (ms / 1000.0), 1),
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": tf_sus, "unit": "TFLOP/s",
@@ -493,7 +508,10 @@ def main_c5(args):
                      "algorithmic_flops_per_step": step_flops,
                      "note": "whole step: routed + shared expert + router MMA flops per GPU over the step time"},
         "load_imbalance": imbalance,
-        "all_to_all_ms_per_step": round(exchange_ms, 3),
+        # device time of the NCCL all-to-all calls; the peer transport's stores run inside the
+        # dispatch and combine kernels and have no separate time
+        "all_to_all_ms_per_step": (round(exchange_ms, 3) if world > 1 and args.ep_transport != "p2p"
+                                   else None),
         "e2e": {"value": round(K * C5_TOKENS / (e2e_ms / 1000.0), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": T * HIDDEN * 2 * world, "d2h_bytes_per_step": T * HIDDEN * 2 * world},
         "cpu_baseline": None,

@@ -225,7 +225,12 @@ class ExpertParallelMoE:
     """The block with its routed experts split over the process group."""
 
     def __init__(self, shard: "ops.MoEWeights", num_experts: int, group=None, backend=None,
-                 transport: str = "auto"):
+                 transport: str = "auto", capacity: int = 256):
+        """``capacity``: the largest per-rank batch that takes the fixed-block
+        exchange (peer stores, or the equal-split all-to-all); the peer
+        transport's buffers are sized for it (about 3 * world * capacity * d * 4
+        bytes per rank).  Larger batches use the count exchange."""
+        self.capacity_max_tokens = int(capacity)
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -270,12 +275,12 @@ class ExpertParallelMoE:
         torch.cuda.synchronize()
         return float(sum(a.elapsed_time(b) for a, b in self.exchange_events))
 
-    # Decode-sized batches take the fixed-capacity exchange: every rank sends
-    # every destination a block of T rows (token order; rows of tokens with no
-    # expert there carry ids -1 and cost no expert work), so no counts travel
-    # to the host and the step is graph-capturable.  Larger batches exchange
-    # only the rows that are needed, after a count all-to-all.
-    capacity_max_tokens = 256
+    # Batches up to the capacity take the fixed-block exchange: every rank
+    # sends every destination a block of T rows (token order; rows of tokens
+    # with no expert there carry ids -1 and cost no expert work, and the peer
+    # transport does not even store them), so no counts travel to the host and
+    # the step is graph-capturable.  Larger batches exchange only the rows
+    # that are needed, after a count all-to-all.
 
     def __call__(self, x):
         if int(x.shape[0]) <= self.capacity_max_tokens:
