@@ -38,6 +38,9 @@ def _per_slot_ref(p, x, routes):
     (dict(seed=32, experts=8, hidden=160, inter=96, shared_inter=32, top_k=2), 40, None),     # ragged K, N
     (dict(seed=33, experts=8, hidden=512, inter=256, shared_inter=32, top_k=3), 150, 0),      # a 150-token expert
     (dict(seed=34, experts=32, hidden=384, inter=224, shared_inter=32, top_k=8), 17, None),   # cnt 17, 33 ...
+    # >= 128 positions per expert: the pool kernel's 128-wide items
+    (dict(seed=35, experts=8, hidden=256, inter=128, shared_inter=32, top_k=2), 600, None),
+    (dict(seed=36, experts=8, hidden=512, inter=256, shared_inter=32, top_k=3), 400, 0),      # 400-token expert
 ])
 @pytest.mark.parametrize("packed", [False, True])
 def test_gemm_per_slot_outputs_match_qmm_oracle(cfg, T, skew, packed):
@@ -57,8 +60,11 @@ def test_gemm_per_slot_outputs_match_qmm_oracle(cfg, T, skew, packed):
     ref = _per_slot_ref(p, x, routes)
     # h is rounded to bf16 between the two GEMMs; where the float32 tensor-core
     # sum and the float64 oracle sum round h differently (1 ulp), the down
-    # output moves by ~1e-3 of its rms - many ulps for outputs near zero.
-    assert_bf16_close(np32(out), ref, max_ulp=2, min_exact=0.9, floor=2.0 ** -9,
+    # output moves by ~1e-3 of its rms - many ulps for outputs near zero (the
+    # more tokens, the more such outliers: 5 ulps at 8 % of the rms at T=600,
+    # 32 ulps at 3 % of the rms - 0.5 % of the rms absolute - at T=400, where
+    # the array and the pool kernels agree with each other bit for bit).
+    assert_bf16_close(np32(out), ref, max_ulp=2, min_exact=0.9, floor=2.0 ** -7,
                       what=f"gemm per-slot T={T}")
     assert O.normwise_error(np32(out), ref) < 4e-3
 
@@ -82,20 +88,22 @@ def test_gemm_block_matches_float64_reference(packed):
     assert O.normwise_error(got, ref) <= 1.5 * O.normwise_error(out.y, ref) + 2e-3
 
 
-def test_gemm_block_pool_kernel_matches_array_kernel():
+@pytest.mark.parametrize("T", [32, 600])   # 600 tokens: 150 positions per expert, 128-wide items
+def test_gemm_block_pool_kernel_matches_array_kernel(T):
     """The persistent kernel over the tiled pool and the kernel reading the MLX
     arrays dequantise identically; the pool kernel sums the down projection
     in two interleaved accumulators (even and odd 64-input blocks), so the
-    float32 sums may round differently: within one bf16 ulp."""
+    float32 sums may round differently: within one bf16 ulp, rarely two (seen
+    at T=600)."""
     import vxmoe
     from helpers import ulp_diff_bf16
     p = O.make_params(seed=43, experts=16, hidden=256, inter=128, shared_inter=64, top_k=4)
-    x = bf16_t(O.make_x(44, 32, p.hidden))
+    x = bf16_t(O.make_x(44, T, p.hidden))
     a = vxmoe.moe_block(x, weights_from_oracle(p))
     b = vxmoe.moe_block(x, weights_from_oracle(p).pack())
     torch.cuda.synchronize()
     d = ulp_diff_bf16(np32(a), np32(b))
-    assert d.max() <= 1 and float(np.mean(d == 0)) > 0.97
+    assert d.max() <= 2 and float(np.mean(d <= 1)) > 0.9999 and float(np.mean(d == 0)) > 0.97
 
 
 @pytest.mark.slow
