@@ -574,7 +574,10 @@ def main():
             if args.layout == "tiled":
                 w.pack()
             pools.append(w)
-            ep = ExpertParallelMoE(w, EXPERTS, transport=args.ep_transport)
+            # the peer transport carries the whole batch (prefill sizes included) in
+            # fixed blocks; the collective one switches to the count exchange above 256
+            ep = ExpertParallelMoE(w, EXPERTS, transport=args.ep_transport,
+                                   capacity=max(256, T) if args.ep_transport == "p2p" else 256)
             plain.append(ep)
             graphed = args.ep_transport == "p2p" and not args.no_graph
             layers.append(GraphedExpertParallel(ep, T) if graphed else ep)

@@ -67,6 +67,31 @@ def test_ep_single_rank_equals_block(transport, packed):
         dist.destroy_process_group()
 
 
+def test_ep_p2p_prefill_capacity_equals_block():
+    """A capacity above the decode default carries a prefill-sized batch over
+    the peer transport (the tcgen05 GEMM pipeline on the received rows)."""
+    import vxmoe
+    from vxmoe import ep as E
+    dist, dev = _init_single(29656)
+    try:
+        w = _weights(dev)
+        shard = E.shard_weights(w, 0, 1)
+        w.pack()
+        shard.pack()
+        layer = E.ExpertParallelMoE(shard, w.num_experts, transport="p2p", capacity=1024)
+        for T in (300, 700):
+            x = torch.randn((T, w.hidden), device=dev).to(torch.bfloat16)
+            y = layer(x)
+            ref = vxmoe.moe_block(x, w)
+            torch.cuda.synchronize()
+            assert layer.last_stats["mode"] == "p2p"
+            np.testing.assert_array_equal(_bits(y), _bits(ref))
+        assert layer.exchange.errors() == 0
+    finally:
+        E.close_exchanges()
+        dist.destroy_process_group()
+
+
 def test_ep_p2p_graph_replay_equals_eager():
     from vxmoe import ep as E
     dist, dev = _init_single(29654)
