@@ -1,0 +1,58 @@
+"""A layer loaded from a checkpoint-shaped safetensors file runs the block
+with the same bits as the same weights built in memory, and the block works at
+the real checkpoint's width (d=2560, I=Is=640, models/flashnext/preflight.py:
+53-56) within the block tolerance of the oracle."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import vxmoe_oracle as O
+from helpers import bf16_t, np32, weights_from_oracle
+from test_loader_cpu import checkpoint_tensors
+
+pytestmark = pytest.mark.gpu
+
+
+def test_loaded_layer_equals_in_memory_weights(tmp_path):
+    import vxmoe
+    from vxmoe import loader as L
+    p = O.make_params(seed=61, experts=32, hidden=512, inter=256, shared_inter=128, top_k=4)
+    tensors, bf16 = checkpoint_tensors(p, 5)
+    path = str(tmp_path / "model.safetensors")
+    L.save_safetensors(path, tensors, bf16=bf16)
+    store = L.SafeTensorStore([path])
+    w = L.load_moe_layer(store, 5, top_k=p.top_k, device="cuda")
+    ref_w = weights_from_oracle(p).pack()
+    for T in (1, 7, 64):
+        x = bf16_t(O.make_x(62 + T, T, p.hidden))
+        y = vxmoe.moe_block(x, w)
+        ref = vxmoe.moe_block(x, ref_w)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(y.view(torch.int16).cpu().numpy(), ref.view(torch.int16).cpu().numpy())
+
+
+def test_g64_layer_is_refused(tmp_path):
+    from vxmoe import loader as L
+    p = O.make_params(seed=63, experts=8, hidden=256, inter=128, shared_inter=64, top_k=2)
+    tensors, bf16 = checkpoint_tensors(p, 0, group_override=64)
+    path = str(tmp_path / "g64.safetensors")
+    L.save_safetensors(path, tensors, bf16=bf16)
+    with pytest.raises(ValueError):
+        L.load_moe_layer(L.SafeTensorStore([path]), 0, top_k=2, device="cuda")
+
+
+@pytest.mark.parametrize("T", [1, 16, 300])
+def test_block_at_checkpoint_width(T):
+    """d=2560, I=640 (40 row tiles of the pool, 20 and 5 chunks of 128
+    inputs): decode GEMV and prefill GEMM paths against the oracle."""
+    import vxmoe
+    p = O.make_params(seed=64, experts=64, hidden=2560, inter=640, shared_inter=640, top_k=10)
+    w = weights_from_oracle(p).pack()
+    x = O.make_x(65, T, p.hidden)
+    y, inds, _ = vxmoe.moe_block(bf16_t(x), w, return_routing=True)
+    logits = np32(vxmoe.router(bf16_t(x), w).logits)
+    out = O.moe_block(x, p, logits=logits)
+    np.testing.assert_array_equal(inds.cpu().numpy(), out.router.inds)
+    assert O.normwise_error(np32(y), out.y) < 1e-2
