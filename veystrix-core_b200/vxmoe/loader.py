@@ -109,7 +109,7 @@ class SafeTensorStore:
 
     def tensor(self, name: str, device) -> torch.Tensor:
         ref = self.refs[name]
-        host = torch.from_numpy(np.ascontiguousarray(self.numpy(name)))
+        host = torch.from_numpy(np.array(self.numpy(name), copy=True))   # writable host copy
         torch_dtype = _DTYPES[ref.dtype][1]
         if ref.dtype == "BF16":
             host = host.view(torch.bfloat16)
