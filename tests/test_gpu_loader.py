@@ -33,11 +33,35 @@ def test_loaded_layer_equals_in_memory_weights(tmp_path):
         np.testing.assert_array_equal(y.view(torch.int16).cpu().numpy(), ref.view(torch.int16).cpu().numpy())
 
 
-def test_g64_layer_is_refused(tmp_path):
+def test_g64_layer_runs_within_tolerance(tmp_path):
+    """A G64 checkpoint layer (every projection in groups of 64) is expanded
+    to groups of 32 at load time: routing bit-exact against the oracle on the
+    device's logits, outputs within the block tolerance of the G64 oracle."""
+    import vxmoe
+    from vxmoe import loader as L
+    p = O.make_params(seed=63, experts=32, hidden=512, inter=256, shared_inter=128, top_k=4, group_size=64)
+    tensors, bf16 = checkpoint_tensors(p, 2)
+    path = str(tmp_path / "g64.safetensors")
+    L.save_safetensors(path, tensors, bf16=bf16)
+    store = L.SafeTensorStore([path])
+    assert L.infer_switch_quantization(store, L.layer_prefix(2) + ".switch_mlp") == (64, 4)
+    w = L.load_moe_layer(store, 2, top_k=p.top_k, device="cuda")
+    for T in (3, 200):   # decode GEMV and prefill GEMM
+        x = O.make_x(66 + T, T, p.hidden)
+        y, inds, _ = vxmoe.moe_block(bf16_t(x), w, return_routing=True)
+        logits = np32(vxmoe.router(bf16_t(x), w).logits)
+        out = O.moe_block(x, p, logits=logits)
+        np.testing.assert_array_equal(inds.cpu().numpy(), out.router.inds)
+        assert O.normwise_error(np32(y), out.y) < 1e-2
+
+
+def test_8bit_layer_is_refused(tmp_path):
     from vxmoe import loader as L
     p = O.make_params(seed=63, experts=8, hidden=256, inter=128, shared_inter=64, top_k=2)
-    tensors, bf16 = checkpoint_tensors(p, 0, group_override=64)
-    path = str(tmp_path / "g64.safetensors")
+    tensors, bf16 = checkpoint_tensors(p, 0)
+    name = L.layer_prefix(0) + ".switch_mlp.gate_proj.weight"
+    tensors[name] = np.zeros((8, 128, 256 // 4), np.uint32)   # four codes per word: 8-bit
+    path = str(tmp_path / "q8.safetensors")
     L.save_safetensors(path, tensors, bf16=bf16)
     with pytest.raises(ValueError):
         L.load_moe_layer(L.SafeTensorStore([path]), 0, top_k=2, device="cuda")

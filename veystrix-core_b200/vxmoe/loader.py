@@ -14,7 +14,8 @@ The checkpoint layout is the one the reference's Flash-Next loader reads
 The quantization of each layer is inferred from its tensor shapes, as the
 reference does per layer (``infer_switch_quantization``, loader.py:379-401),
 because converted checkpoints may mix layouts.  The kernels take 4-bit codes
-in groups of 32; other layouts are rejected with ValueError.
+in groups of 32; coarser groups (64, ...) are expanded to that form at load
+time (Q4Projection.from_group), other layouts are rejected with ValueError.
 
 The reader is a small safetensors parser (8-byte little-endian header length,
 a JSON header, then the raw tensors); tensors are memory-mapped and copied to
@@ -149,8 +150,15 @@ def moe_layers(store: SafeTensorStore) -> List[int]:
 
 
 def _proj(store: SafeTensorStore, prefix: str, device) -> "ops.Q4Projection":
-    return ops.Q4Projection(store.tensor(f"{prefix}.weight", device), store.tensor(f"{prefix}.scales", device),
-                            store.tensor(f"{prefix}.biases", device))
+    """One 4-bit projection; a coarser grouping (64, 128 ...) is expanded to
+    the kernels' groups of 32 (Q4Projection.from_group)."""
+    inputs = int(store.shape(f"{prefix}.weight")[-1]) * 8
+    groups = int(store.shape(f"{prefix}.scales")[-1])
+    if groups <= 0 or inputs % groups:
+        raise ValueError(f"{prefix}: {inputs} inputs do not split into {groups} groups")
+    return ops.Q4Projection.from_group(store.tensor(f"{prefix}.weight", device),
+                                       store.tensor(f"{prefix}.scales", device),
+                                       store.tensor(f"{prefix}.biases", device), inputs // groups)
 
 
 def load_moe_layer(store: SafeTensorStore, index: int, top_k: int, device=None,
@@ -164,9 +172,9 @@ def load_moe_layer(store: SafeTensorStore, index: int, top_k: int, device=None,
     if f"{sw}.gate_proj.weight" not in store:
         raise KeyError(f"layer {index} has no routed expert block")
     group, bits = infer_switch_quantization(store, sw)
-    if bits != 4 or group != 32:
-        raise ValueError(f"layer {index}: {bits}-bit codes in groups of {group}; the kernels take 4-bit, "
-                         "group 32")
+    if bits != 4 or group % 32:
+        raise ValueError(f"layer {index}: {bits}-bit codes in groups of {group}; the kernels take 4-bit "
+                         "codes in groups of a multiple of 32")
     shared = f"{mlp}.shared_expert.gate_proj.weight" in store
     w = ops.MoEWeights(
         _proj(store, f"{sw}.gate_proj", device), _proj(store, f"{sw}.up_proj", device),

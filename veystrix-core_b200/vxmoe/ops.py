@@ -127,6 +127,25 @@ class Q4Projection:
                     self.experts, self.out_features, self.in_features, GROUP_SIZE)
 
     @staticmethod
+    def from_group(weight: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+                   group_size: int) -> "Q4Projection":
+        """A projection quantized in groups of `group_size` (a multiple of
+        32, e.g. the G64 checkpoints of models/flashnext/metal_runtime.py:
+        950-971) in the kernels' group-32 form: every scale and bias is
+        repeated for each 32-input group it covers.  Each dequantized weight
+        scale*q + bias is unchanged; a GEMV's float sums run per 32 inputs
+        instead of per group, within the block tolerance of the G64 result."""
+        if group_size % GROUP_SIZE or group_size <= 0:
+            raise ValueError(f"group size {group_size} is not a multiple of {GROUP_SIZE}")
+        r = group_size // GROUP_SIZE
+        if r > 1:
+            scales = scales.repeat_interleave(r, dim=-1).contiguous()
+            biases = biases.repeat_interleave(r, dim=-1).contiguous()
+        p = Q4Projection(weight, scales, biases)
+        p.validate()
+        return p
+
+    @staticmethod
     def from_any(value, device=None) -> "Q4Projection":
         """Accept a Q4Projection, a (weight, scales, biases) triple or a
         mapping with those keys; numpy arrays are uploaded (bf16 values held
