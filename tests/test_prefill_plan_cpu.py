@@ -1,0 +1,56 @@
+"""Chunk plan and layer-major windows (vxmoe.prefill), the rules of
+models/flashnext/prefill.py:109-207 and layer_major.py:155-186."""
+from __future__ import annotations
+
+import pytest
+
+from vxmoe import prefill as P
+
+
+def test_grid_edges_and_short_tail_merge():
+    assert P.plan_chunks(5000, 2048) == [(0, 2048), (2048, 4096), (4096, 5000)]
+    # a 34-token tail would run decode-shaped kernels: merged into the chunk before
+    assert P.plan_chunks(4130, 2048) == [(0, 2048), (2048, 4130)]
+    # ... unless its edge is a requested boundary
+    assert P.plan_chunks(4130, 2048, boundaries=[4100]) == [(0, 2048), (2048, 4096), (4096, 4100),
+                                                            (4100, 4130)]
+    assert P.plan_chunks(0, 2048) == []
+    assert P.plan_chunks(100, 0) == [(0, 100)]
+
+
+@pytest.mark.parametrize("policy", ["grid", "balanced"])
+def test_resumed_run_continues_the_cold_plan(policy):
+    """A run restored at an edge of the cold plan (offset tokens already
+    cached) takes exactly the cold run's remaining spans."""
+    total, chunk, anchors = 9000, 2048, [700, 5100]
+    cold = P.plan_chunks(total, chunk, boundaries=anchors, policy=policy)
+    for a, _ in cold[1:]:
+        tail = P.plan_chunks(total - a, chunk, boundaries=anchors, offset=a, policy=policy)
+        assert [(s + a, e + a) for s, e in tail] == [sp for sp in cold if sp[0] >= a]
+
+
+def test_balanced_pieces():
+    assert P.plan_chunks(5000, 2048, policy="balanced") == [(0, 1667), (1667, 3334), (3334, 5000)]
+    assert P.plan_chunks(5000, 2048, boundaries=[1000], policy="balanced") == [(0, 1000), (1000, 3000),
+                                                                                (3000, 5000)]
+    spans = P.plan_chunks(10_001, 2048, policy="balanced")
+    sizes = [e - s for s, e in spans]
+    assert max(sizes) <= 2048 and max(sizes) - min(sizes) <= 1 and sum(sizes) == 10_001
+
+
+def test_windows():
+    spans = [(0, 2048), (2048, 4096), (4096, 6144), (6144, 8192), (8192, 9000)]
+    assert P.plan_windows(spans, 0, 4096) == [spans[0:2], spans[2:4], spans[4:5]]
+    # a required position ends the window where it falls
+    assert P.plan_windows(spans, 0, 8192, required=[4096]) == [spans[0:2], spans[2:5]]
+    # an anchor past the window's middle is preferred to the last edge that fits
+    assert P.plan_windows(spans, 0, 8192, anchors=[6144]) == [spans[0:3], spans[3:5]]
+    # a chunk larger than the window forms its own window
+    assert P.plan_windows([(0, 5000), (5000, 6000)], 0, 4096) == [[(0, 5000)], [(5000, 6000)]]
+
+
+def test_bad_policy_and_sizes():
+    with pytest.raises(ValueError):
+        P.plan_chunks(100, 64, policy="budgeted")
+    with pytest.raises(ValueError):
+        P.plan_chunks(-1, 64)
