@@ -197,20 +197,19 @@ __global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(const __grid_c
           const uint4 wg = lds128(wrow), w8 = lds128(wrow + 8 * 64);
           const uint32_t ag[4] = {wg.x, wg.y, wg.z, wg.w};
           const uint32_t a8[4] = {w8.x, w8.y, w8.z, w8.w};
-          // Two independent accumulator chains (even / odd MMAs) halve the
-          // dependent MMA latency per chunk.
-          float d[4] = {0.f, 0.f, 0.f, 0.f}, e2[4] = {0.f, 0.f, 0.f, 0.f};
+          // One accumulator chain over the chunk's eight MMAs (the resident
+          // warps hide its latency; a second chain cost more instructions
+          // than it saved).  The tiled kernel uses the same order.
+          float d[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
           for (int mm = 0; mm < 8; mm += 2) {
             const int wi = mm >> 1;
             mma16816(d, nib_pair128(ag[wi]), nib_pair128(a8[wi]), nib_pair128(ag[wi] >> 4),
                      nib_pair128(a8[wi] >> 4), bq[2 * mm], bq[2 * mm + 1]);
-            mma16816(e2, nib_pair128(ag[wi] >> 8), nib_pair128(a8[wi] >> 8),
+            mma16816(d, nib_pair128(ag[wi] >> 8), nib_pair128(a8[wi] >> 8),
                      nib_pair128(ag[wi] >> 12), nib_pair128(a8[wi] >> 12), bq[2 * mm + 2],
                      bq[2 * mm + 3]);
           }
-#pragma unroll
-          for (int i = 0; i < 4; ++i) d[i] += e2[i];
           float sc[2][4];   // [h] {s0, s1, b0, b1}
           if (EVEN) {
             const uint4 sb = lds128(st + S::kW + ((p * MT + m) * 32 + lane) * 16);

@@ -253,11 +253,11 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
           const uint4 wg = lds128(wrow), w8 = lds128(wrow + 512);
           const uint32_t ag[4] = {wg.x, wg.y, wg.z, wg.w};
           const uint32_t a8[4] = {w8.x, w8.y, w8.z, w8.w};
-          float d[NQ][4], e2[NQ][4];
+          float d[NQ][4];
 #pragma unroll
           for (int q = 0; q < NQ; ++q)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) d[q][i] = e2[q][i] = 0.f;
+            for (int i = 0; i < 4; ++i) d[q][i] = 0.f;
 #pragma unroll
           for (int mm = 0; mm < 8; mm += 2) {
             const int wi = mm >> 1;
@@ -267,9 +267,9 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
             const uint32_t h2 = nib_pair128(ag[wi] >> 12), h3 = nib_pair128(a8[wi] >> 12);
 #pragma unroll
             for (int q = 0; q < NQ; ++q) {
-              // two independent accumulator chains (even / odd MMAs)
+              // one accumulator chain per B operand, in the MLX-layout kernel's order
               mma16816(d[q], f0, f1, f2, f3, bq[q][2 * mm], bq[q][2 * mm + 1]);
-              mma16816(e2[q], h0, h1, h2, h3, bq[q][2 * mm + 2], bq[q][2 * mm + 3]);
+              mma16816(d[q], h0, h1, h2, h3, bq[q][2 * mm + 2], bq[q][2 * mm + 3]);
             }
           }
           const uint4 sb = lds128(st + kWBytes + (p * MT + m) * 256 + (g * 2 + (c & 1)) * 16);
@@ -286,9 +286,9 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
 #pragma unroll
             for (int q = 0; q < NQ; ++q) {
               float v = acc[p][m][q][h];
-              v = fmaf(s0, d[q][2 * h] + e2[q][2 * h], v);
+              v = fmaf(s0, d[q][2 * h], v);
               v = fmaf(c0, xs[q][0], v);
-              v = fmaf(s1, d[q][2 * h + 1] + e2[q][2 * h + 1], v);
+              v = fmaf(s1, d[q][2 * h + 1], v);
               v = fmaf(c1, xs[q][1], v);
               acc[p][m][q][h] = v;
             }
