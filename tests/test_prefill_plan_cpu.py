@@ -54,3 +54,38 @@ def test_bad_policy_and_sizes():
         P.plan_chunks(100, 64, policy="budgeted")
     with pytest.raises(ValueError):
         P.plan_chunks(-1, 64)
+
+
+# Budgeted policy (prefill.py:109-140): a model whose attention term grows with
+# the position, so the chunks shrink along the prompt.
+_MODEL = P.ChunkMemoryModel(per_token=100_000, pair_bytes=48, query_cap=2048)
+
+
+def test_budgeted_chunks_shrink_with_position():
+    # 2048 fits while 2048*1e5 + 2048*(p+2048)*48 <= 1e9, i.e. p <= 6041;
+    # 1024 while p <= 17237; then 512.
+    spans = P.plan_chunks(20_000, 0, policy="budgeted", budget=10**9, model=_MODEL)
+    sizes = [e - s for s, e in spans]
+    assert sizes == [2048] * 3 + [1024] * 11 + [512] * 4 + [544]   # 32-token tail merged
+    for s, e in spans[:-1]:
+        assert _MODEL.increment(e - s, s) <= 10**9
+    # a cap below the largest candidate
+    assert {e - s for s, e in P.plan_chunks(3000, 1024, policy="budgeted", budget=10**9,
+                                              model=_MODEL)[:-1]} == {1024}
+
+
+def test_budgeted_anchors_tiny_budget_and_resume():
+    anchors = [700, 5100]
+    cold = P.plan_chunks(9000, 0, boundaries=anchors, policy="budgeted", budget=10**9, model=_MODEL)
+    assert (0, 700) in cold and any(e == 5100 for _, e in cold)
+    for a, _ in cold[1:]:
+        tail = P.plan_chunks(9000 - a, 0, boundaries=anchors, offset=a, policy="budgeted",
+                             budget=10**9, model=_MODEL)
+        assert [(s + a, e + a) for s, e in tail] == [sp for sp in cold if sp[0] >= a]
+    # nothing fits: the smallest candidate everywhere
+    huge = P.ChunkMemoryModel(per_token=10**7)
+    spans = P.plan_chunks(1000, 0, policy="budgeted", budget=10**8, model=huge)
+    assert [e - s for s, e in spans] == [256, 256, 256, 232]
+    with pytest.raises(ValueError):
+        P.plan_chunks(1000, 0, policy="budgeted", budget=10**6, model=huge)
+

@@ -17,6 +17,11 @@ continues with exactly the cold run's remaining spans):
   one before it unless that edge is a requested boundary.
 * ``balanced``: between consecutive anchors, the fewest equal pieces of at
   most the chunk size, the first ``length % pieces`` pieces one token longer.
+* ``budgeted``: greedy from position 0, each chunk the largest of
+  CANDIDATE_CHUNKS (up to the cap) whose estimated device-memory increment at
+  its start position fits the budget (the smallest when none fits), cut at
+  anchors, with the grid rule's short-tail merge.  Each chunk depends only on
+  its start position, so the plan is prefix-stable like the other two.
 
 Windows group whole chunks up to a token budget, ending at a required
 position inside them, else at the last anchor past the window's middle, else
@@ -24,12 +29,84 @@ at the last chunk edge that fits.
 """
 from __future__ import annotations
 
+from dataclasses import dataclass
 from typing import Callable, List, Optional, Sequence, Tuple
 
 import torch
 
 MIN_CHUNK_TOKENS = 64          # a shorter tail would run the decode-shaped kernels
+CANDIDATE_CHUNKS = (2048, 1024, 512, 256)   # largest first (prefill.py:45)
+MIN_BUDGET_BYTES = 100_000_000               # prefill.py:104-105
 Span = Tuple[int, int]
+
+
+@dataclass(frozen=True)
+class ChunkMemoryModel:
+    """Device bytes a chunk of `chunk` tokens adds while it runs with
+    `position` tokens already cached - the terms of the reference's estimate
+    (prefill_budget.py:115-135): a transient per live token, attention scores
+    for min(chunk, query_cap) queries against every key up to the chunk's end
+    at `pair_bytes` per (query, key) pair, and the cache the chunk appends.
+    `layer_bytes(chunk)` adds what one MoE-block call over the chunk takes
+    (`block_memory_model`); the attention and cache terms belong to the model
+    around the block and are the caller's to supply."""
+    per_token: float = 0.0
+    pair_bytes: float = 0.0
+    query_cap: int = 2048
+    kv_per_token: float = 0.0
+    layer_bytes: Optional[Callable[[int], int]] = None
+
+    def increment(self, chunk: int, position: int) -> int:
+        chunk, position = int(chunk), int(position)
+        scores = min(chunk, self.query_cap) * (position + chunk) * self.pair_bytes
+        extra = self.layer_bytes(chunk) if self.layer_bytes is not None else 0
+        return int(chunk * (self.per_token + self.kv_per_token) + scores + extra)
+
+
+def block_memory_model(weights, **model) -> ChunkMemoryModel:
+    """A ChunkMemoryModel whose layer term is this block's own device memory
+    for a chunk: the library's scratch for one call (vx_moe_block_workspace)
+    plus the output rows and the routes (ids int32, weights bf16)."""
+    import ctypes
+
+    from ._lib import load
+    lib = load()
+    st = weights.vx()
+    row = weights.hidden * 2 + weights.top_k * (4 + 2)
+
+    def layer_bytes(chunk: int) -> int:
+        return int(lib.vx_moe_block_workspace(int(chunk), ctypes.byref(st))) + int(chunk) * row
+
+    return ChunkMemoryModel(layer_bytes=layer_bytes, **model)
+
+
+def budgeted_chunk(position: int, cap: int, budget: int, model: ChunkMemoryModel) -> int:
+    """Largest candidate chunk <= cap whose increment at `position` fits the
+    budget; the smallest candidate when none fits (prefill.py:109-117)."""
+    cands = [c for c in CANDIDATE_CHUNKS if c <= cap] or [min(CANDIDATE_CHUNKS)]
+    for c in cands:
+        if model.increment(c, position) <= budget:
+            return c
+    return cands[-1]
+
+
+def budgeted_edges(end: int, cap: int, budget: int, model: ChunkMemoryModel,
+                   anchors: Sequence[int] = (), start: int = 0) -> List[int]:
+    """Internal edges of the budgeted plan over [start, end] (prefill.py:120-140)."""
+    wanted = sorted({int(a) for a in anchors if start < int(a) < end})
+    edges: List[int] = []
+    pos = int(start)
+    while pos < end:
+        stop = min(pos + budgeted_chunk(pos, cap, budget, model), end)
+        cut = next((a for a in wanted if pos < a < stop), None)
+        if cut is not None:
+            stop = cut
+        if stop < end:
+            edges.append(stop)
+        pos = stop
+    if edges and end - edges[-1] < MIN_CHUNK_TOKENS and edges[-1] not in wanted:
+        edges.pop()
+    return edges
 
 
 def balanced_edges(end: int, chunk: int, anchors: Sequence[int] = ()) -> List[int]:
@@ -48,14 +125,25 @@ def balanced_edges(end: int, chunk: int, anchors: Sequence[int] = ()) -> List[in
 
 
 def plan_chunks(total: int, chunk: int, boundaries: Sequence[int] = (), offset: int = 0,
-                policy: str = "grid", anchors: Optional[Sequence[int]] = None) -> List[Span]:
+                policy: str = "grid", anchors: Optional[Sequence[int]] = None,
+                budget: Optional[int] = None, model: Optional[ChunkMemoryModel] = None) -> List[Span]:
     """Spans [(start, end), ...] covering range(total) of a prompt whose first
-    token sits at absolute position `offset` (tokens already in the cache)."""
+    token sits at absolute position `offset` (tokens already in the cache).
+    The budgeted policy takes `budget` (bytes, at least MIN_BUDGET_BYTES) and
+    the memory `model`; its cap is `chunk`, or the largest candidate when 0."""
     total, chunk, offset = int(total), int(chunk), int(offset)
     if total < 0 or chunk < 0 or offset < 0:
         raise ValueError("negative prompt length, chunk size or offset")
     end = offset + total
-    if policy == "balanced":
+    if policy == "budgeted":
+        if budget is None or model is None:
+            raise ValueError("the budgeted policy needs a budget and a memory model")
+        if budget < MIN_BUDGET_BYTES:
+            raise ValueError(f"chunk budget must be at least {MIN_BUDGET_BYTES} bytes")
+        cold = budgeted_edges(end, chunk or max(CANDIDATE_CHUNKS), int(budget), model,
+                              boundaries if anchors is None else anchors)
+        points = [0] + [e - offset for e in cold if offset < e < end] + [total]
+    elif policy == "balanced":
         cold = balanced_edges(end, chunk, boundaries if anchors is None else anchors)
         points = [0] + [e - offset for e in cold if offset < e < end] + [total]
     elif policy == "grid":
@@ -67,7 +155,7 @@ def plan_chunks(total: int, chunk: int, boundaries: Sequence[int] = (), offset: 
             ordered.pop()
         points = [0] + [e - offset for e in ordered] + [total]
     else:
-        raise ValueError(f"unknown chunk policy {policy!r} (grid or balanced)")
+        raise ValueError(f"unknown chunk policy {policy!r} (grid, balanced or budgeted)")
     return [(a, b) for a, b in zip(points, points[1:]) if b > a]
 
 
