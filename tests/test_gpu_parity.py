@@ -247,7 +247,9 @@ def test_router_full_production(prod_params):
 @pytest.mark.parametrize("P,E,skew", [(0, 8, False), (1, 8, False), (10, 512, False),
                                       (200, 512, False), (256, 1024, False), (256, 8, True),
                                       (257, 512, True), (80, 3, False),
-                                      (640, 512, False), (4096, 64, True), (65536, 512, True),
+                                      (640, 512, False), (1024, 1024, True), (1024, 8, False),
+                                      (513, 1, False), (1025, 512, True),
+                                      (4096, 64, True), (65536, 512, True),
                                       (20480, 512, False), (100003, 64, False)])
 def test_permute_bit_exact(P, E, skew):
     import vxmoe
@@ -265,13 +267,15 @@ def test_permute_bit_exact(P, E, skew):
     assert int(perm.errors.item()) == 0
 
 
-def test_permute_large_drops_out_of_range_ids():
-    """Prefill-sized input (the multi-CTA permutation): invalid ids are
-    counted, get inverse -1 and leave the order of the others stable."""
+@pytest.mark.parametrize("P", [40000, 900])
+def test_permute_large_drops_out_of_range_ids(P):
+    """Prefill-sized input (the multi-CTA permutation) and a decode-sized one
+    (the one-CTA permutation, four ids a thread): invalid ids are counted,
+    get inverse -1 and leave the order of the others stable."""
     import vxmoe
     rng = np.random.default_rng(77)
-    ids = rng.integers(0, 256, 40000).astype(np.int32)
-    bad = rng.random(40000) < 0.01
+    ids = rng.integers(0, 256, P).astype(np.int32)
+    bad = rng.random(P) < 0.01
     ids[bad] = np.where(rng.random(int(bad.sum())) < 0.5, -1, 256)
     perm = vxmoe.permute(torch.from_numpy(ids).to(DEV), 256)
     good = np.nonzero(~bad)[0]
@@ -394,6 +398,12 @@ def test_block_production_decode(prod_params):
 @pytest.mark.slow
 def test_block_production_batched_decode(prod_params):
     _block_check(prod_params, O.make_x(1, 64, 2048), "production T=64")
+
+
+def test_block_production_fused_permutation_many_token_blocks(prod_params):
+    """T*k = 1000 routes: the last of 13 token blocks of the fused router
+    sorts them (second arrival), four ids a thread."""
+    _block_check(prod_params, O.make_x(5, 100, 2048), "production T=100")
 
 
 def test_block_empty_batch(small_params):

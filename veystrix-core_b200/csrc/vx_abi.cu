@@ -547,7 +547,7 @@ size_t vx_router_workspace(int32_t T, const vx_moe_weights* W) {
   if (!W || T < 0) return 0;
   Carver c(nullptr);
   c.take<uint16_t>(int64_t(T) * W->num_experts);   // logits (when the caller passes none)
-  c.take<int32_t>((int64_t(T) + 7) / 8);           // arrival counters of the fused router
+  c.take<int32_t>(router_counters(T));             // arrival counters of the fused router
   return c.size();
 }
 
@@ -586,7 +586,7 @@ int vx_router(const uint16_t* x, int32_t T, const vx_moe_weights* W, uint16_t* l
   if (!workspace || workspace_bytes < vx_router_workspace(T, W)) return VX_EWORKSPACE;
   Carver c(workspace);
   uint16_t* lg = c.take<uint16_t>(int64_t(T) * dm.E);
-  int32_t* counters = c.take<int32_t>((int64_t(T) + 7) / 8);
+  int32_t* counters = c.take<int32_t>(router_counters(T));
   if (!logits) logits = lg;
   return router_impl(x, T, W, dm, logits, inds, weights, sg, counters, static_cast<cudaStream_t>(stream));
 }
@@ -693,7 +693,7 @@ size_t vx_moe_block_workspace(int32_t T, const vx_moe_weights* W) {
   c.take<int32_t>(int64_t(T) * dm.k);    // inds
   c.take<uint16_t>(int64_t(T) * dm.k);   // weights
   c.take<uint16_t>(T);                   // sg
-  c.take<int32_t>((int64_t(T) + 7) / 8);  // router arrival counters
+  c.take<int32_t>(router_counters(T));    // router arrival counters
   carve_experts(c, T, dm);
   return c.size();
 }
@@ -713,15 +713,15 @@ int vx_moe_block(const uint16_t* x, int32_t T, const vx_moe_weights* W, uint16_t
   int32_t* inds_ws = c.take<int32_t>(int64_t(T) * dm.k);
   uint16_t* w_ws = c.take<uint16_t>(int64_t(T) * dm.k);
   uint16_t* sg = c.take<uint16_t>(T);
-  int32_t* counters = c.take<int32_t>((int64_t(T) + 7) / 8);
+  int32_t* counters = c.take<int32_t>(router_counters(T));
   ExpertScratch es = carve_experts(c, T, dm);
   if (!inds) inds = inds_ws;
   if (!weights) weights = w_ws;
   cudaError_t e = cudaMemsetAsync(es.err, 0, 2 * sizeof(int32_t), st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
-  // A decode-sized batch (one token block of the router) is sorted by expert
-  // in the router's last CTA.
-  const bool fuse_perm = T <= 8 && int64_t(T) * dm.k <= kPermSmall && dm.E <= kPermSmallMaxE;
+  // A decode-sized batch (at most kPermSmall routes) is sorted by expert in
+  // the router's last CTA.
+  const bool fuse_perm = int64_t(T) * dm.k <= kPermSmall && dm.E <= kPermSmallMaxE;
   PermSmallArgs pa{dm.E, dm.shared ? T : 0, dm.k, item_chunk(expert_path(T, dm), dm), nullptr,
                    es.order, es.inverse, es.offsets, es.active, es.n_active, es.src_rows, es.err,
                    es.items, es.n_items};

@@ -8,6 +8,12 @@
 
 #define VX_DEVICE __device__ __forceinline__
 
+// Trace points (a CTA's thread 0 records a timestamp for a numbered phase):
+// empty unless a timing build defines VX_STAMP before including the sources.
+#ifndef VX_STAMP
+#define VX_STAMP(slot) ((void)0)
+#endif
+
 namespace vx {
 
 constexpr int kWarp = 32;

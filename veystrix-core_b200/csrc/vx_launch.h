@@ -203,7 +203,7 @@ int64_t permute_scratch_ints(int64_t P, int E);
 // Decode-sized permutations (at most kPermSmall ids, E <= kPermSmallMaxE) run
 // in one 256-thread CTA: the one-CTA permute kernel, or the fused router's
 // last CTA when it is handed these outputs (PermSmallArgs::order non-null).
-constexpr int kPermSmall = 256;
+constexpr int kPermSmall = 1024;
 constexpr int kPermSmallMaxE = 1024;
 
 struct PermSmallArgs {
@@ -220,9 +220,10 @@ cudaError_t launch_softmax_topk(const uint16_t* logits, int T, int E, int k, int
                                 uint16_t* scores, uint16_t* weights, uint16_t* mass,
                                 cudaStream_t st);
 // Logits, top-k/renorm, (seg != null) the shared-expert gate and (perm !=
-// null; T <= 8, T*k <= kPermSmall) the expert sort of the routes in one
-// launch; bias (bf16 [E] or null) is added to the bf16 logits; counters:
-// (T+7)/8 ints of scratch (zeroed by the launcher).
+// null; T*k <= kPermSmall) the expert sort of the routes in one launch;
+// bias (bf16 [E] or null) is added to the bf16 logits; counters:
+// router_counters(T) ints of scratch (zeroed by the launcher).
+inline int64_t router_counters(int64_t T) { return (T + 7) / 8 + 1; }
 struct PermSmallArgs;
 cudaError_t launch_router_fused(const uint16_t* x, int T, const uint16_t* wg, int E, int K, int k,
                                 const vx_q4* seg, uint16_t* logits, int32_t* inds, uint16_t* weights,

@@ -9,11 +9,31 @@
 namespace vx {
 
 // ---- decode-sized inputs: at most kPermSmall ids ---------------------------
-// The same outputs as permute_kernel from one 256-thread CTA with no
-// per-expert histogram: an id's position is the number of valid ids below it
-// plus the equal ids before it (a stable counting rank over at most 256
-// ids), the run offsets come from per-expert counts and one block scan, and
-// the active list and work items from run starts found in sorted order.
+// The same outputs as permute_kernel from one 256-thread CTA.  Ids are taken
+// in rounds of 256 in index order (thread t holds id 256r + t of round r);
+// an id's sorted position is its expert's run start, plus the equal ids of
+// earlier rounds (a running count per expert), plus the equal ids of lower
+// warps in the round (per-warp 16-bit counts tagged with the round, so a
+// stale count of an earlier round reads as zero), plus its rank among equal
+// lanes of its warp (peer_mask: one ballot per key bit).  The run offsets come from per-expert
+// counts and one block scan, the active list and the work items from run
+// starts found in sorted order (four consecutive sorted positions a thread).
+constexpr int kPermSmallRounds = kPermSmall / 256;
+
+// Lanes of the warp holding the same key as this lane, for keys in
+// [-1, 1024): one ballot per bit (11 bits; -1 differs from every valid key in
+// bit 10).  The same set as __match_any_sync, without its per-distinct-value
+// cost when all 32 keys differ.
+VX_DEVICE unsigned peer_mask(int key) {
+  unsigned peers = 0xFFFFFFFFu;
+#pragma unroll
+  for (int b = 0; b < 11; ++b) {
+    const bool bit = (key >> b) & 1;
+    const unsigned v = __ballot_sync(0xFFFFFFFFu, bit);
+    peers &= bit ? v : ~v;
+  }
+  return peers;
+}
 
 // Exclusive scan of one int per thread over a 256-thread CTA; *total gets
 // the sum (valid on every thread after the call).
@@ -47,25 +67,44 @@ VX_DEVICE void perm_small(const PermSmallArgs& a, const int32_t* ids, int P) {
   int32_t *order = a.order, *inverse = a.inverse, *offsets = a.offsets, *active = a.active;
   int32_t *n_active = a.n_active, *src_rows = a.src_rows, *err = a.err, *items = a.items;
   int32_t* n_items = a.n_items;
-  __shared__ int s_key[kPermSmall];
-  __shared__ int s_cnt[kPermSmallMaxE];
-  __shared__ int s_off[kPermSmallMaxE];
-  __shared__ int s_sorted[kPermSmall];   // expert of each sorted position
+  __shared__ int s_cnt[kPermSmallMaxE];                    // ids per expert
+  __shared__ int s_off[kPermSmallMaxE];                    // run starts
+  __shared__ int s_run[kPermSmallMaxE];                    // next position of each run
+  __shared__ __align__(16) uint16_t s_hist[8][kPermSmallMaxE];   // (round + 1) << 8 | count
+  __shared__ uint16_t s_sorted[kPermSmall];                // expert of each sorted position
   __shared__ int warp_tot[8];
-  const int tid = threadIdx.x;
+  __shared__ int s_bad;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int e = tid; e < E; e += 256) s_cnt[e] = 0;
-  int key = 0x7FFFFFFF;
-  bool valid = false;
-  if (tid < P) {
-    const int id = __ldcg(ids + tid);   // may have been written earlier in the same kernel
-    valid = id >= 0 && id < E;
-    if (valid) key = id;
-    else inverse[tid] = -1;
-  }
-  s_key[tid] = key;
-  const int bad = __syncthreads_count(tid < P && !valid);
-  if (valid) atomicAdd(&s_cnt[key], 1);
+  // only rows of warps below the last warp holding ids are ever read
+  const int hist_rows = min(7, (min(P, 256) + 31) / 32 - 1);
+  for (int w = 0; w < hist_rows; ++w)
+    for (int e = tid; e < E; e += 256) s_hist[w][e] = 0;
+  if (tid == 0) s_bad = 0;
   __syncthreads();
+  int key[kPermSmallRounds];
+  int nbad = 0;
+  // all loads first (one memory round trip), then the counts
+#pragma unroll
+  for (int r = 0; r < kPermSmallRounds; ++r) {
+    const int i = 256 * r + tid;
+    key[r] = i < P ? __ldcg(ids + i) : -1;   // may have been written earlier in the same kernel
+  }
+#pragma unroll
+  for (int r = 0; r < kPermSmallRounds; ++r) {
+    const int i = 256 * r + tid;
+    if (i >= P) continue;
+    if (key[r] >= 0 && key[r] < E) {
+      atomicAdd(&s_cnt[key[r]], 1);
+    } else {
+      key[r] = -1;
+      inverse[i] = -1;
+      ++nbad;
+    }
+  }
+  if (nbad) atomicAdd(&s_bad, nbad);
+  __syncthreads();
+  VX_STAMP(5);
 
   // run offsets: each thread scans a contiguous block of E/256 experts
   const int per = (E + 255) / 256, e0 = tid * per;
@@ -77,41 +116,80 @@ VX_DEVICE void perm_small(const PermSmallArgs& a, const int32_t* ids, int P) {
   for (int j = 0; j < per; ++j)
     if (e0 + j < E) {
       s_off[e0 + j] = run;
+      s_run[e0 + j] = run;
       offsets[e0 + j] = run;
       run += s_cnt[e0 + j];
     }
   if (tid == 0) {
     offsets[E] = routed;
     if (shared_items >= 0) offsets[E + 1] = routed + shared_items;
-    if (err && bad) atomicAdd(err, bad);
+    if (err && s_bad) atomicAdd(err, s_bad);
+  }
+  __syncthreads();
+  VX_STAMP(6);
+
+  // stable position of each valid id, one round of 256 ids at a time
+  static_assert(kPermSmallMaxE <= 1024, "peer_mask covers 10-bit keys");
+#pragma unroll 1
+  for (int r = 0; r < kPermSmallRounds && 256 * r < P; ++r) {
+    const int i = 256 * r + tid;
+    int kr = key[0];
+    if (r == 1) kr = key[1];
+    if (r == 2) kr = key[2];
+    if (r == 3) kr = key[3];
+    const unsigned tag = unsigned(r + 1) << 8;
+    const unsigned peers = peer_mask(kr);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    const bool leader = (__ffs(peers) - 1) == lane;
+    if (kr >= 0 && leader) s_hist[warp][kr] = uint16_t(tag | __popc(peers));
+    __syncthreads();   // this round's counts are in; the previous round's runs advanced
+    if (kr >= 0) {
+      int pos = s_run[kr] + rank;
+      for (int w = 0; w < warp; ++w) {
+        const unsigned h = s_hist[w][kr];
+        pos += (h & 0xFF00u) == tag ? int(h & 0xFFu) : 0;
+      }
+      order[pos] = i;
+      inverse[i] = pos;
+      s_sorted[pos] = uint16_t(kr);
+      if (src_rows) src_rows[pos] = src_map ? src_map[i] : i / k_div;
+    }
+    __syncthreads();   // s_run and s_hist read before they change
+    if (kr >= 0 && leader) atomicAdd(&s_run[kr], __popc(peers));
   }
   __syncthreads();
 
-  // stable position of each valid id
-  if (valid) {
-    int r = s_off[key];
-    for (int j = 0; j < tid; ++j) r += s_key[j] == key;
-    order[r] = tid;
-    inverse[tid] = r;
-    s_sorted[r] = key;
-    if (src_rows) src_rows[r] = src_map ? src_map[tid] : tid / k_div;
+  VX_STAMP(7);
+  // active experts and items, from the runs in sorted order: thread t looks
+  // at sorted positions 4t..4t+3, so thread order is position order
+  int ek[kPermSmallRounds];
+  bool starts[kPermSmallRounds], istart[kPermSmallRounds];
+  int na = 0, ni = 0;
+#pragma unroll
+  for (int j = 0; j < kPermSmallRounds; ++j) {
+    const int pidx = kPermSmallRounds * tid + j;
+    const bool in = pidx < routed;
+    ek[j] = in ? int(s_sorted[pidx]) : 0;
+    starts[j] = in && (pidx == 0 || int(s_sorted[pidx - 1]) != ek[j]);
+    istart[j] = in && ((pidx - s_off[ek[j]]) % item_chunk == 0);
+    na += starts[j] ? 1 : 0;
+    ni += istart[j] ? 1 : 0;
   }
-  __syncthreads();
-
-  // active experts and items, from the runs in sorted order
-  const bool in = tid < routed;
-  const int ek = in ? s_sorted[tid] : 0;
-  const bool starts = in && (tid == 0 || s_sorted[tid - 1] != ek);
-  const bool istart = in && ((tid - s_off[ek]) % item_chunk == 0);
-  int n_act, n_it;
-  const int ai = scan256(starts ? 1 : 0, warp_tot, &n_act);
-  const int ii = scan256(istart ? 1 : 0, warp_tot, &n_it);
-  if (starts) active[ai] = ek;
-  if (items && istart) {
-    int32_t* it = items + 3 * ii;
-    it[0] = ek;
-    it[1] = tid;
-    it[2] = min(item_chunk, s_off[ek] + s_cnt[ek] - tid);
+  // one scan for both counts (each at most kPermSmall: 16 bits apiece)
+  int both;
+  const int ex = scan256((na << 16) | ni, warp_tot, &both);
+  const int n_act = both >> 16, n_it = both & 0xFFFF;
+  int ai = ex >> 16, ii = ex & 0xFFFF;
+#pragma unroll
+  for (int j = 0; j < kPermSmallRounds; ++j) {
+    const int pidx = kPermSmallRounds * tid + j;
+    if (starts[j]) active[ai++] = ek[j];
+    if (items && istart[j]) {
+      int32_t* it = items + 3 * ii++;
+      it[0] = ek[j];
+      it[1] = pidx;
+      it[2] = min(item_chunk, s_off[ek[j]] + s_cnt[ek[j]] - pidx);
+    }
   }
   const int sh_items = shared_items > 0 ? (shared_items + item_chunk - 1) / item_chunk : 0;
   if (tid == 0) {
@@ -128,7 +206,7 @@ VX_DEVICE void perm_small(const PermSmallArgs& a, const int32_t* ids, int P) {
     }
   if (src_rows)
     for (int t = tid; t < shared_items; t += 256) src_rows[routed + t] = t;
+  VX_STAMP(8);
 }
-
 
 }  // namespace vx
