@@ -160,7 +160,9 @@ static ExpertPath expert_path(int T, const BlockDims& dm) {
   return dm.pool ? kPathGemvTiled : kPathGemvMlx;
 }
 
-static ExpertScratch carve_experts(Carver& c, int T, const BlockDims& dm) {
+// extra_zeroed: ints placed right after s.err, so that one memset clears
+// both (the block call keeps the router's arrival counters there).
+static ExpertScratch carve_experts(Carver& c, int T, const BlockDims& dm, int extra_zeroed = 0) {
   const int64_t P = int64_t(T) * dm.k, Ts = dm.shared ? T : 0;
   const ExpertPath path = expert_path(T, dm);
   ExpertScratch s;
@@ -170,7 +172,7 @@ static ExpertScratch carve_experts(Carver& c, int T, const BlockDims& dm) {
   s.active = c.take<int32_t>(dm.E + 1);
   s.n_active = c.take<int32_t>(1);
   s.src_rows = c.take<int32_t>(P + Ts);
-  s.err = c.take<int32_t>(2);      // [0] dropped ids, [1] pipeline timeouts
+  s.err = c.take<int32_t>(2 + extra_zeroed);   // [0] dropped ids, [1] pipeline timeouts
   s.max_items = max_items_bound(P, dm.E, int(Ts));
   s.items = c.take<int32_t>(3 * int64_t(s.max_items));
   s.n_items = c.take<int32_t>(1);
@@ -555,12 +557,14 @@ size_t vx_router_workspace(int32_t T, const vx_moe_weights* W) {
 // and the shared-expert gate (vx_router.cu router_fused_kernel).
 static int router_impl(const uint16_t* x, int T, const vx_moe_weights* W, const BlockDims& dm,
                        uint16_t* logits, int32_t* inds, uint16_t* weights, uint16_t* sg,
-                       int32_t* counters, cudaStream_t st, const PermSmallArgs* perm = nullptr) {
+                       int32_t* counters, cudaStream_t st, const PermSmallArgs* perm = nullptr,
+                       bool counters_zeroed = false) {
   profile_mark(st, "");
   const bool gate = sg && W->shared_expert_gate.w;
   cudaError_t e = launch_router_fused(x, T, W->router_w, dm.E, dm.d, dm.k,
                                       gate ? &W->shared_expert_gate : nullptr, logits, inds, weights,
-                                      gate ? sg : nullptr, counters, perm, W->router_bias, st);
+                                      gate ? sg : nullptr, counters, perm, W->router_bias, st,
+                                      counters_zeroed);
   if (e != cudaSuccess) return vx_cuda_fail(e);
   profile_mark(st, "router");
   return VX_OK;
@@ -693,8 +697,7 @@ size_t vx_moe_block_workspace(int32_t T, const vx_moe_weights* W) {
   c.take<int32_t>(int64_t(T) * dm.k);    // inds
   c.take<uint16_t>(int64_t(T) * dm.k);   // weights
   c.take<uint16_t>(T);                   // sg
-  c.take<int32_t>(router_counters(T));    // router arrival counters
-  carve_experts(c, T, dm);
+  carve_experts(c, T, dm, int(router_counters(T)));   // err + router arrival counters
   return c.size();
 }
 
@@ -713,11 +716,13 @@ int vx_moe_block(const uint16_t* x, int32_t T, const vx_moe_weights* W, uint16_t
   int32_t* inds_ws = c.take<int32_t>(int64_t(T) * dm.k);
   uint16_t* w_ws = c.take<uint16_t>(int64_t(T) * dm.k);
   uint16_t* sg = c.take<uint16_t>(T);
-  int32_t* counters = c.take<int32_t>(router_counters(T));
-  ExpertScratch es = carve_experts(c, T, dm);
+  const int n_counters = int(router_counters(T));
+  ExpertScratch es = carve_experts(c, T, dm, n_counters);
+  int32_t* counters = es.err + 2;
   if (!inds) inds = inds_ws;
   if (!weights) weights = w_ws;
-  cudaError_t e = cudaMemsetAsync(es.err, 0, 2 * sizeof(int32_t), st);
+  // one memset clears the error words and the router's arrival counters
+  cudaError_t e = cudaMemsetAsync(es.err, 0, size_t(2 + n_counters) * sizeof(int32_t), st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
   // A decode-sized batch (at most kPermSmall routes) is sorted by expert in
   // the router's last CTA.
@@ -726,7 +731,7 @@ int vx_moe_block(const uint16_t* x, int32_t T, const vx_moe_weights* W, uint16_t
                    es.order, es.inverse, es.offsets, es.active, es.n_active, es.src_rows, es.err,
                    es.items, es.n_items};
   s = router_impl(x, T, W, dm, logits, inds, weights, dm.shared ? sg : nullptr, counters, st,
-                  fuse_perm ? &pa : nullptr);
+                  fuse_perm ? &pa : nullptr, true);
   if (s) return s;
   s = run_experts(x, T, inds, W, dm, es, st, true, fuse_perm);
   if (s) return s;

@@ -222,13 +222,14 @@ cudaError_t launch_softmax_topk(const uint16_t* logits, int T, int E, int k, int
 // Logits, top-k/renorm, (seg != null) the shared-expert gate and (perm !=
 // null; T*k <= kPermSmall) the expert sort of the routes in one launch;
 // bias (bf16 [E] or null) is added to the bf16 logits; counters:
-// router_counters(T) ints of scratch (zeroed by the launcher).
+// router_counters(T) ints of scratch, zeroed by the launcher unless the
+// caller cleared them earlier on the stream (counters_zeroed).
 inline int64_t router_counters(int64_t T) { return (T + 7) / 8 + 1; }
 struct PermSmallArgs;
 cudaError_t launch_router_fused(const uint16_t* x, int T, const uint16_t* wg, int E, int K, int k,
                                 const vx_q4* seg, uint16_t* logits, int32_t* inds, uint16_t* weights,
                                 uint16_t* sg, int32_t* counters, const PermSmallArgs* perm,
-                                const uint16_t* bias, cudaStream_t st);
+                                const uint16_t* bias, cudaStream_t st, bool counters_zeroed = false);
 
 // Expert-parallel exchange buffer of one rank (vx_ep.cu): a 256-byte header
 // (u32 flag_dispatch[8], flag_combine[8], epoch, tickets[3]), then, for a step

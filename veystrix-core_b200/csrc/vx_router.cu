@@ -415,7 +415,7 @@ __global__ void __launch_bounds__(32 * kRouterSlices) router_fused_kernel(
 cudaError_t launch_router_fused(const uint16_t* x, int T, const uint16_t* wg, int E, int K, int k,
                                 const vx_q4* seg, uint16_t* logits, int32_t* inds, uint16_t* weights,
                                 uint16_t* sg, int32_t* counters, const PermSmallArgs* perm,
-                                const uint16_t* bias, cudaStream_t st) {
+                                const uint16_t* bias, cudaStream_t st, bool counters_zeroed) {
   if (T == 0) return cudaSuccess;
   if (k > kMaxK) return cudaErrorInvalidValue;
   const int nTB = (T + 7) / 8, nEB = (E + 15) / 16;
@@ -424,8 +424,11 @@ cudaError_t launch_router_fused(const uint16_t* x, int T, const uint16_t* wg, in
     if (int64_t(T) * k > kPermSmall || E > kPermSmallMaxE) return cudaErrorInvalidValue;
     pa = *perm;
   }
-  cudaError_t e = cudaMemsetAsync(counters, 0, size_t(router_counters(T)) * sizeof(int32_t), st);
-  if (e != cudaSuccess) return e;
+  cudaError_t e = cudaSuccess;
+  if (!counters_zeroed) {
+    e = cudaMemsetAsync(counters, 0, size_t(router_counters(T)) * sizeof(int32_t), st);
+    if (e != cudaSuccess) return e;
+  }
   vx_q4 q{};
   if (seg) q = *seg;
   dim3 grid(nEB + 1, nTB);
