@@ -15,9 +15,10 @@ namespace vx {
 // earlier rounds (a running count per expert), plus the equal ids of lower
 // warps in the round (per-warp 16-bit counts tagged with the round, so a
 // stale count of an earlier round reads as zero), plus its rank among equal
-// lanes of its warp (peer_mask: one ballot per key bit).  The run offsets come from per-expert
-// counts and one block scan, the active list and the work items from run
-// starts found in sorted order (four consecutive sorted positions a thread).
+// lanes of its warp (peer_mask: one ballot per key bit).  The run offsets,
+// the active list and the work items (each run cut into pieces of at most
+// item_chunk positions, in expert order) come from the per-expert counts and
+// one block scan of the three running totals.
 constexpr int kPermSmallRounds = kPermSmall / 256;
 
 // Lanes of the warp holding the same key as this lane, for keys in
@@ -35,24 +36,25 @@ VX_DEVICE unsigned peer_mask(int key) {
   return peers;
 }
 
-// Exclusive scan of one int per thread over a 256-thread CTA; *total gets
+// Exclusive scan of one value per thread over a 256-thread CTA; *total gets
 // the sum (valid on every thread after the call).
-VX_DEVICE int scan256(int v, int* warp_tot, int* total) {
+template <class V>
+VX_DEVICE V scan256(V v, V* warp_tot, V* total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int inc = v;
+  V inc = v;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const int n = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+    const V n = __shfl_up_sync(0xFFFFFFFFu, inc, o);
     if (lane >= o) inc += n;
   }
   __syncthreads();   // warp_tot free from a previous call
   if (lane == 31) warp_tot[warp] = inc;
   __syncthreads();
-  int before = 0, all = 0;
+  V before = 0, all = 0;
 #pragma unroll
   for (int w = 0; w < 8; ++w) {
-    const int t = warp_tot[w];
-    before += w < warp ? t : 0;
+    const V t = warp_tot[w];
+    before += w < warp ? t : V(0);
     all += t;
   }
   *total = all;
@@ -68,11 +70,9 @@ VX_DEVICE void perm_small(const PermSmallArgs& a, const int32_t* ids, int P) {
   int32_t *n_active = a.n_active, *src_rows = a.src_rows, *err = a.err, *items = a.items;
   int32_t* n_items = a.n_items;
   __shared__ int s_cnt[kPermSmallMaxE];                    // ids per expert
-  __shared__ int s_off[kPermSmallMaxE];                    // run starts
   __shared__ int s_run[kPermSmallMaxE];                    // next position of each run
   __shared__ __align__(16) uint16_t s_hist[8][kPermSmallMaxE];   // (round + 1) << 8 | count
-  __shared__ uint16_t s_sorted[kPermSmall];                // expert of each sorted position
-  __shared__ int warp_tot[8];
+  __shared__ uint64_t warp_tot64[8];
   __shared__ int s_bad;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int e = tid; e < E; e += 256) s_cnt[e] = 0;
@@ -106,25 +106,57 @@ VX_DEVICE void perm_small(const PermSmallArgs& a, const int32_t* ids, int P) {
   __syncthreads();
   VX_STAMP(5);
 
-  // run offsets: each thread scans a contiguous block of E/256 experts
+  // run offsets, active experts and work items: each thread takes a
+  // contiguous block of E/256 experts; one scan carries the running counts
+  // of active experts (bits 0-15), items (16-31) and routes (32-47), each at
+  // most kPermSmall
   const int per = (E + 255) / 256, e0 = tid * per;
-  int local = 0;
-  for (int j = 0; j < per; ++j)
-    if (e0 + j < E) local += s_cnt[e0 + j];
-  int routed;
-  int run = scan256(local, warp_tot, &routed);
+  uint64_t local = 0;
   for (int j = 0; j < per; ++j)
     if (e0 + j < E) {
-      s_off[e0 + j] = run;
-      s_run[e0 + j] = run;
-      offsets[e0 + j] = run;
-      run += s_cnt[e0 + j];
+      const uint64_t c = uint64_t(s_cnt[e0 + j]);
+      if (c) local += 1u | (((c + item_chunk - 1) / item_chunk) << 16) | (c << 32);
     }
+  uint64_t all;
+  const uint64_t ex = scan256<uint64_t>(local, warp_tot64, &all);
+  int run = int(ex >> 32) & 0xFFFF, ai = int(ex) & 0xFFFF, ii = int(ex >> 16) & 0xFFFF;
+  const int routed = int(all >> 32) & 0xFFFF, n_act = int(all) & 0xFFFF, n_it = int(all >> 16) & 0xFFFF;
+  for (int j = 0; j < per; ++j) {
+    const int e = e0 + j;
+    if (e >= E) break;
+    const int c = s_cnt[e];
+    s_run[e] = run;
+    offsets[e] = run;
+    if (c) {
+      active[ai++] = e;
+      if (items)
+        for (int q = 0; q < c; q += item_chunk, ++ii) {
+          int32_t* it = items + 3 * ii;
+          it[0] = e;
+          it[1] = run + q;
+          it[2] = min(item_chunk, c - q);
+        }
+    }
+    run += c;
+  }
+  const int sh_items = shared_items > 0 ? (shared_items + item_chunk - 1) / item_chunk : 0;
   if (tid == 0) {
     offsets[E] = routed;
     if (shared_items >= 0) offsets[E + 1] = routed + shared_items;
     if (err && s_bad) atomicAdd(err, s_bad);
+    if (shared_items > 0) active[n_act] = E;
+    *n_active = n_act + (shared_items > 0 ? 1 : 0);
+    if (items) *n_items = n_it + sh_items;
   }
+  if (items)
+    for (int j = tid; j < sh_items; j += 256) {
+      int32_t* it = items + 3 * (n_it + j);
+      it[0] = E;
+      it[1] = routed + j * item_chunk;
+      it[2] = min(item_chunk, shared_items - j * item_chunk);
+    }
+  if (src_rows)
+    for (int t = tid; t < shared_items; t += 256) src_rows[routed + t] = t;
   __syncthreads();
   VX_STAMP(6);
 
@@ -151,61 +183,12 @@ VX_DEVICE void perm_small(const PermSmallArgs& a, const int32_t* ids, int P) {
       }
       order[pos] = i;
       inverse[i] = pos;
-      s_sorted[pos] = uint16_t(kr);
       if (src_rows) src_rows[pos] = src_map ? src_map[i] : i / k_div;
     }
     __syncthreads();   // s_run and s_hist read before they change
     if (kr >= 0 && leader) atomicAdd(&s_run[kr], __popc(peers));
   }
-  __syncthreads();
-
   VX_STAMP(7);
-  // active experts and items, from the runs in sorted order: thread t looks
-  // at sorted positions 4t..4t+3, so thread order is position order
-  int ek[kPermSmallRounds];
-  bool starts[kPermSmallRounds], istart[kPermSmallRounds];
-  int na = 0, ni = 0;
-#pragma unroll
-  for (int j = 0; j < kPermSmallRounds; ++j) {
-    const int pidx = kPermSmallRounds * tid + j;
-    const bool in = pidx < routed;
-    ek[j] = in ? int(s_sorted[pidx]) : 0;
-    starts[j] = in && (pidx == 0 || int(s_sorted[pidx - 1]) != ek[j]);
-    istart[j] = in && ((pidx - s_off[ek[j]]) % item_chunk == 0);
-    na += starts[j] ? 1 : 0;
-    ni += istart[j] ? 1 : 0;
-  }
-  // one scan for both counts (each at most kPermSmall: 16 bits apiece)
-  int both;
-  const int ex = scan256((na << 16) | ni, warp_tot, &both);
-  const int n_act = both >> 16, n_it = both & 0xFFFF;
-  int ai = ex >> 16, ii = ex & 0xFFFF;
-#pragma unroll
-  for (int j = 0; j < kPermSmallRounds; ++j) {
-    const int pidx = kPermSmallRounds * tid + j;
-    if (starts[j]) active[ai++] = ek[j];
-    if (items && istart[j]) {
-      int32_t* it = items + 3 * ii++;
-      it[0] = ek[j];
-      it[1] = pidx;
-      it[2] = min(item_chunk, s_off[ek[j]] + s_cnt[ek[j]] - pidx);
-    }
-  }
-  const int sh_items = shared_items > 0 ? (shared_items + item_chunk - 1) / item_chunk : 0;
-  if (tid == 0) {
-    if (shared_items > 0) active[n_act] = E;
-    *n_active = n_act + (shared_items > 0 ? 1 : 0);
-    if (items) *n_items = n_it + sh_items;
-  }
-  if (items)
-    for (int j = tid; j < sh_items; j += 256) {
-      int32_t* it = items + 3 * (n_it + j);
-      it[0] = E;
-      it[1] = routed + j * item_chunk;
-      it[2] = min(item_chunk, shared_items - j * item_chunk);
-    }
-  if (src_rows)
-    for (int t = tid; t < shared_items; t += 256) src_rows[routed + t] = t;
   VX_STAMP(8);
 }
 
