@@ -269,8 +269,10 @@ cudaError_t launch_softmax_topk(const uint16_t* logits, int T, int E, int k, int
 // then an acquire-release arrival on the token block's counter; the CTA that
 // arrives last (every tile is then visible to it) runs softmax/top-k for
 // the block's 8 tokens (one warp each) and resets the counter.  CTA eb == nEB
-// computes sigmoid(shared_expert_gate(x)) for the 8 tokens.  The counters
-// (one per token block) must be zero at launch.
+// computes sigmoid(shared_expert_gate(x)) for the 8 tokens.  With perm.order
+// set, the token blocks' last CTAs take a second ticket (counter nTB) and the
+// last of them sorts all T*k routes by expert (perm_small).  The counters
+// (one per token block, plus the second ticket) must be zero at launch.
 template <int PER>
 __global__ void __launch_bounds__(32 * kRouterSlices) router_fused_kernel(
     const uint16_t* __restrict__ x, int T, const uint16_t* __restrict__ wg, int E, int K, int k, vx_q4 seg,
