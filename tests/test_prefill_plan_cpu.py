@@ -89,3 +89,22 @@ def test_budgeted_anchors_tiny_budget_and_resume():
     with pytest.raises(ValueError):
         P.plan_chunks(1000, 0, policy="budgeted", budget=10**6, model=huge)
 
+
+
+def test_plans_match_the_reference_planner():
+    """Golden plans written by the reference's own planner (make_prefill_golden.py):
+    grid, balanced and budgeted, cold and resumed; the budgeted ones with the
+    reference's estimate expressed as a ChunkMemoryModel."""
+    import json
+    import os
+    d = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "prefill_plans.json")))
+    assert tuple(d["candidates"]) == P.CANDIDATE_CHUNKS
+    est = d["estimate"]
+    model = P.ChunkMemoryModel(per_token=est["per_token"], pair_bytes=est["pair_bytes"],
+                               query_cap=est["query_cap"], kv_per_token=est["kv_per_token"])
+    for c in d["cases"]:
+        kw = dict(boundaries=c["boundaries"], offset=c["offset"], policy=c["policy"], anchors=c["anchors"])
+        if c["policy"] == "budgeted":
+            kw.update(budget=c["budget"], model=model)
+        got = P.plan_chunks(c["total"], c["chunk"], **kw)
+        assert [list(s) for s in got] == c["spans"], c
