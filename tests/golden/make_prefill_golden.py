@@ -5,11 +5,12 @@ Run in a checkout where the Veystrix-Core reference tree is available:
     python tests/golden/make_prefill_golden.py --reference <path-to-Veystrix-Core>
 
 It imports models/flashnext/prefill.py (the planner of :109-207 and the
-budgeted policy's estimate in prefill_budget.py:115-135).  That module also
-imports MLX and two runtime modules at the top, which the planning functions
-never call; they are replaced by empty stand-ins for the import.  The plans
-are written to prefill_plans.json beside this script; nothing at test time
-touches the reference tree.
+budgeted policy's estimate in prefill_budget.py:115-135) and layer_major.py
+(the window planner of :155-186).  Those modules also import MLX and two
+runtime modules at the top, which the planning functions never call; they are
+replaced by empty stand-ins for the import.  The plans are written to
+prefill_plans.json beside this script; nothing at test time touches the
+reference tree.
 """
 from __future__ import annotations
 
@@ -35,6 +36,16 @@ CASES = [
     (3000, 0, [], 0, "budgeted", None, 100),
 ]
 
+WINDOWS = [
+    # (total, chunk, offset, window, required, anchors)
+    (9000, 2048, 0, 4096, [], []),
+    (9000, 2048, 0, 8192, [4096], []),
+    (9000, 2048, 0, 8192, [], [6144]),
+    (12000, 1024, 3000, 6000, [7000], [10000, 12500]),
+    (20000, 512, 0, 3000, [], [1536, 2560, 9000]),
+    (6000, 5000, 0, 4096, [], []),
+]
+
 
 def main() -> None:
     ap = argparse.ArgumentParser()
@@ -48,7 +59,7 @@ def main() -> None:
     qsa = types.ModuleType("qsa_chunk")
     qsa.QSA_CHUNK_THRESHOLD = 2048
     sys.modules["models.flashnext.qsa_chunk"] = qsa
-    from models.flashnext import prefill, prefill_budget
+    from models.flashnext import layer_major, prefill, prefill_budget
 
     out = {"estimate": {"per_token": prefill_budget.PER_TOKEN_TRANSIENT,
                         "pair_bytes": prefill_budget.SDPA_PAIR_BYTES,
@@ -63,10 +74,17 @@ def main() -> None:
                              "policy": policy, "anchors": anchors,
                              "budget": None if mb is None else prefill.chunk_budget_bytes(),
                              "spans": [list(s) for s in spans]})
+    out["windows"] = []
+    for total, chunk, offset, window, required, anchors in WINDOWS:
+        spans = prefill.plan_chunks(total, chunk, [], offset, policy="grid")
+        groups = layer_major.plan_windows(spans, offset, window, required, anchors)
+        out["windows"].append({"spans": [list(x) for x in spans], "offset": offset, "window": window,
+                               "required": required, "anchors": anchors,
+                               "groups": [[list(x) for x in g] for g in groups]})
     path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "prefill_plans.json")
     with open(path, "w") as f:
         json.dump(out, f, indent=1)
-    print(f"wrote {len(out['cases'])} plans to {path}")
+    print(f"wrote {len(out['cases'])} plans and {len(out['windows'])} window plans to {path}")
 
 
 if __name__ == "__main__":

@@ -108,3 +108,16 @@ def test_plans_match_the_reference_planner():
             kw.update(budget=c["budget"], model=model)
         got = P.plan_chunks(c["total"], c["chunk"], **kw)
         assert [list(s) for s in got] == c["spans"], c
+
+
+def test_windows_match_the_reference_planner():
+    """Golden layer-major windows from the reference's plan_windows
+    (layer_major.py:155-186), required positions and anchors included."""
+    import json
+    import os
+    d = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "prefill_plans.json")))
+    assert d["windows"]
+    for w in d["windows"]:
+        spans = [tuple(s) for s in w["spans"]]
+        got = P.plan_windows(spans, w["offset"], w["window"], w["required"], w["anchors"])
+        assert [[list(s) for s in g] for g in got] == w["groups"], w
