@@ -73,6 +73,17 @@ def peaks():
         return 6650.0, 1590.0, "fallback"
 
 
+def block_launches(T, k=TOPK, E=EXPERTS):
+    """Kernels one single-GPU block call launches (the library's dispatch):
+    the router, with the expert sort in its last token block while T*k <=
+    1024, else a permutation launch (three above 16,384 routes); then the
+    activation records, gate/up and down GEMVs (decode), or the x gather and
+    the two tcgen05 GEMMs (T*k >= 4E); then the combine."""
+    P = T * k
+    perm = 0 if P <= 1024 else (1 if P <= 16384 else 3)
+    return 1 + perm + 3 + 1
+
+
 def layer_bytes(U, T):
     """Algorithmic bytes of one layer step: each touched expert once, the
     shared expert, the router, the shared gate row, x in and y out."""
@@ -338,7 +349,7 @@ def main_stack(args):
                 "h2d_bytes_per_step": T * HIDDEN * 2, "d2h_bytes_per_step": T * HIDDEN * 2},
         "cpu_baseline": cpu,
         "clocks": clocks,
-        "gpu_launches": 7 * L * K,   # per layer: RMSNorm + the block's six kernels
+        "gpu_launches": (1 + block_launches(T)) * L * K,   # per layer: RMSNorm + the block's kernels
     }
     print(json.dumps(line), flush=True)
 
@@ -585,10 +596,11 @@ def main():
     nx = K + W
     xs = (torch.randn((nx, T, HIDDEN), device=dev, generator=g)).to(torch.bfloat16)
     torch.cuda.synchronize()
-    # our kernels per step: router, permute, activation records, gate/up, down, combine;
-    # EP adds the shared expert's own pass (permute .. unpermute) and, on the peer
-    # transport, dispatch, the dispatch wait and the combine
-    launches_per_step = 6 if world == 1 else (14 if args.ep_transport == "p2p" else 11)
+    # our kernels per step on one GPU: block_launches(T); EP runs the router, the
+    # shard's pass (permute, activation records, gate/up, down), the shared expert's own
+    # pass (permute .. unpermute) and, on the peer transport, dispatch, the dispatch
+    # wait and the combine
+    launches_per_step = block_launches(T) if world == 1 else (14 if args.ep_transport == "p2p" else 11)
 
     def step(i):
         return layers[i % len(layers)](xs[i])
