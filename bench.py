@@ -649,6 +649,27 @@ def main():
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
     clocks = sampler.stop() if sampler else None
 
+    # spread of single steps (outside the timed regions): each of up to 200
+    # steps between its own pair of events; per step the max over ranks
+    n_dist = min(K, 200)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(n_dist)]
+    barrier()
+    for i, (a, b) in enumerate(evs):
+        a.record(stream)
+        step(W + i)
+        b.record(stream)
+    barrier()
+    per_step = torch.tensor([a.elapsed_time(b) for a, b in evs], device=dev, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(per_step, op=dist.ReduceOp.MAX)
+    per_step = sorted(per_step.tolist())
+
+    def pct(f):
+        return round(per_step[min(len(per_step) - 1, int(f * (len(per_step) - 1) + 0.5))], 5)
+
+    step_dist = {"steps": n_dist, "median": pct(0.5), "p10": pct(0.1), "p90": pct(0.9)}
+
     # routing statistics (outside the timed regions): distinct experts this
     # rank's weights serve per step (under expert parallelism, among the
     # tokens of all ranks routed to its shard)
@@ -719,6 +740,8 @@ def main():
         "steps": K, "warmup": W, "ms_per_step": round(ms / K, 5), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": config_dict(args, world),
+        # single steps timed one by one after the timed region (launch gaps included)
+        "step_ms_spread": step_dist,
         "hbm": {"achieved_gbs": round(achieved_layer, 1),
                 "frac_of_8tbps": round(achieved_layer / NOMINAL_HBM_GBS, 4),
                 "frac_of_measured": round(achieved_layer / hbm_gbs, 4),
