@@ -715,7 +715,7 @@ def main():
     if rank != 0:
         return
 
-    hbm_gbs, _, peak_kind = peaks()
+    hbm_gbs, bf16_tflops, peak_kind = peaks()
     value = K * T * world / (ms / 1000.0)
     total_bytes = sum(layer_bytes(U, T) for U in Us)
     achieved_layer = total_bytes / (ms / 1000.0) / 1e9
@@ -727,9 +727,17 @@ def main():
         ach = b / (avg_ms / 1000.0) / 1e9 if b else None
         roof = {"kernel": dom, "bound": "hbm", "achieved": round(ach, 1) if ach else None,
                 "peak": hbm_gbs, "unit": "GB/s", "frac": round(ach / hbm_gbs, 4) if ach else None,
-                "traffic": traffic_for(dom), "peak_kind": peak_kind,
+                "traffic": traffic_for(dom, T), "peak_kind": peak_kind,
                 "algorithmic_bytes_per_launch": int(b) if b else None,
                 "avg_launch_ms": round(avg_ms, 5)}
+    # prefill batches run the tcgen05 GEMMs: their tensor-pipe rate beside the HBM roofline
+    tensor = None
+    if world == 1 and T * TOPK >= 4 * EXPERTS and "gate_up_swiglu" in stages:
+        flops = 2.0 * HIDDEN * 2 * (T * TOPK * INTER + T * SHARED_INTER)   # gate and up, routed + shared
+        tf = flops / (stages["gate_up_swiglu"][1] / 1000.0) / 1e12
+        tensor = {"kernel": "gate_up_swiglu", "achieved": round(tf, 1), "peak": bf16_tflops,
+                  "unit": "TFLOP/s", "frac": round(tf / bf16_tflops, 4),
+                  "peak_kind": f"{peak_kind} bf16 GEMM burst", "flops_per_launch": int(flops)}
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         v, cores, kind, sample, _ = cpu_oracle_time(40, 2, budget_s=15.0, tokens=T)
@@ -742,6 +750,7 @@ def main():
         "config": config_dict(args, world),
         # single steps timed one by one after the timed region (launch gaps included)
         "step_ms_spread": step_dist,
+        "tensor_roofline": tensor,
         "hbm": {"achieved_gbs": round(achieved_layer, 1),
                 "frac_of_8tbps": round(achieved_layer / NOMINAL_HBM_GBS, 4),
                 "frac_of_measured": round(achieved_layer / hbm_gbs, 4),
@@ -757,13 +766,14 @@ def main():
     print(json.dumps(line), flush=True)
 
 
-def traffic_for(kernel):
-    """DRAM bytes per launch of `kernel` from the committed ncu summary, if any."""
+def traffic_for(kernel, tokens):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary, when
+    it was captured on this workload (the same tokens per step), else None."""
     path = os.path.join(ROOT, "profiles", "ncu_traffic.json")
     try:
         with open(path) as fh:
-            d = json.load(fh)
-        return d.get(kernel, {}).get("dram_bytes_per_launch")
+            d = json.load(fh).get(kernel, {})
+        return d.get("dram_bytes_per_launch") if d.get("tokens") == tokens else None
     except Exception:
         return None
 
