@@ -2,10 +2,12 @@
  * vxmoe.h - C ABI of the B200 (sm_100a) routed sparse-MoE block.
  *
  * Plain pointers, sizes and a cudaStream_t (passed as void*).  Every pointer
- * is device memory owned by the caller; the library allocates nothing and
- * takes scratch space only from the caller's workspace.  Every entry point
- * is stream-ordered on the caller's stream, performs no host synchronisation
- * and returns a vx_status code.
+ * is device memory owned by the caller; the library allocates no device
+ * memory.  Scratch space comes from a workspace the caller passes, except for
+ * vx_moe_block_noalloc, which uses the library's own static device array of
+ * VX_NOALLOC_SCRATCH_BYTES instead.  Every entry point is stream-ordered on
+ * the caller's stream, performs no host synchronisation and returns a
+ * vx_status code.
  *
  * bf16 values travel as uint16_t bit patterns.  Q4 weights use the MLX
  * affine layout of the reference: uint32 words along the input axis, element
@@ -220,10 +222,13 @@ int vx_moe_block(const uint16_t* x, int32_t T, const vx_moe_weights* W,
  * code that must not call cudaMalloc once it is running).  No counterpart in
  * the reference.  Scratch comes from a static device array of
  * VX_NOALLOC_SCRATCH_BYTES inside the library, which every GPU that loads the
- * library keeps until the process exits.  A batch whose scratch
- * (vx_moe_block_workspace) exceeds the array returns VX_EWORKSPACE.  The
- * first call on a device looks up the array's device address (set-up, once
- * per device); make that first call before any stream capture.  All calls
+ * library keeps until the process exits.  Arguments are checked as
+ * vx_moe_block checks them (same status codes; T == 0 returns VX_OK); then a
+ * batch whose scratch (vx_moe_block_workspace) exceeds the array returns
+ * VX_EWORKSPACE.  The first call on a device looks up the array's device
+ * address (set-up, once per device, repeated only if the device's context
+ * changes, e.g. after cudaDeviceReset); make that first call before any
+ * stream capture.  All calls
  * share one array: calls that overlap on the GPU (other streams, other host
  * threads) race and must be serialised by the caller.  Allocates nothing. */
 #define VX_NOALLOC_SCRATCH_BYTES (2u << 20)

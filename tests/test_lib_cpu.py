@@ -162,22 +162,3 @@ def test_build_executor_infers_dimensions_from_packs():
     assert (ex.expert_count, ex.hidden_size, ex.top_k) == (4, 64, 2)
     with pytest.raises(ValueError):
         build_executor(packs=packs, bits=8)
-
-
-def test_router_timeline_tool_compiles(tmp_path):
-    """The trace tool compiles the library's router source with its trace
-    points enabled; it must keep building as that source changes (nvcc
-    cross-compiles for sm_100a without a GPU)."""
-    import shutil
-    import subprocess
-    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
-    if not os.path.exists(nvcc):
-        pytest.skip("nvcc not available")
-    src = os.path.join(ROOT, "veystrix-core_b200", "trace", "router_timeline.cu")
-    out = tmp_path / "router_timeline"
-    r = subprocess.run([nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17",
-                        "-I", os.path.join(ROOT, "include"),
-                        "-I", os.path.join(ROOT, "veystrix-core_b200", "csrc"), src, "-o", str(out)],
-                       capture_output=True, text=True, timeout=600)
-    assert r.returncode == 0, r.stderr[-2000:]
-    assert out.exists()

@@ -394,6 +394,19 @@ struct RouterScratch {
   uint16_t* logits;
 };
 
+// The checks vx_moe_block makes before it looks at the workspace: the
+// weights, the token count and the activation pointers.  VX_OK for a valid
+// call (T == 0 included).
+int block_args_status(const uint16_t* x, int T, const vx_moe_weights* W, const uint16_t* y) {
+  BlockDims dm;
+  int s = check_weights(W, true, &dm);
+  if (s) return s;
+  if (T < 0) return VX_EINVAL_SHAPE;
+  if (T == 0) return VX_OK;
+  if (!x || !y || !aligned16(x)) return VX_EINVAL_SHAPE;
+  return VX_OK;
+}
+
 }  // namespace vx
 
 using namespace vx;
@@ -703,12 +716,10 @@ size_t vx_moe_block_workspace(int32_t T, const vx_moe_weights* W) {
 
 int vx_moe_block(const uint16_t* x, int32_t T, const vx_moe_weights* W, uint16_t* y, int32_t* inds,
                  uint16_t* weights, void* workspace, size_t workspace_bytes, void* stream) {
+  int s = block_args_status(x, T, W, y);
+  if (s || T == 0) return s;
   BlockDims dm;
-  int s = check_weights(W, true, &dm);
-  if (s) return s;
-  if (T < 0) return VX_EINVAL_SHAPE;
-  if (T == 0) return VX_OK;
-  if (!x || !y || !aligned16(x)) return VX_EINVAL_SHAPE;
+  check_weights(W, true, &dm);
   if (!workspace || workspace_bytes < vx_moe_block_workspace(T, W)) return VX_EWORKSPACE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   Carver c(workspace);

@@ -8,12 +8,6 @@
 
 #define VX_DEVICE __device__ __forceinline__
 
-// Trace points (a CTA's thread 0 records a timestamp for a numbered phase):
-// empty unless a timing build defines VX_STAMP before including the sources.
-#ifndef VX_STAMP
-#define VX_STAMP(slot) ((void)0)
-#endif
-
 namespace vx {
 
 constexpr int kWarp = 32;
@@ -165,6 +159,10 @@ VX_DEVICE Q4Ptr q4_expert(const vx_q4& bank, int e) {
 
 // Host-side launch check used by every entry point.
 int vx_cuda_fail(cudaError_t e);
+namespace vx {
+// Argument checks of vx_moe_block short of the workspace (vx_abi.cu).
+int block_args_status(const uint16_t* x, int T, const vx_moe_weights* W, const uint16_t* y);
+}  // namespace vx
 
 #define VX_LAUNCH_CHECK()                                   \
   do {                                                      \

@@ -104,7 +104,6 @@ VX_DEVICE void perm_small(const PermSmallArgs& a, const int32_t* ids, int P) {
   }
   if (nbad) atomicAdd(&s_bad, nbad);
   __syncthreads();
-  VX_STAMP(5);
 
   // run offsets, active experts and work items: each thread takes a
   // contiguous block of E/256 experts; one scan carries the running counts
@@ -158,7 +157,6 @@ VX_DEVICE void perm_small(const PermSmallArgs& a, const int32_t* ids, int P) {
   if (src_rows)
     for (int t = tid; t < shared_items; t += 256) src_rows[routed + t] = t;
   __syncthreads();
-  VX_STAMP(6);
 
   // stable position of each valid id, one round of 256 ids at a time
   static_assert(kPermSmallMaxE <= 1024, "peer_mask covers 10-bit keys");
@@ -188,8 +186,6 @@ VX_DEVICE void perm_small(const PermSmallArgs& a, const int32_t* ids, int P) {
     __syncthreads();   // s_run and s_hist read before they change
     if (kr >= 0 && leader) atomicAdd(&s_run[kr], __popc(peers));
   }
-  VX_STAMP(7);
-  VX_STAMP(8);
 }
 
 }  // namespace vx

@@ -178,7 +178,6 @@ __device__ __forceinline__ void topk_row(const uint16_t* lr, int E, int k, int32
   }
   uint32_t key[PER];
   float m = -INFINITY;
-  VX_STAMP(9);
 #pragma unroll
   for (int j = 0; j < PER; ++j) {
     const int e = e0 + j;
@@ -193,7 +192,6 @@ __device__ __forceinline__ void topk_row(const uint16_t* lr, int E, int k, int32
     if (e0 + j < E) s += expf(__fsub_rn(key_logit(key[j]), m));
   s = warp_sum<32>(s);
   const float inv = __fdiv_rn(1.0f, s);
-  VX_STAMP(10);
 
   uint32_t lm = 0;
 #pragma unroll
@@ -211,7 +209,6 @@ __device__ __forceinline__ void topk_row(const uint16_t* lr, int E, int k, int32
       }
     }
   }
-  VX_STAMP(11);
   const int my_i = int(0xFFFFu - (my_key & 0xFFFFu));
   const float my_p = bf16r(__fmul_rn(expf(__fsub_rn(key_logit(my_key), m)), inv));
   float tot = 0.f;
@@ -280,7 +277,6 @@ __global__ void __launch_bounds__(32 * kRouterSlices) router_fused_kernel(
     uint16_t* __restrict__ sg, int32_t* __restrict__ counters, PermSmallArgs perm,
     const uint16_t* __restrict__ bias) {
   chain_begin();
-  VX_STAMP(0);
   const int nEB = (E + 15) / 16;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = blockIdx.y * 8;
@@ -349,7 +345,6 @@ __global__ void __launch_bounds__(32 * kRouterSlices) router_fused_kernel(
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) red[warp][lane][i] = d[i];
-  VX_STAMP(1);
   __syncthreads();
   if (warp == 0) {
     float v[4] = {0.f, 0.f, 0.f, 0.f};
@@ -382,7 +377,6 @@ __global__ void __launch_bounds__(32 * kRouterSlices) router_fused_kernel(
   }
   __syncthreads();
   if (!s_last) return;
-  VX_STAMP(2);
   const int t = t0 + warp;
   if (t < T)
     topk_row<PER, true>(logits + int64_t(t) * E, E, k, inds + int64_t(t) * k, nullptr, weights + int64_t(t) * k,
@@ -394,7 +388,6 @@ __global__ void __launch_bounds__(32 * kRouterSlices) router_fused_kernel(
     // barrier puts this block's ids before thread 0's acquire-release add.
     __shared__ int s_final;
     __syncthreads();   // every token's ids of this block are written
-    VX_STAMP(3);
     if (threadIdx.x == 0) {
       int prev = 0;
       if (gridDim.y > 1)
@@ -406,7 +399,6 @@ __global__ void __launch_bounds__(32 * kRouterSlices) router_fused_kernel(
     }
     __syncthreads();
     if (s_final) {
-      VX_STAMP(4);
       perm_small(perm, inds, T * k);
       if (threadIdx.x == 0) counters[gridDim.y] = 0;
     }
