@@ -15,6 +15,11 @@ e2e        the same through the public API with x copied from pinned host
            memory and y copied back inside the timed region.
 roofline   the dominant kernel's algorithmic bytes per launch over its
            CUDA-event duration against the measured HBM copy bandwidth.
+c1_decode_1_token, c4_prefill_2048_tokens
+           (single GPU, default run) the two north-star shapes - BASELINE
+           config 1 (one decode token) and config 4 (2,048-token prefill) -
+           timed in the same process on the same rotating pools: step time,
+           HBM fraction and, for C4, the gate/up GEMM's tensor-pipe rate.
 """
 from __future__ import annotations
 
@@ -58,6 +63,8 @@ def parse():
                     help="expert-parallel exchange: peer stores over NVLink or NCCL all-to-all")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch the block's kernels one by one instead of replaying a CUDA graph")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the C1 (1 token) and C4 (2,048 tokens) sub-measurements of the default run")
     ap.add_argument("--layout", default="tiled", choices=("tiled", "mlx"),
                     help="expert weights as the tiled resident pool (default) or the MLX arrays")
     return ap.parse_args()
@@ -104,17 +111,19 @@ def stage_bytes(stage, U, T):
 class ClockSampler:
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap,"
+              "utilization.gpu")
 
-    def __init__(self, index):
+    def __init__(self, index, period_ms=50):
         self.path = tempfile.mktemp(suffix=".csv")
         self.fh = open(self.path, "w")
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100", "-i", str(index)], stdout=self.fh, stderr=subprocess.DEVNULL)
+                 "-lms", str(period_ms), "-i", str(index)], stdout=self.fh, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+        self.t0 = time.time()
 
     def stop(self):
         if self.proc is None:
@@ -125,25 +134,35 @@ class ClockSampler:
         except Exception:
             self.proc.kill()
         self.fh.close()
-        sm, mx, reasons = [], [], set()
+        sm, mx, busy, reasons = [], [], [], set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
         for line in open(self.path):
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
+                clk, top = float(parts[1]), float(parts[2])
             except ValueError:
                 continue
+            sm.append(clk)
+            mx.append(top)
+            try:
+                if float(parts[9]) >= 50.0:
+                    busy.append(clk)
+            except ValueError:
+                pass
             for name, val in zip(names, parts[5:9]):
                 if val.lower().startswith("active"):
                     reasons.add(name)
         os.unlink(self.path)
         if not sm:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "samples": len(sm),
-                "reasons": sorted(reasons)}
+        # the window also holds host-side set-up with the GPU idle: the median
+        # is taken over the samples with the GPU busy (utilisation >= 50 %)
+        return {"sm_mhz": statistics.median(busy or sm), "sm_max_mhz": max(mx),
+                "samples": len(sm), "samples_under_load": len(busy), "reasons": sorted(reasons),
+                "window": f"sampled every 50 ms from before warm-up to the end of the GPU work "
+                          f"({time.time() - self.t0:.1f} s)"}
 
 
 # --------------------------------------------------------------------------
@@ -151,11 +170,22 @@ class ClockSampler:
 # --------------------------------------------------------------------------
 
 
-def cpu_oracle_time(steps, warmup, budget_s, tokens=64, seed=0):
+def cpu_sample(args):
+    """The CPU sample both legs time (the cpu_baseline of the vxmoe arm and the
+    reference arm), fixed by the command line alone so that the two legs of
+    one driver run time the same work: steps of the workload's own token
+    count, at most 4,096 tokens in all (about 5-10 s of the restatement on 16
+    host threads), after three untimed warm-up steps."""
+    tokens = args.tokens
+    steps = max(2, min(args.steps, 4096 // max(1, tokens)))
+    return steps, 3, tokens
+
+
+def cpu_oracle_time(steps, warmup, tokens=64, seed=0):
     """Time the CPU restatement of the block (the reference's MLX path is not
-    installable here) on steps of the benchmark workload, shrinking the
-    tokens per step (powers of two) so `steps` fit in about `budget_s`.
-    Returns (tokens/s, cores, kind, sample description, tokens per step)."""
+    installable here) on `steps` batches of `tokens` tokens of the benchmark
+    workload.  Returns (tokens/s over the timed steps, cores, kind, sample
+    description)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import numpy as np
     import vxmoe_oracle as O
@@ -168,34 +198,29 @@ def cpu_oracle_time(steps, warmup, budget_s, tokens=64, seed=0):
         runner, cores = (lambda x: O.moe_block(x, params)), 1
         impl = "NumPy restatement of the block on 1 host thread"
     rng = np.random.default_rng(seed + 1)
-    probe = O.bf16_round(rng.normal(0, 1, size=(tokens, HIDDEN)))
-    runner(probe)
-    t0 = time.perf_counter()
-    runner(probe)
-    t_full = time.perf_counter() - t0
-    per = tokens
-    while per > 1 and steps * t_full * per / tokens > budget_s:
-        per //= 2
-    xs = [O.bf16_round(rng.normal(0, 1, size=(per, HIDDEN))) for _ in range(steps + warmup)]
+    xs = [O.bf16_round(rng.normal(0, 1, size=(tokens, HIDDEN))) for _ in range(steps + warmup)]
     for i in range(warmup):
         runner(xs[i])
-    t0 = time.perf_counter()
+    per_step = []
     for i in range(steps):
+        t0 = time.perf_counter()
         runner(xs[warmup + i])
-    dt = time.perf_counter() - t0
-    sample = (f"{impl} (MLX unavailable): {steps} steps of {per} of the workload's {tokens} "
-              f"decode tokens, same layer shape and distributions")
-    return steps * per / dt, cores, "port", sample, per
+        per_step.append(time.perf_counter() - t0)
+    dt = sum(per_step)
+    sample = (f"{impl} (MLX unavailable): {steps} timed steps of {tokens} tokens after {warmup} "
+              f"warm-up steps, same layer shape and distributions; median step "
+              f"{1000.0 * statistics.median(per_step):.1f} ms")
+    return steps * tokens / dt, cores, "port", sample
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    v, cores, kind, sample, per_step = cpu_oracle_time(args.steps, max(1, min(args.warmup, 3)),
-                                                       budget_s=150.0, tokens=args.tokens)
+    steps, warmup, tokens = cpu_sample(args)
+    v, cores, kind, sample = cpu_oracle_time(steps, warmup, tokens=tokens)
     line = {
         "metric": METRIC, "value": round(v, 3), "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000.0 * per_step / v, 3),
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000.0 * tokens / v, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic", "impl": "reference",
         "config": config_dict(args, world),
@@ -277,10 +302,10 @@ def main_stack(args):
         return h_out
 
     stream = torch.cuda.current_stream(dev)
+    sampler = ClockSampler(dev.index)
     for i in range(W):
         step(xs[i])
     torch.cuda.synchronize()
-    sampler = ClockSampler(dev.index)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(K):
@@ -297,7 +322,6 @@ def main_stack(args):
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
-    clocks = sampler.stop()
 
     # routing statistics and stage times: one step without the graph
     h = xs[W].clone()
@@ -311,6 +335,7 @@ def main_stack(args):
     stages = _lib.profile_read()
     _lib.profile_enable(False)
     torch.cuda.synchronize()
+    clocks = sampler.stop()
 
     hbm_gbs, _, peak_kind = peaks()
     step_bytes = sum(layer_bytes(U, T) for U in Us)
@@ -326,7 +351,8 @@ def main_stack(args):
                 "avg_launch_ms": round(stages[dom][1], 5)}
     cpu = None
     if not args.no_cpu_baseline:
-        v, cores, kind, sample, _ = cpu_oracle_time(10, 1, budget_s=10.0, tokens=T)
+        steps_c, warm_c, _ = cpu_sample(args)
+        v, cores, kind, sample = cpu_oracle_time(steps_c, warm_c, tokens=T)
         cpu = {"value": round(v / L, 4), "unit": "tokens/s", "cores": cores, "kind": kind,
                "sample": sample + f"; one layer timed, tokens/s divided by {L} layers"}
     line = {
@@ -430,10 +456,10 @@ def main_c5(args):
         return float(t.item())
 
     stream = torch.cuda.current_stream(dev)
+    sampler = ClockSampler(dev.index) if rank == 0 else None
     for i in range(W):
         step(xs[i % 2])
     barrier()
-    sampler = ClockSampler(dev.index) if rank == 0 else None
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     e0.record(stream)
@@ -618,10 +644,10 @@ def main():
         return float(t.item())
 
     stream = torch.cuda.current_stream(dev)
+    sampler = ClockSampler(dev.index) if rank == 0 else None
     for i in range(W):
         step(i)
     barrier()
-    sampler = ClockSampler(dev.index) if rank == 0 else None
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     e0.record(stream)
@@ -647,7 +673,6 @@ def main():
     e1.record(stream)
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
-    clocks = sampler.stop() if sampler else None
 
     # spread of single steps (outside the timed regions): each of up to 200
     # steps between its own pair of events; per step the max over ranks
@@ -700,6 +725,12 @@ def main():
     _lib.profile_enable(False)
     barrier()
 
+    # the two north-star shapes on the same rotating pools (single GPU)
+    extra = None
+    if world == 1 and T == 64 and args.layout == "tiled" and not args.no_graph and not args.no_extra:
+        extra = extra_configs(pools, W, K, dev, stream)
+    clocks = sampler.stop() if sampler else None
+
     ep_timeouts = 0
     if dist is not None:
         from vxmoe import ep as ep_mod
@@ -740,7 +771,8 @@ def main():
                   "peak_kind": f"{peak_kind} bf16 GEMM burst", "flops_per_launch": int(flops)}
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        v, cores, kind, sample, _ = cpu_oracle_time(40, 2, budget_s=15.0, tokens=T)
+        steps_c, warm_c, tok_c = cpu_sample(args)
+        v, cores, kind, sample = cpu_oracle_time(steps_c, warm_c, tokens=tok_c)
         cpu = {"value": round(v, 3), "unit": "tokens/s", "cores": cores, "kind": kind,
                "sample": sample}
     line = {
@@ -763,7 +795,77 @@ def main():
         "clocks": clocks,
         "gpu_launches": launches_per_step * K,
     }
+    if extra is not None:
+        line.update(extra)
     print(json.dumps(line), flush=True)
+
+
+def extra_configs(pools, W, K, dev, stream):
+    """BASELINE config 1 (one decode token) and config 4 (a 2,048-token
+    prefill) through the same resident pools as the headline, each pool's
+    block captured as a CUDA graph for that batch size and the pools rotated
+    per step (inputs larger than L2).  Returns the two sub-objects of the
+    JSON line: step time, tokens/s, the layer's algorithmic HBM bytes over the
+    step time and, for C4, the gate/up GEMM's tensor-pipe rate."""
+    import torch
+    import vxmoe
+    from vxmoe import _lib
+    hbm_gbs, tf_burst, peak_kind = peaks()
+    out = {}
+    for key, T, steps in (("c1_decode_1_token", 1, max(K, 100)),
+                          ("c4_prefill_2048_tokens", 2048, max(3, min(K, 10)))):
+        g = torch.Generator(device=dev)
+        g.manual_seed(9000 + T)
+        xs = torch.randn((W + steps, T, HIDDEN), device=dev, generator=g).to(torch.bfloat16)
+        graphs = [vxmoe.GraphedBlock(w, T) for w in pools]
+        for i in range(W):
+            graphs[i % len(graphs)](xs[i])
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(steps):
+            graphs[(W + i) % len(graphs)](xs[W + i])
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        Us = []
+        for i in range(steps):
+            w = pools[(W + i) % len(pools)]
+            r = vxmoe.route(xs[W + i], w.router_w, TOPK, w.shared_expert_gate)
+            Us.append(int(torch.unique(r.inds).numel()))
+        n_prof = min(steps, 20)
+        _lib.profile_enable(True)
+        for i in range(n_prof):
+            vxmoe.moe_block(xs[W + i], pools[(W + i) % len(pools)])
+        stages = _lib.profile_read()
+        _lib.profile_enable(False)
+        torch.cuda.synchronize()
+        del graphs
+        step_bytes = sum(layer_bytes(U, T) for U in Us) / len(Us)
+        gbs = step_bytes / (ms / 1000.0) / 1e9
+        entry = {
+            "tokens": T, "steps": steps, "ms_per_step": round(ms, 5),
+            "tokens_per_s": round(T / (ms / 1000.0), 1),
+            "hbm": {"achieved_gbs": round(gbs, 1), "frac_of_8tbps": round(gbs / NOMINAL_HBM_GBS, 4),
+                    "frac_of_measured": round(gbs / hbm_gbs, 4), "bytes_per_step": int(step_bytes),
+                    "distinct_experts_mean": round(sum(Us) / len(Us), 1)},
+            "stages_ms": {k: round(v[1], 5) for k, v in stages.items()},
+            "launch": "one CUDA graph per weight pool, pools rotated per step",
+        }
+        if T == 1:
+            entry["north_star"] = ">= 0.70 of 8 TB/s at decode batch 1 (hbm.frac_of_8tbps)"
+        if "gate_up_swiglu" in stages and T * TOPK >= 4 * EXPERTS:
+            flops = 2.0 * HIDDEN * 2 * (T * TOPK * INTER + T * SHARED_INTER)
+            tf = flops / (stages["gate_up_swiglu"][1] / 1000.0) / 1e12
+            layer_tf = LAYER_FLOPS_PER_TOKEN * T / (ms / 1000.0) / 1e12
+            entry["tensor_roofline"] = {
+                "kernel": "gate_up_swiglu", "achieved": round(tf, 1), "peak": tf_burst,
+                "unit": "TFLOP/s", "frac": round(tf / tf_burst, 4),
+                "peak_kind": f"{peak_kind} bf16 GEMM burst", "flops_per_launch": int(flops),
+                "layer_frac": round(layer_tf / tf_burst, 4),
+                "north_star": ">= 0.60 of dense bf16 peak at 2,048-token prefill (frac)"}
+        out[key] = entry
+    return out
 
 
 def traffic_for(kernel, tokens):
