@@ -29,6 +29,7 @@ at the last chunk edge that fits.
 """
 from __future__ import annotations
 
+import bisect
 from dataclasses import dataclass
 from typing import Callable, List, Optional, Sequence, Tuple
 
@@ -81,47 +82,91 @@ def block_memory_model(weights, **model) -> ChunkMemoryModel:
 
 
 def budgeted_chunk(position: int, cap: int, budget: int, model: ChunkMemoryModel) -> int:
-    """Largest candidate chunk <= cap whose increment at `position` fits the
-    budget; the smallest candidate when none fits (prefill.py:109-117)."""
-    cands = [c for c in CANDIDATE_CHUNKS if c <= cap] or [min(CANDIDATE_CHUNKS)]
-    for c in cands:
-        if model.increment(c, position) <= budget:
-            return c
-    return cands[-1]
+    """The chunk the budgeted policy takes at `position`: the largest
+    candidate size not above `cap` whose memory increment there fits the
+    budget, else the smallest size allowed (prefill.py:109-117)."""
+    sizes = sorted((c for c in CANDIDATE_CHUNKS if c <= cap), reverse=True)
+    if not sizes:
+        sizes = [min(CANDIDATE_CHUNKS)]
+    fitting = (c for c in sizes if model.increment(c, position) <= budget)
+    return next(fitting, sizes[-1])
+
+
+# -- one walk for every policy ------------------------------------------------
+#
+# A plan is the list of cut positions a walk from position 0 to the prompt's
+# end makes.  Each policy is a step function: the policy's next cut after a
+# position (the walk never steps past an anchor, so a step only needs the
+# anchor-bounded segment it starts in).  Anchors are cuts of every policy.
+# Because each cut depends only on the position it is taken from, the cuts
+# after any cut of the cold plan are the same whether the walk starts at 0
+# or there: a run resumed at a cut takes the cold run's remaining spans.
+
+Step = Callable[[int, int], int]   # (position, segment end) -> next cut (may pass the segment end)
+
+
+def _walk(end: int, step: Step, anchors: Sequence[int], merge_short_tail: bool) -> List[int]:
+    """Cuts in (0, end) of the walk: at each position the nearer of the
+    policy's next cut and the next anchor.  With `merge_short_tail` a last
+    piece shorter than MIN_CHUNK_TOKENS joins the one before it, unless the
+    cut before it is an anchor."""
+    stops = sorted({int(a) for a in anchors if 0 < int(a) < end})
+    cuts: List[int] = []
+    pos, k = 0, 0
+    while pos < end:
+        while k < len(stops) and stops[k] <= pos:
+            k += 1
+        seg_end = stops[k] if k < len(stops) else end
+        nxt = min(step(pos, seg_end), seg_end)
+        if nxt <= pos:
+            raise RuntimeError("chunk plan made no progress")
+        if nxt < end:
+            cuts.append(nxt)
+        pos = nxt
+    if merge_short_tail and cuts and end - cuts[-1] < MIN_CHUNK_TOKENS and cuts[-1] not in stops:
+        cuts.pop()
+    return cuts
+
+
+def _grid_step(chunk: int) -> Step:
+    # the next multiple of the chunk size (absolute positions)
+    return lambda pos, seg_end: (pos // chunk + 1) * chunk if chunk else seg_end
+
+
+def _balanced_step(chunk: int, segment_start: Callable[[int], int]) -> Step:
+    # a segment of n tokens in ceil(n / chunk) pieces as equal as integers
+    # allow, the longer pieces first: the cut after `pos` is the first piece
+    # boundary past it
+    def step(pos: int, seg_end: int) -> int:
+        lo = segment_start(pos)
+        n = seg_end - lo
+        pieces = -(-n // chunk) if chunk else 1
+        size, longer = divmod(n, pieces)
+        r = pos - lo
+        if r < longer * (size + 1):                 # inside the longer pieces
+            return lo + (r // (size + 1) + 1) * (size + 1)
+        return lo + longer * (size + 1) + ((r - longer * (size + 1)) // size + 1) * size
+    return step
+
+
+def _budgeted_step(cap: int, budget: int, model: ChunkMemoryModel) -> Step:
+    return lambda pos, seg_end: pos + budgeted_chunk(pos, cap, budget, model)
 
 
 def budgeted_edges(end: int, cap: int, budget: int, model: ChunkMemoryModel,
-                   anchors: Sequence[int] = (), start: int = 0) -> List[int]:
-    """Internal edges of the budgeted plan over [start, end] (prefill.py:120-140)."""
-    wanted = sorted({int(a) for a in anchors if start < int(a) < end})
-    edges: List[int] = []
-    pos = int(start)
-    while pos < end:
-        stop = min(pos + budgeted_chunk(pos, cap, budget, model), end)
-        cut = next((a for a in wanted if pos < a < stop), None)
-        if cut is not None:
-            stop = cut
-        if stop < end:
-            edges.append(stop)
-        pos = stop
-    if edges and end - edges[-1] < MIN_CHUNK_TOKENS and edges[-1] not in wanted:
-        edges.pop()
-    return edges
+                   anchors: Sequence[int] = ()) -> List[int]:
+    """Cuts of the budgeted plan of a prompt ending at `end` (prefill.py:120-140)."""
+    return _walk(end, _budgeted_step(cap, budget, model), anchors, True)
 
 
 def balanced_edges(end: int, chunk: int, anchors: Sequence[int] = ()) -> List[int]:
-    """Internal edges of the balanced cold plan over [0, end]."""
-    points = [0] + sorted({int(a) for a in anchors if 0 < int(a) < end}) + [int(end)]
-    edges: List[int] = []
-    for lo, hi in zip(points, points[1:]):
-        n = hi - lo
-        pieces = -(-n // chunk) if chunk else 1
-        size, extra = divmod(n, pieces)
-        pos = lo
-        for i in range(pieces):
-            pos += size + (1 if i < extra else 0)
-            edges.append(pos)
-    return edges[:-1]
+    """Cuts of the balanced plan of a prompt ending at `end`."""
+    marks = sorted({int(a) for a in anchors if 0 < int(a) < end})
+
+    def segment_start(pos: int) -> int:
+        return max([0] + [a for a in marks if a <= pos])
+
+    return _walk(end, _balanced_step(chunk, segment_start), marks, False)
 
 
 def plan_chunks(total: int, chunk: int, boundaries: Sequence[int] = (), offset: int = 0,
@@ -129,62 +174,61 @@ def plan_chunks(total: int, chunk: int, boundaries: Sequence[int] = (), offset: 
                 budget: Optional[int] = None, model: Optional[ChunkMemoryModel] = None) -> List[Span]:
     """Spans [(start, end), ...] covering range(total) of a prompt whose first
     token sits at absolute position `offset` (tokens already in the cache).
-    The budgeted policy takes `budget` (bytes, at least MIN_BUDGET_BYTES) and
-    the memory `model`; its cap is `chunk`, or the largest candidate when 0."""
+    The grid policy cuts at `boundaries`; the other two at `anchors` (the
+    boundaries when none are given).  The budgeted policy takes `budget`
+    (bytes, at least MIN_BUDGET_BYTES) and the memory `model`; its cap is
+    `chunk`, or the largest candidate when 0."""
     total, chunk, offset = int(total), int(chunk), int(offset)
     if total < 0 or chunk < 0 or offset < 0:
         raise ValueError("negative prompt length, chunk size or offset")
     end = offset + total
-    if policy == "budgeted":
+    marks = boundaries if anchors is None else anchors
+    if policy == "grid":
+        cuts = _walk(end, _grid_step(chunk), boundaries, True)
+    elif policy == "balanced":
+        cuts = balanced_edges(end, chunk, marks)
+    elif policy == "budgeted":
         if budget is None or model is None:
             raise ValueError("the budgeted policy needs a budget and a memory model")
         if budget < MIN_BUDGET_BYTES:
             raise ValueError(f"chunk budget must be at least {MIN_BUDGET_BYTES} bytes")
-        cold = budgeted_edges(end, chunk or max(CANDIDATE_CHUNKS), int(budget), model,
-                              boundaries if anchors is None else anchors)
-        points = [0] + [e - offset for e in cold if offset < e < end] + [total]
-    elif policy == "balanced":
-        cold = balanced_edges(end, chunk, boundaries if anchors is None else anchors)
-        points = [0] + [e - offset for e in cold if offset < e < end] + [total]
-    elif policy == "grid":
-        edges = set(range((offset // chunk + 1) * chunk, end, chunk)) if chunk else set()
-        wanted = {int(b) for b in boundaries if offset < int(b) < end}
-        edges |= wanted
-        ordered = sorted(edges)
-        if ordered and end - ordered[-1] < MIN_CHUNK_TOKENS and ordered[-1] not in wanted:
-            ordered.pop()
-        points = [0] + [e - offset for e in ordered] + [total]
+        cuts = budgeted_edges(end, chunk or max(CANDIDATE_CHUNKS), int(budget), model, marks)
     else:
         raise ValueError(f"unknown chunk policy {policy!r} (grid, balanced or budgeted)")
-    return [(a, b) for a, b in zip(points, points[1:]) if b > a]
+    # the spans of this run: the cold plan's cuts after the cached prefix
+    points = [offset] + [c for c in cuts if offset < c < end] + [end]
+    return [(a - offset, b - offset) for a, b in zip(points, points[1:]) if b > a]
 
 
 def plan_windows(spans: Sequence[Span], offset: int, window: int, required: Sequence[int] = (),
                  anchors: Sequence[int] = ()) -> List[List[Span]]:
     """Group consecutive chunk spans into layer-major windows of at most
-    `window` tokens (a single larger chunk forms its own window)."""
+    `window` tokens; a single larger chunk forms its own window.  A window
+    ends at the first span end inside it that is a `required` position (a
+    point the caller must observe between layers); otherwise, unless it
+    already reaches the last span, at the last span end past its middle that
+    is an `anchor`, else at the last span end that fits."""
     spans = [(int(a), int(b)) for a, b in spans]
-    req = {int(p) for p in required}
-    anc = {int(p) for p in anchors}
-    out: List[List[Span]] = []
-    i = 0
-    while i < len(spans):
-        first = spans[i][0]
-        limit = first + int(window)
-        j = i
-        while j + 1 < len(spans) and spans[j + 1][1] <= limit:
-            j += 1
-        forced = [m for m in range(i, j + 1) if offset + spans[m][1] in req]
-        if forced:
-            j = forced[0]
-        elif j + 1 < len(spans):
-            half = first + int(window) // 2
-            nice = [m for m in range(i, j + 1) if offset + spans[m][1] in anc and spans[m][1] > half]
-            if nice:
-                j = nice[-1]
-        out.append(spans[i:j + 1])
-        i = j + 1
-    return out
+    ends = [b for _, b in spans]
+    must = [offset + b in set(int(p) for p in required) for b in ends]
+    nice = [offset + b in set(int(p) for p in anchors) for b in ends]
+    groups: List[List[Span]] = []
+    first = 0
+    while first < len(spans):
+        start = spans[first][0]
+        # the last span that still ends within the window (at least one span)
+        last = max(first, bisect.bisect_right(ends, start + int(window), first) - 1)
+        stop = next((m for m in range(first, last + 1) if must[m]), None)
+        if stop is None:
+            stop = last
+            if last + 1 < len(spans):
+                middle = start + int(window) // 2
+                preferred = [m for m in range(first, last + 1) if nice[m] and ends[m] > middle]
+                if preferred:
+                    stop = preferred[-1]
+        groups.append(spans[first:stop + 1])
+        first = stop + 1
+    return groups
 
 
 Layer = Callable[[torch.Tensor], torch.Tensor]
