@@ -101,7 +101,10 @@ typedef struct vx_moe_weights {
   const vx_moe_pool* pool;    /* may be NULL */
   /* Expert pipeline: VX_PATH_AUTO picks the grouped GEMV for decode-sized
    * batches and the tcgen05 grouped GEMM once the batch averages at least
-   * four routed positions per expert (T*top_k >= 4*num_experts). */
+   * four routed positions per expert (T*top_k >= 4*num_experts); under
+   * AUTO, vx_moe_block runs a batch of at most 4 tokens over a tiled pool as
+   * one cooperative launch (router to combine, VXMOE_DECODE=0 disables it).
+   * VX_PATH_GEMV / VX_PATH_GEMM force the multi-kernel pipelines. */
   int32_t expert_path;
   /* bf16 [E] added to the bf16 router logits before softmax/top-k (rounded
    * to bf16 again), or NULL.  The skewed-load benchmark configuration adds

@@ -397,10 +397,13 @@ def expert_mlp_qmm(x, gate: Q4Bank, up: Q4Bank, down: Q4Bank, group_size=GROUP_S
     return g, u, h, y
 
 
-def shared_parts(x, p: MoEParams):
+def shared_parts(x, p: MoEParams, path: str = "decode"):
     """``shared = shared_expert(x)``, ``sg = sigmoid(shared_expert_gate(x))``
-    in bf16 (``adaptive_topk.py:264-265``)."""
-    _, _, _, shared = expert_mlp_bf16(
+    in bf16 (``adaptive_topk.py:264-265``).  ``path="prefill"`` computes the
+    shared expert as the batched quantized matmul does (:func:`expert_mlp_qmm`);
+    the gate row is a single-row product either way."""
+    mlp = expert_mlp_qmm if path == "prefill" else expert_mlp_bf16
+    _, _, _, shared = mlp(
         x, p.shared_gate.expert(0), p.shared_up.expert(0), p.shared_down.expert(0),
         p.group_size)
     z = _proj_bf16(x, p.shared_expert_gate.expert(0), p.group_size)   # [T, 1]
@@ -408,9 +411,12 @@ def shared_parts(x, p: MoEParams):
     return shared, sg
 
 
-def routed_outputs(x, inds, p: MoEParams):
+def routed_outputs(x, inds, p: MoEParams, path: str = "decode"):
     """Per-(token, slot) bf16 down outputs [T, k, d], computing each distinct
-    expert once for all of its tokens (the sorted gather_qmm pass)."""
+    expert once for all of its tokens (the sorted gather_qmm pass).
+    ``path="prefill"`` uses the batched quantized matmul's arithmetic
+    (:func:`expert_mlp_qmm`), the decode default MLX's qmv formula."""
+    mlp = expert_mlp_qmm if path == "prefill" else expert_mlp_bf16
     x = f32(x)
     T, k = inds.shape
     out = np.zeros((T, k, p.hidden), dtype=np.float32)
@@ -419,8 +425,8 @@ def routed_outputs(x, inds, p: MoEParams):
     for e in np.unique(flat):
         pairs = np.nonzero(flat == e)[0]
         toks = pairs // k
-        _, _, h, y = expert_mlp_bf16(x[toks], p.gate.expert(e), p.up.expert(e),
-                                     p.down.expert(e), p.group_size)
+        _, _, h, y = mlp(x[toks], p.gate.expert(e), p.up.expert(e), p.down.expert(e),
+                         p.group_size)
         out.reshape(T * k, -1)[pairs] = y
         hs.reshape(T * k, -1)[pairs] = h
     return out, hs
@@ -462,18 +468,22 @@ class BlockOut:
     h: np.ndarray = field(repr=False, default=None)
 
 
-def moe_block(x, p: MoEParams, semantics: str = "fused", logits=None) -> BlockOut:
+def moe_block(x, p: MoEParams, semantics: str = "fused", logits=None,
+              path: str = "decode") -> BlockOut:
     """The routed sparse-MoE block ``_moe_call`` (``adaptive_topk.py:54-293``)
     at threshold 1.0 and blend 1.0.
 
     ``semantics="fused"`` is the custom-executor combine (float32); the
-    ``"generic"`` form is the bf16 combine of the MLX path.
+    ``"generic"`` form is the bf16 combine of the MLX path.  ``path`` picks the
+    expert arithmetic: ``"decode"`` (MLX's qmv, the custom executor's few-row
+    regime) or ``"prefill"`` (the sorted batched quantized matmul of
+    ``expert_cache.py:2017-2037``, bf16-dequantised tiles).
     """
     x = bf16_round(x)
     r = router(x, p.router_w, p.top_k, logits=logits)
-    shared, sg = shared_parts(x, p)
+    shared, sg = shared_parts(x, p, path)
     shared_y = bf16_round(sg * shared)
-    yd, h = routed_outputs(x, r.inds, p)
+    yd, h = routed_outputs(x, r.inds, p, path)
     if semantics == "fused":
         y = fused_combine(yd, r.weights, shared_y)
     elif semantics == "generic":
@@ -675,6 +685,27 @@ def max_rel_error(actual, ref, floor_frac: float = 0.05) -> float:
         return 0.0
     floor = floor_frac * float(np.sqrt(np.mean(r * r))) + 1e-30
     return float(np.max(np.abs(a - r) / np.maximum(np.abs(r), floor)))
+
+
+def summand_scale(yd, weights, shared_y=None) -> np.ndarray:
+    """Per-output magnitude of the terms a block output sums:
+    ``sum_s |w_s * y_s| + |shared_y|`` [T, d].  The rounding error of a sum
+    is bounded relative to this (not to the sum itself, which may cancel),
+    so it is the natural denominator floor of a max-relative-error check."""
+    s = np.abs(f32(yd).astype(np.float64) * f32(weights).astype(np.float64)[..., None]).sum(axis=-2)
+    if shared_y is not None:
+        s = s + np.abs(f32(shared_y).astype(np.float64))
+    return s
+
+
+def max_rel_error_floored(actual, ref, floor) -> float:
+    """max |a-r| / max(|r|, floor) with a per-element floor array."""
+    a = np.asarray(actual, dtype=np.float64)
+    r = np.asarray(ref, dtype=np.float64)
+    if r.size == 0:
+        return 0.0
+    den = np.maximum(np.abs(r), np.asarray(floor, dtype=np.float64)) + 1e-30
+    return float(np.max(np.abs(a - r) / den))
 
 
 def normwise_error(actual, ref) -> float:

@@ -62,3 +62,50 @@ def assert_bf16_close(actual, expected, max_ulp=1, min_exact=0.97, floor=2.0 ** 
     ok = (d <= max_ulp) | (np.abs(a - r) <= floor * scale)
     assert ok.all(), f"{what}: max ulp diff {d[~ok].max()} at |ref|={np.abs(r[~ok]).min():.3g} (rms {scale:.3g})"
     assert exact >= min_exact, f"{what}: only {exact:.4f} exact"
+
+
+def block_errors(got, oracle_y, ref64, scale):
+    """Errors of a block output against the bf16-semantics oracle and the
+    unrounded float64 reference.  max_rel_*: max |a-r| / max(|r|, scale),
+    the denominator floored per output by `scale`, the magnitude of the terms
+    the output sums (oracle.summand_scale: sum_s |w_s y_s| + |shared_y|) - an
+    output that cancels to near zero is measured against its summands;
+    max_rel_rms_*: the same with the floor at the output's rms (reported
+    only); normwise_*: max abs error over max |ref|; allclose_*: the
+    reference harness's allclose(atol=rtol=1e-2)
+    (models/flashnext/tests/bench/bench_runtime_layer.py:471-472)."""
+    got = np.asarray(got, dtype=np.float64)
+    out = {}
+    for name, ref in (("oracle", oracle_y), ("f64", ref64)):
+        ref = np.asarray(ref, dtype=np.float64)
+        out[f"max_rel_{name}"] = O.max_rel_error_floored(got, ref, scale)
+        out[f"max_rel_rms_{name}"] = O.max_rel_error(got, ref, 1.0)
+        out[f"normwise_{name}"] = O.normwise_error(got, ref)
+        out[f"allclose_{name}"] = bool(np.allclose(got, ref, atol=1e-2, rtol=1e-2))
+    ref64 = np.asarray(ref64, dtype=np.float64)
+    out["max_rel_oracle_own_f64"] = O.max_rel_error_floored(oracle_y, ref64, scale)
+    out["normwise_oracle_own_f64"] = O.normwise_error(oracle_y, ref64)
+    return out
+
+
+def assert_block_bar(got, oracle_y, ref64, scale, what):
+    """The block-output bar, printed and asserted:
+    * against the oracle (the reference's bf16 arithmetic restated): max
+      relative error <= 1e-2 with the summand-magnitude floor, and normwise
+      error < 1e-2;
+    * against the float64 reference: no worse than the reference's own bf16
+      arithmetic (the oracle) by more than 25 % + 2e-3, in both metrics - the
+      oracle itself sits at 1-3e-2 max relative error from exact math, so a
+      literal 1e-2 there would reject the reference's own arithmetic;
+    * allclose(atol=rtol=1e-2) against both, the reference harness's check."""
+    e = block_errors(got, oracle_y, ref64, scale)
+    print(f"[block bar] {what}: " + ", ".join(
+        f"{k}={v:.3e}" if isinstance(v, float) else f"{k}={v}" for k, v in e.items()))
+    assert e["max_rel_oracle"] <= 1e-2, f"{what}: floored max rel error vs oracle {e['max_rel_oracle']}"
+    assert e["normwise_oracle"] < 1e-2, f"{what}: normwise error vs oracle {e['normwise_oracle']}"
+    assert e["max_rel_f64"] <= 1.25 * e["max_rel_oracle_own_f64"] + 2e-3, \
+        f"{what}: max rel vs f64 {e['max_rel_f64']} (oracle's own {e['max_rel_oracle_own_f64']})"
+    assert e["normwise_f64"] <= 1.25 * e["normwise_oracle_own_f64"] + 2e-3, \
+        f"{what}: normwise vs f64 {e['normwise_f64']} (oracle's own {e['normwise_oracle_own_f64']})"
+    assert e["allclose_oracle"] and e["allclose_f64"], f"{what}: allclose(1e-2, 1e-2) failed"
+    return e

@@ -3,8 +3,11 @@
 Bar: bit-exact for nibble unpack, dequantised weights, the bf16 SwiGLU
 contract, top-k expert ids and the permutation; bf16 outputs of float
 accumulations within one bf16 ulp of the oracle (float32 vs float64 sums);
-block outputs within 1e-2 (normwise) of the oracle and no further from the
-unrounded float64 reference than the oracle's own bf16 semantics are.
+block outputs within 1e-2 of the oracle (max relative error with each
+output's denominator floored at the magnitude of the terms it sums; and
+normwise), no further from the unrounded float64 reference than the oracle's
+own bf16 semantics are, and allclose(atol=rtol=1e-2) against both
+(helpers.assert_block_bar).
 """
 from __future__ import annotations
 
@@ -15,8 +18,8 @@ import pytest
 import torch
 
 import vxmoe_oracle as O
-from helpers import (assert_bf16_close, bank_t, bf16_t, np32, u32_t, ulp_diff_bf16,
-                     weights_from_oracle)
+from helpers import (assert_block_bar, assert_bf16_close, bank_t, bf16_t, np32, u32_t,
+                     ulp_diff_bf16, weights_from_oracle)
 
 pytestmark = pytest.mark.gpu
 
@@ -367,21 +370,22 @@ def test_executor_against_reference_golden(golden_dir):
 
 
 def _block_check(p, x, what):
+    """The block against the oracle on the device's logits, with the oracle's
+    expert arithmetic matching the device path the batch takes (the tcgen05
+    GEMM's bf16-dequantised tiles once T*k >= 4E, MLX's qmv below)."""
     import vxmoe
     w = weights_from_oracle(p)
     y, inds, wts = vxmoe.moe_block(bf16_t(x), w, return_routing=True)
     logits = np32(vxmoe.router(bf16_t(x), w).logits)
-    out = O.moe_block(x, p, logits=logits)
+    path = "prefill" if x.shape[0] * p.top_k >= 4 * p.num_experts else "decode"
+    out = O.moe_block(x, p, logits=logits, path=path)
     np.testing.assert_array_equal(inds.cpu().numpy(), out.router.inds)
     got = np32(y)
-    err_oracle = O.normwise_error(got, out.y)
-    assert err_oracle < 1e-2, f"{what}: vs oracle {err_oracle}"
     ref = O.moe_block_reference_f64(x, p, out.router.inds, out.router.logits)
-    e_gpu = O.normwise_error(got, ref)
-    e_orc = O.normwise_error(out.y, ref)
+    scale = O.summand_scale(out.yd, out.router.weights, out.shared_y)
+    assert_block_bar(got, out.y, ref, scale, f"{what} ({path})")
     rms = np.linalg.norm(got - ref) / np.linalg.norm(ref)
     assert rms < 1e-2, f"{what}: rms vs float64 {rms}"
-    assert e_gpu <= 1.5 * e_orc + 2e-3, f"{what}: {e_gpu} vs oracle's own {e_orc}"
     return got, out
 
 

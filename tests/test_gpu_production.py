@@ -1,0 +1,193 @@
+"""Parity at the production shapes the benchmark runs (d=2048, 512 experts
+top-10 + shared, I=512, Q4 g32, the tiled resident pool of the bench):
+
+* C4 - one 2,048-token prefill through the tcgen05 pool GEMM;
+* C5 - an 8,192-token prefill with +2.0 on the router logits of 32 hot
+  experts (the skewed load of the 65,536-token configuration: thousands of
+  positions on each hot expert);
+* C3 - three distinct stacked layers (RMSNorm, block, residual) at decode
+  batch 1 and 16.
+
+Top-k ids (on the device's logits) and the token permutation are checked for
+every token, bit for bit.  Per-slot expert outputs and block outputs are
+checked on a fixed sample of tokens, against the oracle's restatement of the
+prefill path (bf16-dequantised tiles, exact sums, bf16 out) or the decode
+path (MLX's qmv formula), with the bar of helpers.assert_block_bar.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import vxmoe_oracle as O
+from helpers import (assert_bf16_close, assert_block_bar, bf16_t, np32, ulp_diff_bf16,
+                     weights_from_oracle)
+
+pytestmark = pytest.mark.gpu
+
+HOT = 32
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.fail("GPU tests need a CUDA device")
+    import vxmoe
+    vxmoe._lib.load()
+
+
+@pytest.fixture(scope="module")
+def prod():
+    """Production parameters (seed 0) and their device weights in the bench's
+    layout (MLX arrays plus the tiled pool)."""
+    p = O.make_params(seed=0)
+    w = weights_from_oracle(p).pack()
+    return p, w
+
+
+def _sample(T, n, seed):
+    return np.sort(np.random.default_rng(seed).choice(T, n, replace=False))
+
+
+def _prefill_refs(p, x, inds, weights, sg):
+    """Per-slot routed outputs [n, k, d] on the prefill path (bf16 tiles,
+    exact sums), the shared expert on the same path, and the fused combine
+    with the device's renormalised weights and shared gate."""
+    n, k = inds.shape
+    yd = np.zeros((n, k, p.hidden), np.float32)
+    for e in np.unique(inds):
+        tt, ss = np.nonzero(inds == e)
+        _, _, _, y = O.expert_mlp_qmm(x[tt], p.gate.expert(e), p.up.expert(e), p.down.expert(e))
+        yd[tt, ss] = y
+    _, _, _, shared = O.expert_mlp_qmm(x, p.shared_gate.expert(0), p.shared_up.expert(0),
+                                       p.shared_down.expert(0))
+    shared_y = O.bf16_round(sg * shared)
+    y = O.fused_combine(yd, weights, shared_y)
+    return yd, y, O.summand_scale(yd, weights, shared_y)
+
+
+def _f64_block(p, x, inds, logits):
+    return O.moe_block_reference_f64(x, p, inds, logits)
+
+
+def _check_prefill(p, w, x, what, bias=None, n_sample=48):
+    import vxmoe
+    T = x.shape[0]
+    xt = bf16_t(x)
+    if bias is not None:
+        w.router_bias = bf16_t(bias)
+    try:
+        y, inds, wts = vxmoe.moe_block(xt, w, return_routing=True)
+        r_dev = vxmoe.router(xt, w)
+        yd_dev = vxmoe.moe_experts(xt, inds, w)                     # per-slot [T, k, d]
+    finally:
+        w.router_bias = None
+    torch.cuda.synchronize()
+    assert T * p.top_k >= 4 * p.num_experts                           # the GEMM path
+    logits = np32(r_dev.logits)
+    r = O.router(x, p.router_w, p.top_k, logits=logits)               # biased logits as given
+    got_inds = inds.cpu().numpy()
+    np.testing.assert_array_equal(got_inds, r.inds)
+    # renormalised weights: float32 softmax sums in a different order than
+    # NumPy's, so a weight may round one bf16 ulp apart (as at decode sizes)
+    assert ulp_diff_bf16(np32(wts), r.weights).max() <= 2
+    # the token permutation of all T*k routes
+    perm = vxmoe.permute(inds, p.num_experts)
+    order, inverse, _, offsets = O.gather_sort(r.inds, p.num_experts)
+    np.testing.assert_array_equal(perm.order.cpu().numpy(), order)
+    np.testing.assert_array_equal(perm.inverse.cpu().numpy(), inverse)
+    np.testing.assert_array_equal(perm.offsets.cpu().numpy(), offsets)
+    assert int(perm.errors.item()) == 0
+    counts = np.diff(offsets)
+    # sampled tokens: per-slot outputs and the block output
+    s = _sample(T, n_sample, T)
+    sg = np32(r_dev.shared_gate)[s]
+    yd_ref, y_ref, scale = _prefill_refs(p, x[s], r.inds[s], np32(wts)[s], sg)
+    got_slots = np32(yd_dev)[s]
+    assert_bf16_close(got_slots, yd_ref, max_ulp=2, min_exact=0.9, floor=2.0 ** -7,
+                      what=f"{what}: per-slot outputs")
+    assert O.normwise_error(got_slots, yd_ref) < 4e-3
+    ref64 = _f64_block(p, x[s], r.inds[s], logits[s])
+    assert_block_bar(np32(y)[s], y_ref, ref64, scale, what)
+    return counts
+
+
+def test_c4_prefill_2048_production(prod):
+    """BASELINE config 4 on one GPU: 2,048 tokens, every expert active (about
+    40 positions each), the persistent tcgen05 kernel over the tiled pool."""
+    p, w = prod
+    x = O.make_x(404, 2048, p.hidden)
+    counts = _check_prefill(p, w, x, "C4 T=2048")
+    assert counts.sum() == 2048 * p.top_k and (counts > 0).all()
+
+
+def test_c5_skewed_prefill_production(prod):
+    """The skewed load of BASELINE config 5 at 8,192 tokens: +2.0 on the logits
+    of 32 hot experts (chosen with seed 0, as the bench does) puts most slots
+    on them - thousands of positions per hot expert, many items of the pool
+    kernel for each."""
+    p, w = prod
+    hot = np.random.default_rng(0).choice(p.num_experts, HOT, replace=False)
+    bias = np.zeros(p.num_experts, np.float32)
+    bias[hot] = 2.0
+    x = O.make_x(505, 8192, p.hidden)
+    counts = _check_prefill(p, w, x, "C5-shaped T=8192 skewed", bias=bias, n_sample=32)
+    assert counts[hot].sum() > 0.5 * counts.sum()
+    assert counts.max() > 1000                  # one expert carries > 1000 positions
+
+
+# ---------------------------------------------------------------- C3 stack
+
+LAYERS = 3
+
+
+@pytest.fixture(scope="module")
+def stack(prod):
+    """Three distinct layers: the production experts rolled by a per-layer
+    offset (each layer maps expert e to a different bank row), a fresh router
+    per layer, the shared expert of the production parameters."""
+    p0, _ = prod
+    layers = []
+    for i in range(LAYERS):
+        shift = 97 * i
+
+        def roll(b):
+            return O.Q4Bank(np.roll(b.w, shift, axis=0), np.roll(b.scales, shift, axis=0),
+                            np.roll(b.biases, shift, axis=0))
+
+        rng = np.random.default_rng(700 + i)
+        router_w = O.bf16_round(rng.normal(0.0, 0.02, size=p0.router_w.shape))
+        p = O.MoEParams(roll(p0.gate), roll(p0.up), roll(p0.down), router_w, p0.shared_gate,
+                        p0.shared_up, p0.shared_down, p0.shared_expert_gate, p0.top_k, p0.group_size)
+        layers.append((p, weights_from_oracle(p).pack()))
+    return layers
+
+
+@pytest.mark.parametrize("T", [1, 16])
+def test_c3_stack_three_production_layers(stack, T):
+    """BASELINE config 3's layer body, h <- h + MoE(RMSNorm(h)), through three
+    distinct production layers.  Each layer is checked on the device's own
+    input to it (so that a near-tie in one layer's routing cannot make the
+    chains diverge): RMSNorm within one bf16 ulp, top-k ids exact, the block
+    output at the block bar, and the residual add exact."""
+    import vxmoe
+    gain = O.bf16_round(np.ones(2048, np.float32))
+    gain_t = bf16_t(gain)
+    h = bf16_t(O.make_x(300 + T, T, 2048))
+    for li, (p, w) in enumerate(stack):
+        h_np = np32(h)
+        n = vxmoe.rms_norm(h, gain_t, 1e-6)
+        n_np = np32(n)
+        assert ulp_diff_bf16(n_np, O.rms_norm(h_np, gain, 1e-6)).max() <= 1
+        y, inds, _ = vxmoe.moe_block(n, w, return_routing=True)
+        logits = np32(vxmoe.router(n, w).logits)
+        out = O.moe_block(n_np, p, logits=logits)
+        np.testing.assert_array_equal(inds.cpu().numpy(), out.router.inds)
+        ref64 = O.moe_block_reference_f64(n_np, p, out.router.inds, out.router.logits)
+        scale = O.summand_scale(out.yd, out.router.weights, out.shared_y)
+        assert_block_bar(np32(y), out.y, ref64, scale, f"C3 layer {li} T={T}")
+        h_next = h + y
+        np.testing.assert_array_equal(O.bf16_bits(np32(h_next)),
+                                      O.bf16_bits(O.bf16_round(h_np + np32(y))))
+        h = h_next

@@ -51,17 +51,40 @@ def up_to_date():
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
+    """Compile every source to an object in parallel (one nvcc per file; no
+    device code crosses files), then link the shared library."""
     if not force and up_to_date():
         return LIB
     os.makedirs(LIBDIR, exist_ok=True)
-    tmp = LIB + ".tmp"
-    cmd = [nvcc_path(), *ARCH_FLAGS, *NVCC_FLAGS, "-I", INCLUDE, "-I", CSRC,
-           *sources(), "-o", tmp]
-    proc = subprocess.run(cmd, capture_output=True, text=True)
-    log = proc.stdout + proc.stderr
+    import concurrent.futures
+    import tempfile
+    nvcc = nvcc_path()
+    compile_flags = [f for f in NVCC_FLAGS if f != "-shared"]
+    logs = []
+    with tempfile.TemporaryDirectory(prefix="vxmoe_build_") as objdir:
+        def compile_one(src):
+            obj = os.path.join(objdir, os.path.basename(src) + ".o")
+            cmd = [nvcc, *ARCH_FLAGS, *compile_flags, "-I", INCLUDE, "-I", CSRC, "-c", src, "-o", obj]
+            proc = subprocess.run(cmd, capture_output=True, text=True)
+            return src, obj, cmd, proc
+        workers = max(1, min(len(sources()), os.cpu_count() or 1))
+        with concurrent.futures.ThreadPoolExecutor(workers) as pool:
+            results = list(pool.map(compile_one, sources()))
+        failed = False
+        for src, obj, cmd, proc in results:
+            logs.append(" ".join(cmd) + "\n" + proc.stdout + proc.stderr)
+            failed |= proc.returncode != 0
+        tmp = LIB + ".tmp"
+        if not failed:
+            cmd = [nvcc, *ARCH_FLAGS, "-shared", "-Xcompiler", "-fPIC", *[r[1] for r in results],
+                   "-o", tmp]
+            proc = subprocess.run(cmd, capture_output=True, text=True)
+            logs.append(" ".join(cmd) + "\n" + proc.stdout + proc.stderr)
+            failed = proc.returncode != 0
+    log = "\n".join(logs)
     with open(os.path.join(LIBDIR, "build.log"), "w") as fh:
-        fh.write(" ".join(cmd) + "\n" + log)
-    if proc.returncode != 0:
+        fh.write(log)
+    if failed:
         sys.stderr.write(log)
         raise RuntimeError("nvcc failed building libvxmoe.so")
     if verbose:

@@ -160,6 +160,49 @@ static ExpertPath expert_path(int T, const BlockDims& dm) {
   return dm.pool ? kPathGemvTiled : kPathGemvMlx;
 }
 
+// Whether a block call runs as the single cooperative decode launch
+// (vx_decode.cu): the tiled pool on the GEMV side, at most kDecodeMaxT
+// tokens, shapes the kernel covers.  VXMOE_DECODE=0 keeps the multi-kernel
+// pipeline (router, expert GEMVs, combine) for every batch.
+static bool decode_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* s = getenv("VXMOE_DECODE");
+    v = (s && strcmp(s, "0") == 0) ? 0 : 1;
+  }
+  return v == 1;
+}
+
+static bool use_decode(int T, const BlockDims& dm) {
+  // an explicit VX_PATH_GEMV / VX_PATH_GEMM (weights or VXMOE_EXPERT_PATH)
+  // selects the multi-kernel pipelines
+  if (dm.path != VX_PATH_AUTO || path_override() != 0) return false;
+  if (!dm.pool || !decode_enabled() || expert_path(T, dm) != kPathGemvTiled) return false;
+  if (dm.shared && dm.Is != dm.pool->shared_gate_up.out) return false;
+  return decode_supported(T, dm.E, dm.d, dm.k, dm.I, dm.shared ? dm.Is : 0, dm.pool->gate_up.tile_rows,
+                          dm.pool->down.tile_rows);
+}
+
+// Scratch of the decode launch: logits, sg, the SwiGLU outputs h and the
+// four words (error bits, dropped ids, two barrier counters) that one memset
+// clears.
+struct DecodeScratch {
+  uint16_t *logits, *sg, *h;
+  int32_t* words;
+  int ldh, Pp;
+};
+
+static DecodeScratch carve_decode(Carver& c, int T, const BlockDims& dm) {
+  DecodeScratch s;
+  s.Pp = T * dm.k + (dm.shared ? T : 0);
+  s.ldh = std::max(dm.I, dm.shared ? dm.Is : 0);
+  s.words = c.take<int32_t>(4);
+  s.logits = c.take<uint16_t>(int64_t(T) * dm.E);
+  s.sg = c.take<uint16_t>(T);
+  s.h = c.take<uint16_t>(int64_t(s.Pp) * s.ldh);
+  return s;
+}
+
 // extra_zeroed: ints placed right after s.err, so that one memset clears
 // both (the block call keeps the router's arrival counters there).
 static ExpertScratch carve_experts(Carver& c, int T, const BlockDims& dm, int extra_zeroed = 0) {
@@ -711,7 +754,13 @@ size_t vx_moe_block_workspace(int32_t T, const vx_moe_weights* W) {
   c.take<uint16_t>(int64_t(T) * dm.k);   // weights
   c.take<uint16_t>(T);                   // sg
   carve_experts(c, T, dm, int(router_counters(T)));   // err + router arrival counters
-  return c.size();
+  size_t bytes = c.size();
+  if (T <= kDecodeMaxT) {   // the decode launch's (smaller) scratch fits in the same bytes
+    Carver cd(nullptr);
+    carve_decode(cd, T, dm);
+    bytes = std::max(bytes, cd.size());
+  }
+  return bytes;
 }
 
 int vx_moe_block(const uint16_t* x, int32_t T, const vx_moe_weights* W, uint16_t* y, int32_t* inds,
@@ -722,6 +771,47 @@ int vx_moe_block(const uint16_t* x, int32_t T, const vx_moe_weights* W, uint16_t
   check_weights(W, true, &dm);
   if (!workspace || workspace_bytes < vx_moe_block_workspace(T, W)) return VX_EWORKSPACE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (use_decode(T, dm)) {
+    // decode-sized batch: the whole block in one cooperative launch
+    Carver cd(workspace);
+    DecodeScratch ds = carve_decode(cd, T, dm);
+    cudaError_t e = cudaMemsetAsync(ds.words, 0, 4 * sizeof(int32_t), st);
+    if (e != cudaSuccess) return vx_cuda_fail(e);
+    profile_mark(st, "");
+    const vx_moe_pool& pl = *dm.pool;
+    DecodeArgs a{};
+    a.x = x;
+    a.router_w = W->router_w;
+    a.router_bias = W->router_bias;
+    if (dm.shared) a.seg = W->shared_expert_gate;
+    a.gu_rec = static_cast<const unsigned char*>(pl.gate_up.records);
+    a.gu_stride = tile_pool_bytes(1, dm.I, dm.d, 2, pl.gate_up.tile_rows);
+    a.dn_rec = static_cast<const unsigned char*>(pl.down.records);
+    a.dn_stride = tile_pool_bytes(1, dm.d, dm.I, 1, pl.down.tile_rows);
+    a.gu_rec_s = dm.shared ? static_cast<const unsigned char*>(pl.shared_gate_up.records) : nullptr;
+    a.dn_rec_s = dm.shared ? static_cast<const unsigned char*>(pl.shared_down.records) : nullptr;
+    a.T = T;
+    a.E = dm.E;
+    a.d = dm.d;
+    a.k = dm.k;
+    a.I = dm.I;
+    a.Is = dm.shared ? dm.Is : 0;
+    a.dn_mt = pl.down.tile_rows / 16;
+    a.ldh = ds.ldh;
+    a.logits = ds.logits;
+    a.h = ds.h;
+    a.sg = ds.sg;
+    a.err = ds.words;
+    a.sync = reinterpret_cast<uint32_t*>(ds.words + 2);
+    a.y = y;
+    a.inds_out = inds;
+    a.w_out = weights;
+    a.wait_ns = 1000ull * 1000 * 1000;   // a grid barrier gives up after 1 s
+    e = launch_decode(a, st);
+    if (e != cudaSuccess) return vx_cuda_fail(e);
+    profile_mark(st, "decode");
+    return VX_OK;
+  }
   Carver c(workspace);
   uint16_t* logits = c.take<uint16_t>(int64_t(T) * dm.E);
   int32_t* inds_ws = c.take<int32_t>(int64_t(T) * dm.k);

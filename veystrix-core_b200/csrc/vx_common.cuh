@@ -7,6 +7,7 @@
 #include "vxmoe.h"
 
 #define VX_DEVICE __device__ __forceinline__
+#define VX_HOST_DEVICE __host__ __device__
 
 namespace vx {
 

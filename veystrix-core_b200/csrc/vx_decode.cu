@@ -1,0 +1,1010 @@
+// The whole MoE block for a few decode tokens in one cooperative launch
+// (sm_100a): router logits, softmax/top-k/renorm, the expert sort, the
+// routed and shared gate/up projections with SwiGLU, the down projections
+// and the score-weighted combine (models/flashnext/metal_runtime.py:799-974,
+// the reference's custom executor for <= 8 rows; adaptive_topk.py:54-293).
+//
+// Why one launch.  At one token the block moves about 24 MB (ten routed
+// experts, the shared expert, the router) - 3.6 us at full HBM speed - while
+// a chain of separate launches pays a launch gap and a pipeline fill per
+// kernel and leaves most SMs idle behind the router's serial tail.  Here
+// every SM runs one CTA for the whole block; the CTAs meet at two grid
+// barriers (bounded waits on global counters):
+//
+//   phase R   CTAs [0, L) compute the bf16 logits of 8 experts each (the
+//             fused router's mma.sync tile and K slicing, so the logits are
+//             the router kernel's bit for bit); the other CTAs start on the
+//             shared expert, whose gate/up projections need no routing.
+//   barrier 1
+//   phase G   every CTA reads all logits, runs the same top-k (one warp per
+//             token) and the same stable expert sort (one warp, bitonic over
+//             at most 64 routes), then takes a byte-balanced slice of the
+//             routed gate/up tasks (expert, 16-row tile); the 8 warps of a
+//             CTA split each task's 128-input chunks, the CTA adds their
+//             partial sums in warp order and applies the bf16 SwiGLU; h goes
+//             to global.  Down-projection weights stream into shared memory
+//             meanwhile.
+//   barrier 2
+//   phase D   CTA c >= G - n_tiles owns one row tile of the down projection
+//             for every expert of the step: it builds the h records of all
+//             positions, runs its down tiles from shared memory and combines
+//             its rows of y in slot order (float32, no FMA, then the shared
+//             part) - the combine needs no third barrier.
+//
+// Weights come from the tiled resident pool (vx_q4_tile), one record per
+// (expert, row tile, 128-input chunk): 2,560 bytes for a gate/up pair of 16
+// rows, 1,280 or 2,560 bytes for 16 or 32 down rows.  A warp copies a record
+// into a stage of its ring with per-lane 16-byte cp.async (the load/store
+// path; small bulk copies cost more per byte) that arrive on the stage's
+// mbarrier.  The arithmetic of a record is the tiled GEMV's (vx_gemv_tiled.cu):
+// nibbles to bf16 128+q by one lop3, a block-diagonal B operand on mma.sync
+// so each MMA yields per-group sums, and MLX's qmv formula
+// scale*sum(qx) + bias*sum(x) per group in float32.
+//
+// No cluster multicast; every copy lands in the issuing CTA's own shared
+// memory.  Every wait is bounded: a grid barrier gives up after wait_ns
+// (error bit 0x400), an mbarrier after kSpinLimit polls (0x100); the kernel
+// then waits (bounded) for its own copies in flight and returns.
+#include <type_traits>
+
+#include "vx_async.cuh"
+#include "vx_common.cuh"
+#include "vx_launch.h"
+#include "vx_topk.cuh"
+
+namespace vx {
+
+constexpr int kDecThreads = 512;
+constexpr int kDecWarps = kDecThreads / 32;
+constexpr int kDecStage = 2560;         // one pool record (largest: gate/up pair, 32 down rows)
+constexpr int kDecLogitRows = 4;        // experts per logit CTA
+constexpr int kDecMaxRoutes = 64;       // T*k for the one-warp sort
+// gate/up partial sums: [task][warp][projection][row 16][token T] float in a
+// region of kDecPartBytes, so a batch holds kDecPartBytes / (1 KB * T) tasks
+constexpr int kDecPartBytes = 16384;
+
+// ---------------------------------------------------------------------------
+// Shared-memory layout (the host computes the same numbers to size the launch)
+// ---------------------------------------------------------------------------
+
+struct DecLayout {
+  int nch_d, nch_h, Pp, tile_rows, nch_s;
+  int off_x, off_h, off_y, off_sd, off_part, off_tab, off_bar, off_ring;
+  int ring_stages, total;
+};
+
+VX_HOST_DEVICE inline int dec_align(int v, int a) { return (v + a - 1) / a * a; }
+
+VX_HOST_DEVICE inline DecLayout dec_layout(int T, int d, int k, int I, int Is, int dn_mt, int smem_cap) {
+  DecLayout L;
+  L.nch_d = d / 128;
+  L.nch_h = (I > Is ? I : Is) / 128;
+  L.nch_s = Is / 128;
+  L.Pp = T * k + (Is > 0 ? T : 0);
+  L.tile_rows = 16;                                     // rows of y a down owner computes
+  int off = 0;
+  L.off_x = off;                                        // x records [nch_d][T][320]
+  off += dec_align(L.nch_d * T * kActRecord, 128);
+  L.off_h = off;                                        // h records [nch_h][Pp][320]
+  int hbytes = L.nch_h * L.Pp * kActRecord;
+  const int logit_scratch = kDecWarps * 32 * 4 * 4;     // phase R: router K-slice partials
+  if (hbytes < logit_scratch) hbytes = logit_scratch;
+  off += dec_align(hbytes, 128);
+  L.off_y = off;                                        // down outputs [Pp][tile_rows] bf16
+  off += dec_align(L.Pp * L.tile_rows * 2, 128);
+  L.off_sd = off;                                       // the shared expert's down records
+  off += (Is > 0 ? L.nch_s * 1280 : 0);
+  L.off_part = off;                                     // gate/up partial sums
+  off += kDecPartBytes;
+  L.off_tab = off;                                      // routing tables
+  off += dec_align(kDecMaxRoutes * 4 * 2 + kDecMaxRoutes * 2 + (kDecMaxRoutes + 16) * 4 +
+                       (kDecMaxRoutes + 2) * 4 * 3 + 64 * 4,
+                   128);
+  L.off_bar = off;                                      // ring mbarriers + the shared-down one
+  const int avail = smem_cap - off;
+  int stages = (avail - 256) / (kDecStage + 8);
+  stages = stages / kDecWarps * kDecWarps;
+  L.ring_stages = stages;
+  off += dec_align((stages + 1) * 8, 128);
+  L.off_ring = off;
+  off += stages * kDecStage;
+  L.total = off;
+  return L;
+}
+
+// Routing tables inside off_tab.
+struct DecTab {
+  int32_t* inds;      // [T*k] routed expert ids (flat t*k+s)
+  int32_t* posof;     // [T*k] sorted position of flat index (-1: dropped)
+  uint16_t* wts;      // [T*k] renormalised weights (bf16 bits)
+  int32_t* tok;       // [Pp] token of each sorted position
+  int32_t* ex;        // [U+1] expert of slot u (E: the shared expert)
+  int32_t* p0;        // [U+1] first position of slot u
+  int32_t* cnt;       // [U+1] positions of slot u
+  int32_t* plan;      // U, first task, tasks, abort flag
+};
+
+VX_DEVICE DecTab dec_tab(unsigned char* base) {
+  DecTab t;
+  t.inds = reinterpret_cast<int32_t*>(base);
+  t.posof = t.inds + kDecMaxRoutes;
+  t.wts = reinterpret_cast<uint16_t*>(t.posof + kDecMaxRoutes);
+  t.tok = reinterpret_cast<int32_t*>(t.wts + kDecMaxRoutes);
+  t.ex = t.tok + kDecMaxRoutes + 16;
+  t.p0 = t.ex + kDecMaxRoutes + 2;
+  t.cnt = t.p0 + kDecMaxRoutes + 2;
+  t.plan = t.cnt + kDecMaxRoutes + 2;
+  return t;
+}
+
+enum { kPlanU = 0, kPlanFirst = 1, kPlanNr = 2, kPlanAbort = 3 };
+
+// ---------------------------------------------------------------------------
+// grid barrier: arrive (release) and bounded wait (acquire) on a counter that
+// is zero at launch
+// ---------------------------------------------------------------------------
+
+VX_DEVICE uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+VX_DEVICE void grid_arrive(uint32_t* ctr) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
+}
+
+VX_DEVICE bool grid_wait(const uint32_t* ctr, uint32_t target, uint64_t limit_ns) {
+  const uint64_t t0 = gtimer();
+  for (uint32_t i = 0; i < (1u << 26); ++i) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+    if (v >= target) return true;
+    if ((i & 15u) == 15u && gtimer() - t0 > limit_ns) return false;
+  }
+  return false;
+}
+
+// ---------------------------------------------------------------------------
+// activation records (B operand of the record MMAs): one thread per 8-input
+// block, the four blocks of a quant group on adjacent lanes; the group sum is
+// left-to-right over 8 inputs, then (s0+s1)+(s2+s3), as act_records_kernel.
+// ---------------------------------------------------------------------------
+
+VX_DEVICE void put_record_block(unsigned char* rec, int blk, uint4 v, bool live) {
+  float s = 0.f;
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    s += __uint_as_float(w[j] << 16);
+    s += __uint_as_float(w[j] & 0xFFFF0000u);
+  }
+  s += __shfl_xor_sync(0xFFFFFFFFu, s, 1);
+  s += __shfl_xor_sync(0xFFFFFFFFu, s, 2);
+  if (!live) return;
+  const int c = (blk >> 2) & 3, ib = blk & 3;
+  uint4 o;
+  o.x = prmt(v.x, v.z, 0x5410);
+  o.y = prmt(v.x, v.z, 0x7632);
+  o.z = prmt(v.y, v.w, 0x5410);
+  o.w = prmt(v.y, v.w, 0x7632);
+  *reinterpret_cast<uint4*>(rec + (ib * 4 + c) * 16) = o;
+  if (ib == 0) *reinterpret_cast<float*>(rec + kActXsum + c * 4) = s;
+}
+
+// ---------------------------------------------------------------------------
+// one record on the tensor pipe: NM 16-row blocks (gate and up of a pair, or
+// the m-tiles of a down record) against NQ B operands of two tokens each
+// ---------------------------------------------------------------------------
+
+template <int NQ, int NM>
+VX_DEVICE void rec_mma(uint32_t st, uint32_t brec, const uint32_t (&tokoff)[4], int cnt, uint32_t zaddr,
+                       float (&acc)[NM][2][2]) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+  const bool blane = (g & 3) == c;
+  const int tb = g >> 2, ts = c >> 1;
+  uint32_t bq[NQ][16];
+  float xs[NQ][2];
+#pragma unroll
+  for (int q = 0; q < NQ; ++q) {
+    const int jb = 2 * q + tb, js = 2 * q + ts;
+    const bool live = blane && jb < cnt;
+    const uint32_t base = live ? brec + tokoff[jb] + c * 16 : zaddr;
+    const uint32_t step = live ? 64 : 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 v = lds128(base + i * step);
+      bq[q][4 * i + 0] = v.x;
+      bq[q][4 * i + 1] = v.y;
+      bq[q][4 * i + 2] = v.z;
+      bq[q][4 * i + 3] = v.w;
+    }
+    const uint2 v = lds64(js < cnt ? brec + tokoff[js] + kActXsum + (c & 1) * 8 : zaddr);
+    xs[q][0] = __uint_as_float(v.x);
+    xs[q][1] = __uint_as_float(v.y);
+  }
+#pragma unroll
+  for (int pm = 0; pm < NM; ++pm) {
+    const uint32_t wrow = st + pm * 1024 + lane * 16;
+    const uint4 wg = lds128(wrow), w8 = lds128(wrow + 512);
+    const uint32_t ag[4] = {wg.x, wg.y, wg.z, wg.w};
+    const uint32_t a8[4] = {w8.x, w8.y, w8.z, w8.w};
+    // two independent accumulator chains (low and high nibble pairs), added
+    // at the end: half the dependent MMA latency of one chain
+    float d[NQ][4], e[NQ][4];
+#pragma unroll
+    for (int q = 0; q < NQ; ++q)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) d[q][i] = e[q][i] = 0.f;
+#pragma unroll
+    for (int mm = 0; mm < 8; mm += 2) {
+      const int wi = mm >> 1;
+      const uint32_t f0 = nib_pair128(ag[wi]), f1 = nib_pair128(a8[wi]);
+      const uint32_t f2 = nib_pair128(ag[wi] >> 4), f3 = nib_pair128(a8[wi] >> 4);
+      const uint32_t h0 = nib_pair128(ag[wi] >> 8), h1 = nib_pair128(a8[wi] >> 8);
+      const uint32_t h2 = nib_pair128(ag[wi] >> 12), h3 = nib_pair128(a8[wi] >> 12);
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) {
+        mma16816(d[q], f0, f1, f2, f3, bq[q][2 * mm], bq[q][2 * mm + 1]);
+        mma16816(e[q], h0, h1, h2, h3, bq[q][2 * mm + 2], bq[q][2 * mm + 3]);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < NQ; ++q)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) d[q][i] += e[q][i];
+    const uint4 sb = lds128(st + NM * 1024 + pm * 256 + (g * 2 + (c & 1)) * 16);
+    const uint32_t sw[4] = {sb.x, sb.y, sb.z, sb.w};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float s0 = __uint_as_float(sw[2 * h] << 16);
+      const float s1 = __uint_as_float(sw[2 * h] & 0xFFFF0000u);
+      const float b0 = __uint_as_float(sw[2 * h + 1] << 16);
+      const float b1 = __uint_as_float(sw[2 * h + 1] & 0xFFFF0000u);
+      const float c0 = fmaf(-128.f, s0, b0);   // the lop3 operands carry q + 128
+      const float c1 = fmaf(-128.f, s1, b1);
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) {
+        float v = acc[pm][q][h];
+        v = fmaf(s0, d[q][2 * h], v);
+        v = fmaf(c0, xs[q][0], v);
+        v = fmaf(s1, d[q][2 * h + 1], v);
+        v = fmaf(c1, xs[q][1], v);
+        acc[pm][q][h] = v;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// per-warp stream of records: [shared gate/up chunks][routed gate/up chunks]
+// [routed down records], each warp taking chunks ch = w, w + 8, ... of every
+// gate/up task and the down jobs (experts) dj = w, w + 8, ...
+// ---------------------------------------------------------------------------
+
+struct DecPlan {
+  int T, k, E, d, G, L, n_dt;   // n_dt: 16-row tiles of y, one per down owner
+  int P, nch_d, nch_i, rbg, dn_mt;
+  int ns;              // shared gate/up tasks of this CTA
+  int U, first, nr;    // routed: distinct experts, first task, tasks of this CTA (after routing)
+  int td;              // 16-row tile of y this CTA owns, or -1
+  bool routed;         // routing known
+};
+
+struct GuTask {
+  int u, rb;           // slot (-1: the shared expert), 16-row tile
+};
+
+VX_DEVICE GuTask shared_task(const DecPlan& pl, int j) {
+  // the CTA's j-th shared task: global shared task id (c - L) + j*(G - L)
+  const int span = pl.G - pl.L;
+  return {-1, int(blockIdx.x) - pl.L + j * span};
+}
+
+VX_DEVICE GuTask routed_task(const DecPlan& pl, int j) {
+  const int r = pl.first + j;
+  const int u = r / pl.rbg;
+  return {u, r - u * pl.rbg};
+}
+
+struct DecCursor {
+  int ph;   // 0 shared gate/up, 1 routed gate/up, 2 routed down, 3 end
+  int j;    // task / job index within the phase
+  int ch;   // chunk
+};
+
+// First valid record at or after the cursor; false when the stream is
+// exhausted or its next phase needs the routing that is not known yet.
+VX_DEVICE bool dec_seek(const DecPlan& pl, int warp, DecCursor& cu) {
+  for (;;) {
+    if (cu.ph == 0) {
+      if (cu.j < pl.ns && cu.ch < pl.nch_d) return true;
+      if (cu.j < pl.ns) {
+        ++cu.j;
+        cu.ch = warp;
+        continue;
+      }
+      cu.ph = 1;
+      cu.j = 0;
+      cu.ch = warp;
+    }
+    if (cu.ph == 1) {
+      if (!pl.routed) return false;
+      if (cu.j < pl.nr && cu.ch < pl.nch_d) return true;
+      if (cu.j < pl.nr) {
+        ++cu.j;
+        cu.ch = warp;
+        continue;
+      }
+      cu.ph = 2;
+      cu.j = warp;
+      cu.ch = 0;
+    }
+    if (cu.ph == 2) {
+      if (pl.td >= 0 && cu.j < pl.U) {
+        if (cu.ch < pl.nch_i) return true;
+        cu.j += kDecWarps;
+        cu.ch = 0;
+        continue;
+      }
+      cu.ph = 3;
+    }
+    return false;
+  }
+}
+
+VX_DEVICE void dec_advance(DecCursor& cu) {
+  if (cu.ph == 2)
+    ++cu.ch;
+  else
+    cu.ch += kDecWarps;
+}
+
+// Per-warp ring state.
+struct DecRing {
+  uint32_t base, bar0;   // first stage / mbarrier of this warp
+  int R;                 // stages
+  int issued, used;      // records issued / consumed
+  DecCursor cur;         // next record to issue
+  bool timed_out;
+};
+
+// Issues records into free stages: every lane copies its 16-byte pieces with
+// cp.async and arrives on the stage's mbarrier (count 32) once they land.
+VX_DEVICE void ring_fill(const DecodeArgs& a, const DecPlan& pl, const DecTab& tb, DecRing& rg, int warp,
+                         uint64_t pol) {
+  const int lane = threadIdx.x & 31;
+  while (rg.issued - rg.used < rg.R && dec_seek(pl, warp, rg.cur)) {
+    const int s = rg.issued % rg.R;
+    const uint32_t dst = rg.base + s * kDecStage;
+    if (rg.cur.ph <= 1) {
+      // a whole gate/up record: both projections of a 16-row tile
+      const GuTask t = rg.cur.ph == 0 ? shared_task(pl, rg.cur.j) : routed_task(pl, rg.cur.j);
+      const unsigned char* rec = t.u < 0 ? a.gu_rec_s : a.gu_rec + int64_t(tb.ex[t.u]) * a.gu_stride;
+      const unsigned char* src = rec + (int64_t(t.rb) * pl.nch_d + rg.cur.ch) * 2560;
+      for (int off = lane * 16; off < 2560; off += 512)
+        asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(dst + off),
+                     "l"(src + off), "l"(pol)
+                     : "memory");
+    } else {
+      // the 16 owned rows of a down record (record tile td / dn_mt, m-tile
+      // td % dn_mt): their packed words, then their scales and biases
+      const int m = pl.td % pl.dn_mt;
+      const unsigned char* rec = a.dn_rec + int64_t(tb.ex[rg.cur.j]) * a.dn_stride +
+                                 (int64_t(pl.td / pl.dn_mt) * pl.nch_i + rg.cur.ch) * (pl.dn_mt * 1280);
+      for (int off = lane * 16; off < 1280; off += 512) {
+        const unsigned char* src = off < 1024 ? rec + m * 1024 + off : rec + pl.dn_mt * 1024 + m * 256 + (off - 1024);
+        asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(dst + off),
+                     "l"(src), "l"(pol)
+                     : "memory");
+      }
+    }
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(rg.bar0 + 8 * s) : "memory");
+    ++rg.issued;
+    dec_advance(rg.cur);
+  }
+}
+
+// Waits for the next record in the ring and returns its stage address.
+VX_DEVICE uint32_t ring_take(DecRing& rg) {
+  const int s = rg.used % rg.R;
+  const uint32_t parity = uint32_t(rg.used / rg.R) & 1u;
+  if (!mbar_wait(rg.bar0 + 8 * s, parity)) rg.timed_out = true;
+  return rg.base + s * kDecStage;
+}
+
+VX_DEVICE void ring_release(DecRing& rg) {
+  __syncwarp();   // every lane has read the stage before any lane refills it
+  ++rg.used;
+}
+
+// Before an early return: wait (bounded) for this warp's copies in flight.
+VX_DEVICE void ring_drain(DecRing& rg) {
+  while (rg.used < rg.issued) {
+    ring_take(rg);
+    ring_release(rg);
+  }
+}
+
+VX_DEVICE void mbar_init_count(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------
+
+template <int PER, int DNMT>
+__global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const __grid_constant__ DecodeArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ __align__(16) uint32_t zero16[4];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int T = a.T, k = a.k, E = a.E, d = a.d;
+  const int G = gridDim.x;
+  const DecLayout lay = dec_layout(T, d, k, a.I, a.Is, DNMT, a.smem_bytes);
+  DecTab tb = dec_tab(smem + lay.off_tab);
+  const uint32_t zaddr = smem_u32(zero16);
+  const uint64_t pol = policy_evict_first();
+
+  DecPlan pl;
+  pl.T = T;
+  pl.k = k;
+  pl.E = E;
+  pl.d = d;
+  pl.G = G;
+  pl.L = (E + kDecLogitRows - 1) / kDecLogitRows;
+  pl.n_dt = (d + 15) / 16;
+  pl.P = T * k;
+  pl.nch_d = lay.nch_d;
+  pl.nch_i = a.I / 128;
+  pl.rbg = a.I / 16;
+  pl.dn_mt = DNMT;
+  const int ns_total = a.Is / 16;   // shared gate/up tasks (16-row tiles)
+  {
+    const int base = int(blockIdx.x) - pl.L, span = G - pl.L;
+    pl.ns = (base < 0 || base >= ns_total) ? 0 : (ns_total - base + span - 1) / span;
+  }
+  pl.U = 0;
+  pl.first = 0;
+  pl.nr = 0;
+  pl.td = int(blockIdx.x) >= G - pl.n_dt ? int(blockIdx.x) - (G - pl.n_dt) : -1;
+  pl.routed = false;
+  const bool logit_cta = int(blockIdx.x) < pl.L;
+
+  if (threadIdx.x < 4) zero16[threadIdx.x] = 0u;
+  // ---- ring set-up: R stages per warp, one mbarrier (32 arrivals) each
+  DecRing rg;
+  rg.R = lay.ring_stages / kDecWarps;
+  rg.base = smem_u32(smem + lay.off_ring) + warp * rg.R * kDecStage;
+  rg.bar0 = smem_u32(smem + lay.off_bar) + warp * rg.R * 8;
+  rg.issued = rg.used = 0;
+  rg.cur = {0, 0, warp};
+  rg.timed_out = false;
+  if (lane == 0)
+    for (int s = 0; s < rg.R; ++s) mbar_init_count(rg.bar0 + 8 * s, 32);
+  const uint32_t sd_bar = smem_u32(smem + lay.off_bar) + lay.ring_stages * 8;
+  const bool sd_owner = pl.td >= 0 && a.Is > 0;
+  if (threadIdx.x == 0) {
+    tb.plan[kPlanAbort] = 0;
+    if (sd_owner) mbar_init(sd_bar);
+  }
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  __syncthreads();
+
+  // ---- routing-independent copies: shared gate/up records, and the shared
+  // expert's down records of a down owner (their own region, bulk copies)
+  ring_fill(a, pl, tb, rg, warp, pol);
+  if (sd_owner && threadIdx.x == 0) {
+    // the shared expert's owned rows, one 1,280-byte unit per chunk
+    const int m = pl.td % DNMT;
+    mbar_expect(sd_bar, uint32_t(lay.nch_s * 1280));
+    for (int ch = 0; ch < lay.nch_s; ++ch) {
+      const unsigned char* rec = a.dn_rec_s + (int64_t(pl.td / DNMT) * lay.nch_s + ch) * (DNMT * 1280);
+      const uint32_t dst = smem_u32(smem + lay.off_sd) + ch * 1280;
+      bulk_load(dst, rec + m * 1024, 1024, sd_bar, pol);
+      bulk_load(dst + 1024, rec + DNMT * 1024 + m * 256, 256, sd_bar, pol);
+    }
+  }
+
+  // ---- x activation records (every CTA, all tokens)
+  {
+    const int n = T * pl.nch_d * 16;   // whole warps run the loop (shuffles inside)
+    for (int i = threadIdx.x; i < ((n + 31) & ~31); i += kDecThreads) {
+      const bool live = i < n;
+      const int t = live ? i / (pl.nch_d * 16) : 0, r = live ? i - t * pl.nch_d * 16 : 0;
+      const int ch = r >> 4, blk = r & 15;
+      const uint4 v = live ? *reinterpret_cast<const uint4*>(a.x + int64_t(t) * d + ch * 128 + blk * 8)
+                           : make_uint4(0, 0, 0, 0);
+      put_record_block(smem + lay.off_x + (ch * T + t) * kActRecord, blk, v, live);
+    }
+  }
+
+  // ---- phase R: logits (CTAs [0, L)), shared gate (CTA L)
+  if (logit_cta) {
+    // the fused router's 16 x 8 tile with rows g < 4 only (the other rows
+    // zero; an MMA output element depends on its own row alone): the same K
+    // slices per warp (of the router's 8) and the same slice-order
+    // reduction, so each logit equals router_fused_kernel's
+    float* red = reinterpret_cast<float*>(smem + lay.off_h);   // [warps][32][4]
+    const int g = lane >> 2, c = lane & 3;
+    const int ea = int(blockIdx.x) * kDecLogitRows + g, tx = g;
+    const bool row_live = g < kDecLogitRows && ea < E;
+    const uint16_t* ra = a.router_w + int64_t(row_live ? ea : 0) * d;
+    const uint16_t* rx = a.x + int64_t(tx < T ? tx : 0) * d;
+    constexpr int kSlices = 8;   // the fused router's K slices (one per warp there)
+    const int steps = d / 32;
+    const int per = (steps + kSlices - 1) / kSlices;
+    const int s0 = warp < kSlices ? warp * per : steps, s1 = min(steps, s0 + per);
+    float dd[4] = {0.f, 0.f, 0.f, 0.f};
+    constexpr int kBatch = 8;
+    const uint4 zero = make_uint4(0, 0, 0, 0);
+    for (int sb = s0; sb < s1; sb += kBatch) {
+      uint4 wa[kBatch], xb[kBatch];
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i) {
+        const int s = sb + i;
+        const int kk = s * 32 + c * 8;
+        wa[i] = (s < s1 && row_live) ? ldg_nc(ra + kk) : zero;
+        xb[i] = (s < s1 && tx < T) ? __ldg(reinterpret_cast<const uint4*>(rx + kk)) : zero;
+      }
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i) {
+        if (sb + i < s1) {
+          mma16816(dd, wa[i].x, 0u, wa[i].y, 0u, xb[i].x, xb[i].y);
+          mma16816(dd, wa[i].z, 0u, wa[i].w, 0u, xb[i].z, xb[i].w);
+        }
+      }
+    }
+    if (warp < kSlices)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) red[(warp * 32 + lane) * 4 + i] = dd[i];
+    __syncthreads();
+    if (warp == 0) {
+      float v[2] = {0.f, 0.f};
+      for (int w = 0; w < kSlices; ++w)
+#pragma unroll
+        for (int i = 0; i < 2; ++i) v[i] += red[(w * 32 + lane) * 4 + i];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int t = 2 * c + i;
+        if (row_live && t < T) {
+          float l = bf16r(v[i]);
+          if (a.router_bias) l = bf16r(__fadd_rn(l, bf16_to_f32(a.router_bias[ea])));
+          a.logits[int64_t(t) * E + ea] = f32_to_bf16(l);
+        }
+      }
+    }
+  } else if (int(blockIdx.x) == pl.L && a.seg.w) {
+    // sigmoid(shared_expert_gate(x)): warp t -> token t (the router's code)
+    const int t = warp;
+    if (t < T) {
+      const int Gq = d / 32;
+      const uint16_t* xr = a.x + int64_t(t) * d;
+      float acc = 0.f;
+      for (int gq = lane; gq < Gq; gq += 32) {
+        const uint4 w = __ldg(reinterpret_cast<const uint4*>(a.seg.w) + gq);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        float q = 0.f, xs = 0.f;
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          const uint4 xv = __ldg(reinterpret_cast<const uint4*>(xr + gq * 32 + cc * 8));
+          const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+          for (int n = 0; n < 8; ++n) {
+            const float v = __uint_as_float((n & 1) ? (xw[n >> 1] & 0xFFFF0000u) : (xw[n >> 1] << 16));
+            q = fmaf(float(nibble(ws[cc], n)), v, q);
+            xs += v;
+          }
+        }
+        acc += fmaf(bf16_to_f32(a.seg.scales[gq]), q, bf16_to_f32(a.seg.biases[gq]) * xs);
+      }
+      acc = warp_sum<32>(acc);
+      if (lane == 0) a.sg[t] = f32_to_bf16(sigmoid_bf16(bf16r(acc)));
+    }
+  }
+  if (threadIdx.x < T) tb.tok[pl.P + threadIdx.x] = threadIdx.x;   // shared positions P + t
+  __syncthreads();   // logits / sg stored; x records built
+  if (threadIdx.x == 0) grid_arrive(a.sync + 0);
+
+  float* part = reinterpret_cast<float*>(smem + lay.off_part);
+
+  // Runs `n` gate/up tasks (phase ph) in batches of `batch`: every warp
+  // its chunks of each task into its partial sums, then the CTA adds the
+  // warps' partials in warp order, rounds g and u to bf16, applies the bf16
+  // SwiGLU and stores h to global.
+  const int pw_floats = 2 * 16 * T;                         // one (task, warp)
+  const int batch = kDecPartBytes / (kDecWarps * pw_floats * 4);
+  auto run_gu = [&](int ph, int n) {
+    for (int b0 = 0; b0 < n; b0 += batch) {
+      const int nb = min(batch, n - b0);
+      for (int jb = 0; jb < nb; ++jb) {
+        const GuTask t = ph == 0 ? shared_task(pl, b0 + jb) : routed_task(pl, b0 + jb);
+        const int p0 = t.u < 0 ? pl.P : tb.p0[t.u];
+        const int cnt = t.u < 0 ? T : tb.cnt[t.u];
+        uint32_t tokoff[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) tokoff[q] = q < cnt ? uint32_t(tb.tok[p0 + q]) * kActRecord : 0u;
+        float acc[2][2][2] = {};
+        for (int ch = warp; ch < pl.nch_d; ch += kDecWarps) {
+          if (rg.issued - rg.used < rg.R && rg.cur.ph != 3) ring_fill(a, pl, tb, rg, warp, pol);
+          const uint32_t st = ring_take(rg);
+          const uint32_t brec = smem_u32(smem + lay.off_x) + ch * T * kActRecord;
+          if (cnt > 2)
+            rec_mma<2, 2>(st, brec, tokoff, cnt, zaddr, acc);
+          else
+            rec_mma<1, 2>(st, brec, tokoff, cnt, zaddr, acc);
+          ring_release(rg);
+        }
+        float* pw = part + (jb * kDecWarps + warp) * pw_floats;
+#pragma unroll
+        for (int p = 0; p < 2; ++p)
+#pragma unroll
+          for (int q = 0; q < 2; ++q)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const float v = acc[p][q][h] + __shfl_xor_sync(0xFFFFFFFFu, acc[p][q][h], 1);
+              const int j = 2 * q + ((lane & 3) >> 1);
+              if ((lane & 1) == 0 && j < cnt) pw[(p * 16 + (lane >> 2) + 8 * h) * T + j] = v;
+            }
+      }
+      __syncthreads();
+      // reduce: thread -> (task, row, token); h = silu(bf16 g) * bf16 u
+      for (int i = threadIdx.x; i < nb * 16 * T; i += kDecThreads) {
+        const int jb = i / (16 * T), r = (i / T) & 15, j = i % T;
+        const GuTask t = ph == 0 ? shared_task(pl, b0 + jb) : routed_task(pl, b0 + jb);
+        const int p0 = t.u < 0 ? pl.P : tb.p0[t.u];
+        const int cnt = t.u < 0 ? T : tb.cnt[t.u];
+        if (j >= cnt) continue;
+        float gv = 0.f, uv = 0.f;
+        for (int w = 0; w < kDecWarps; ++w) {
+          const float* pw = part + (jb * kDecWarps + w) * pw_floats;
+          gv += pw[r * T + j];
+          uv += pw[(16 + r) * T + j];
+        }
+        const float hv = silu_mul_bf16(bf16r(gv), bf16r(uv));
+        a.h[int64_t(p0 + j) * a.ldh + t.rb * 16 + r] = f32_to_bf16(hv);
+      }
+      __syncthreads();
+    }
+  };
+
+  // ---- shared expert gate/up while the logits are being computed elsewhere
+  if (pl.ns > 0) run_gu(0, pl.ns);
+
+  // ---- barrier 1: every logit stored
+  if (threadIdx.x == 0) {
+    if (!grid_wait(a.sync + 0, uint32_t(G), a.wait_ns)) {
+      atomicOr(a.err, 0x400);
+      tb.plan[kPlanAbort] = 1;
+    }
+  }
+  __syncthreads();
+  if (tb.plan[kPlanAbort]) {
+    ring_drain(rg);
+    if (sd_owner && threadIdx.x == 0) mbar_wait(sd_bar, 0);
+    return;
+  }
+
+  // ---- routing: top-k ids per token (warp t), then the stable expert sort;
+  // the renormalised weights are needed only by the combine and come later
+  if (warp < T) topk_select<PER, true>(a.logits + int64_t(warp) * E, E, k, tb.inds + warp * k);
+  __syncthreads();
+  if (warp == 0) {
+    const int P = pl.P;
+    // ids outside [0, E) (a selection among NaN logits) are dropped, as the
+    // permutation drops them: no position, counted in the error word
+    uint32_t kv[2];
+    int n_bad = 0;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int i = lane + 32 * r;
+      const int e = i < P ? tb.inds[i] : -1;
+      const bool ok = i < P && e >= 0 && e < E;
+      n_bad += (i < P && !ok) ? 1 : 0;
+      kv[r] = ok ? (uint32_t(e) << 6) | uint32_t(i) : 0xFFFFFFFFu;
+      if (i < P) tb.posof[i] = -1;
+    }
+    n_bad = __reduce_add_sync(0xFFFFFFFFu, n_bad);
+    if (n_bad && lane == 0 && blockIdx.x == 0) atomicAdd(a.err + 1, n_bad);
+    __syncwarp();
+    // sorted order by rank: a key's position is the number of keys below it
+    // (valid keys are distinct: the flat index is part of the key); the
+    // sorted keys go through shared memory (the plan region is free here)
+    {
+      int ra = 0, rb = 0;
+#pragma unroll 8
+      for (int j = 0; j < 32; ++j) {
+        const uint32_t xa = __shfl_sync(0xFFFFFFFFu, kv[0], j);
+        const uint32_t xb = __shfl_sync(0xFFFFFFFFu, kv[1], j);
+        ra += (xa < kv[0]) + (xb < kv[0]);
+        rb += (xa < kv[1]) + (xb < kv[1]);
+      }
+      uint32_t* skey = reinterpret_cast<uint32_t*>(part);
+      skey[lane] = skey[lane + 32] = 0xFFFFFFFFu;
+      __syncwarp();
+      if (kv[0] != 0xFFFFFFFFu) skey[ra] = kv[0];
+      if (kv[1] != 0xFFFFFFFFu) skey[rb] = kv[1];
+      __syncwarp();
+      kv[0] = skey[lane];
+      kv[1] = skey[lane + 32];
+    }
+    const uint32_t e0 = kv[0] >> 6, e1 = kv[1] >> 6;
+    const uint32_t prev0 = __shfl_up_sync(0xFFFFFFFFu, e0, 1);
+    uint32_t prev1 = __shfl_up_sync(0xFFFFFFFFu, e1, 1);
+    const uint32_t last0 = __shfl_sync(0xFFFFFFFFu, e0, 31);
+    if (lane == 0) prev1 = last0;
+    const bool v0 = kv[0] != 0xFFFFFFFFu, v1 = kv[1] != 0xFFFFFFFFu;
+    const int Pv = __popc(__ballot_sync(0xFFFFFFFFu, v0)) + __popc(__ballot_sync(0xFFFFFFFFu, v1));
+    const bool h0 = v0 && (lane == 0 || e0 != prev0);
+    const bool h1 = v1 && e1 != prev1;
+    const uint32_t b0 = __ballot_sync(0xFFFFFFFFu, h0), b1 = __ballot_sync(0xFFFFFFFFu, h1);
+    const uint32_t lt = (1u << lane) - 1u;
+    const int U = __popc(b0) + __popc(b1);
+    if (v0) {
+      const int f = int(kv[0] & 63u);
+      tb.posof[f] = lane;
+      tb.tok[lane] = f / k;
+    }
+    if (v1) {
+      const int f = int(kv[1] & 63u);
+      tb.posof[f] = lane + 32;
+      tb.tok[lane + 32] = f / k;
+    }
+    if (h0) {
+      const int u = __popc(b0 & lt);
+      tb.ex[u] = int(e0);
+      tb.p0[u] = lane;
+    }
+    if (h1) {
+      const int u = __popc(b0) + __popc(b1 & lt);
+      tb.ex[u] = int(e1);
+      tb.p0[u] = lane + 32;
+    }
+    if (lane == 0) tb.plan[kPlanU] = U;
+    __syncwarp();
+    for (int u = lane; u < U; u += 32) tb.cnt[u] = (u + 1 < U ? tb.p0[u + 1] : Pv) - tb.p0[u];
+
+    // ---- byte-balanced split of the routed gate/up tasks over the CTAs (in
+    // units of 256 bytes): each CTA's pre-assigned work - its logits (CTAs
+    // [0, L)), its shared gate/up tasks (q + 1 for CTAs [L, L + r), q for
+    // [L + r, G), ns_total = q * (G - L) + r), its down rows (CTAs
+    // [G - n_dt, G)) - plus routed tasks up to an equal share.  The
+    // pre-assigned loads are constant on the intervals those ranges make, so
+    // a CTA's running total of free capacity is a closed form.
+    if (lane == 0) {
+      const int nr_total = U * pl.rbg;
+      const int task_w = pl.nch_d * 10;
+      const int logit_w = kDecLogitRows * d * 2 / 256;
+      const int down_w = (U * pl.nch_i + lay.nch_s) * 5;
+      const int span = G - pl.L, sq = ns_total / span, sr = ns_total % span;
+      const int b0 = pl.L, b1 = pl.L + sr, b2 = G - pl.n_dt;
+      const int64_t tot_pre = int64_t(pl.L) * logit_w + int64_t(ns_total) * task_w + int64_t(pl.n_dt) * down_w;
+      const int64_t target = (tot_pre + int64_t(nr_total) * task_w) / G;
+      // free capacity of the CTAs in [0, c)
+      auto cum_cap = [&](int c) -> int64_t {
+        int64_t sum = 0;
+        // walk the sorted breakpoints: on each piece the load is constant
+        int pts[5] = {0, b0, b1, b2, G};   // loads are constant between sorted points
+        for (int x = 1; x < 5; ++x)          // insertion sort of 5 points
+          for (int y = x; y > 0 && pts[y] < pts[y - 1]; --y) {
+            const int t = pts[y];
+            pts[y] = pts[y - 1];
+            pts[y - 1] = t;
+          }
+        for (int x = 0; x < 4; ++x) {
+          const int lo = pts[x], hi = min(pts[x + 1], c);
+          if (hi <= lo) continue;
+          const int64_t load = (lo < b0 ? logit_w : int64_t(lo < b1 ? sq + 1 : sq) * task_w) +
+                               (lo >= b2 ? down_w : 0);
+          sum += int64_t(hi - lo) * max(int64_t(0), target - load);
+        }
+        return sum;
+      };
+      const int64_t cap_tot = cum_cap(G), c_lo = cum_cap(int(blockIdx.x)), c_hi = cum_cap(int(blockIdx.x) + 1);
+      int first, last;
+      if (cap_tot > 0) {
+        first = int((c_lo * nr_total + cap_tot / 2) / cap_tot);
+        last = int((c_hi * nr_total + cap_tot / 2) / cap_tot);
+      } else {
+        first = int(blockIdx.x) * nr_total / G;
+        last = (int(blockIdx.x) + 1) * nr_total / G;
+      }
+      tb.plan[kPlanFirst] = first;
+      tb.plan[kPlanNr] = last - first;
+    }
+  }
+  __syncthreads();
+  pl.U = tb.plan[kPlanU];
+  pl.first = tb.plan[kPlanFirst];
+  pl.nr = tb.plan[kPlanNr];
+  pl.routed = true;
+  if (blockIdx.x == 0 && a.inds_out)
+    for (int i = threadIdx.x; i < pl.P; i += kDecThreads) a.inds_out[i] = tb.inds[i];
+
+  // ---- phase G: routed gate/up tasks
+  ring_fill(a, pl, tb, rg, warp, pol);
+  run_gu(1, pl.nr);
+
+  // ---- barrier 2: every h row stored (run_gu ends with a CTA barrier)
+  ring_fill(a, pl, tb, rg, warp, pol);
+  if (threadIdx.x == 0) grid_arrive(a.sync + 1);
+
+  // the routing weights (topk_row's arithmetic), off the critical path: the
+  // down owners need them for the combine, CTA 0 writes them out
+  if (pl.td >= 0 || (blockIdx.x == 0 && a.w_out)) {
+    if (warp < T)
+      topk_weights<PER, true>(a.logits + int64_t(warp) * E, E, k, tb.inds + warp * k, tb.wts + warp * k);
+    __syncthreads();
+    if (blockIdx.x == 0 && a.w_out)
+      for (int i = threadIdx.x; i < pl.P; i += kDecThreads) a.w_out[i] = tb.wts[i];
+  }
+  if (pl.td < 0) {
+    if (rg.timed_out) atomicOr(a.err, 0x100);
+    return;   // no down tile (and nothing in flight): done
+  }
+  if (threadIdx.x == 0) {
+    if (!grid_wait(a.sync + 1, uint32_t(G), a.wait_ns)) {
+      atomicOr(a.err, 0x400);
+      tb.plan[kPlanAbort] = 1;
+    }
+  }
+  __syncthreads();
+  if (tb.plan[kPlanAbort]) {
+    ring_drain(rg);
+    if (sd_owner && threadIdx.x == 0) mbar_wait(sd_bar, 0);
+    return;
+  }
+
+  // ---- h records of every position
+  {
+    const int n = lay.Pp * lay.nch_h * 16;
+    for (int i = threadIdx.x; i < ((n + 31) & ~31); i += kDecThreads) {
+      const bool live0 = i < n;
+      const int pos = live0 ? i / (lay.nch_h * 16) : 0;
+      const int r = live0 ? i - pos * lay.nch_h * 16 : 0;
+      const int ch = r >> 4, blk = r & 15;
+      const int K = pos >= pl.P ? a.Is : a.I;
+      const bool live = live0 && ch * 128 < K;
+      const uint4 v = live ? __ldcg(reinterpret_cast<const uint4*>(a.h + int64_t(pos) * a.ldh + ch * 128 + blk * 8))
+                           : make_uint4(0, 0, 0, 0);
+      put_record_block(smem + lay.off_h + (ch * lay.Pp + pos) * kActRecord, blk, v, live);
+    }
+  }
+  __syncthreads();
+
+  // ---- phase D: this CTA's 16 rows of the down projection, one expert a
+  // job: jobs u = warp, warp + 8, ... (the shared expert last)
+  {
+    uint16_t* ydn = reinterpret_cast<uint16_t*>(smem + lay.off_y);
+    const int ndj = pl.U + (a.Is > 0 ? 1 : 0);
+    for (int u = warp; u < ndj; u += kDecWarps) {
+      const bool sh = u == pl.U;
+      const int p0 = sh ? pl.P : tb.p0[u];
+      const int cnt = sh ? T : tb.cnt[u];
+      const int nch = sh ? lay.nch_s : pl.nch_i;
+      uint32_t tokoff[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) tokoff[q] = uint32_t(p0 + q) * kActRecord;
+      float acc[1][2][2] = {};
+      if (sh && !mbar_wait(sd_bar, 0)) rg.timed_out = true;
+      for (int ch = 0; ch < nch; ++ch) {
+        uint32_t st;
+        if (sh) {
+          st = smem_u32(smem + lay.off_sd) + ch * 1280;
+        } else {
+          if (rg.issued - rg.used < rg.R && rg.cur.ph != 3) ring_fill(a, pl, tb, rg, warp, pol);
+          st = ring_take(rg);
+        }
+        const uint32_t brec = smem_u32(smem + lay.off_h) + ch * lay.Pp * kActRecord;
+        if (cnt > 2)
+          rec_mma<2, 1>(st, brec, tokoff, cnt, zaddr, acc);
+        else
+          rec_mma<1, 1>(st, brec, tokoff, cnt, zaddr, acc);
+        if (!sh) ring_release(rg);
+      }
+#pragma unroll
+      for (int q = 0; q < 2; ++q)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float v = acc[0][q][h] + __shfl_xor_sync(0xFFFFFFFFu, acc[0][q][h], 1);
+          const int j = 2 * q + ((lane & 3) >> 1);
+          if ((lane & 1) == 0 && j < cnt) ydn[(p0 + j) * lay.tile_rows + (lane >> 2) + 8 * h] = f32_to_bf16(v);
+        }
+    }
+  }
+  __syncthreads();
+
+  // ---- combine of this CTA's rows (combine_kernel's order)
+  {
+    const uint16_t* ydn = reinterpret_cast<const uint16_t*>(smem + lay.off_y);
+    for (int i = threadIdx.x; i < T * lay.tile_rows; i += kDecThreads) {
+      const int t = i / lay.tile_rows, r = i - t * lay.tile_rows;
+      const int row = pl.td * lay.tile_rows + r;
+      if (row >= d) continue;
+      float acc = 0.f;
+      for (int s = 0; s < k; ++s) {
+        const int pos = tb.posof[t * k + s];
+        if (pos < 0) continue;   // a dropped id
+        const float w = bf16_to_f32(tb.wts[t * k + s]);
+        acc = __fadd_rn(acc, __fmul_rn(bf16_to_f32(ydn[pos * lay.tile_rows + r]), w));
+      }
+      float out = bf16r(acc);
+      if (a.Is > 0) {
+        const float gate = bf16_to_f32(__ldcg(a.sg + t));
+        const float s0 = bf16r(__fmul_rn(bf16_to_f32(ydn[(pl.P + t) * lay.tile_rows + r]), gate));
+        out = bf16r(__fadd_rn(out, s0));
+      }
+      a.y[int64_t(t) * d + row] = f32_to_bf16(out);
+    }
+  }
+  if (rg.timed_out) atomicOr(a.err, 0x100);
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+static int dec_smem_cap() {
+  static int cap[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (cap[dev] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) v = 0;
+    // room for the static shared memory
+    cap[dev] = v > 4096 ? v - 1024 : 0;
+  }
+  return cap[dev];
+}
+
+bool decode_supported(int T, int E, int d, int k, int I, int Is, int gu_tile_rows, int dn_tile_rows) {
+  if (T < 1 || T > kDecodeMaxT || T * k > kDecMaxRoutes || k > kMaxK) return false;
+  if (E < 1 || E > 1024 || d % 128 || I % 128 || (Is && Is % 128) || d > 8192) return false;
+  if (gu_tile_rows != 16 || (dn_tile_rows != 16 && dn_tile_rows != 32)) return false;
+  const int G = sm_count();
+  const int L = (E + kDecLogitRows - 1) / kDecLogitRows;
+  const int n_dt = (d + 15) / 16;            // 16-row owners of y
+  if (L >= G || n_dt > G) return false;   // CTA L computes the shared gate
+  const int cap = dec_smem_cap();
+  if (cap <= 0) return false;
+  const DecLayout lay = dec_layout(T, d, k, I, Is, dn_tile_rows / 16, cap);
+  // enough stages to keep every warp's stream going
+  return lay.ring_stages >= 2 * kDecWarps && lay.total <= cap;
+}
+
+template <int PER, int DNMT>
+static cudaError_t launch_decode_t(const DecodeArgs& a0, cudaStream_t st) {
+  DecodeArgs a = a0;
+  a.smem_bytes = dec_smem_cap();
+  const DecLayout lay = dec_layout(a.T, a.d, a.k, a.I, a.Is, DNMT, a.smem_bytes);
+  auto kern = decode_kernel<PER, DNMT>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, lay.total);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(sm_count());
+  cfg.blockDim = dim3(kDecThreads);
+  cfg.dynamicSmemBytes = lay.total;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+template <int PER>
+static cudaError_t launch_decode_p(const DecodeArgs& a, cudaStream_t st) {
+  return a.dn_mt == 2 ? launch_decode_t<PER, 2>(a, st) : launch_decode_t<PER, 1>(a, st);
+}
+
+cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t st) {
+  if (a.dn_mt != 1 && a.dn_mt != 2) return cudaErrorInvalidValue;
+  const int per = (a.E + 31) / 32;
+  if (per <= 4) return launch_decode_p<4>(a, st);
+  if (per <= 8) return launch_decode_p<8>(a, st);
+  if (per <= 16) return launch_decode_p<16>(a, st);
+  return launch_decode_p<32>(a, st);
+}
+
+}  // namespace vx

@@ -231,6 +231,40 @@ cudaError_t launch_router_fused(const uint16_t* x, int T, const uint16_t* wg, in
                                 uint16_t* sg, int32_t* counters, const PermSmallArgs* perm,
                                 const uint16_t* bias, cudaStream_t st, bool counters_zeroed = false);
 
+// The whole block for at most kDecodeMaxT tokens in one cooperative launch
+// (vx_decode.cu): weights from the tiled pool (gate/up records of 16 rows,
+// down records of 16 or 32 rows).  Scratch (caller workspace): logits
+// [T][E], sg [T], the SwiGLU outputs h [T*k+T][ldh] bf16 of every sorted
+// position, and the two barrier counters in sync[2], zero at launch.
+constexpr int kDecodeMaxT = 4;
+
+struct DecodeArgs {
+  const uint16_t* x;
+  const uint16_t* router_w;
+  const uint16_t* router_bias;        // may be null
+  vx_q4 seg;                          // shared expert gate (w null: none)
+  const unsigned char* gu_rec;        // routed gate/up records
+  const unsigned char* gu_rec_s;      // shared gate/up records (null: no shared expert)
+  const unsigned char* dn_rec;        // routed down records
+  const unsigned char* dn_rec_s;      // shared down records
+  int64_t gu_stride, dn_stride;       // bytes per routed expert
+  int T, E, d, k, I, Is, dn_mt, ldh;  // Is = 0: no shared expert; dn_mt = down tile rows / 16
+  uint16_t* logits;
+  uint16_t* h;
+  uint16_t* sg;
+  uint32_t* sync;
+  int32_t* err;                       // [0] bits 0x400 (a grid barrier wait ran out), 0x100 (a copy
+                                      // wait); [1] routes dropped for an id outside [0, E)
+  uint16_t* y;
+  int32_t* inds_out;                  // may be null
+  uint16_t* w_out;                    // may be null
+  uint64_t wait_ns;
+  int smem_bytes;                     // set by the launcher
+};
+
+bool decode_supported(int T, int E, int d, int k, int I, int Is, int gu_tile_rows, int dn_tile_rows);
+cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t st);
+
 // Expert-parallel exchange buffer of one rank (vx_ep.cu): a 256-byte header
 // (u32 flag_dispatch[8], flag_combine[8], epoch, tickets[3]), then, for a step
 // of T <= cap tokens per rank, rows i = r*T + t of

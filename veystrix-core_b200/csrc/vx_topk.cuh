@@ -1,0 +1,233 @@
+// Softmax + top-k + renorm of one token's bf16 router logits, one warp per
+// token (models/flashnext/adaptive_topk.py:59-65, :257-262; compiled.py:
+// 60-70).  Shared by the router kernels and the single-launch decode kernel.
+#pragma once
+
+#include "vx_common.cuh"
+
+namespace vx {
+
+// ---- softmax + top-k + renorm: one warp per token --------------------------
+// Register-only: lane r keeps the r-th selection.  The selection sum runs in
+// slot order on every lane, as the reference's mass reduction does.
+//
+// Selection order: larger logit first, the smaller expert id among equal
+// logits.  Each candidate is one 32-bit key - the bf16 logit mapped to an
+// order-preserving unsigned 16-bit code (-0 folded onto +0, so zeros tie as
+// equal floats do) above 0xFFFF - id - so a round of the selection is one
+// warp-wide unsigned max (redux) plus a lane-local refresh.
+constexpr int kMaxK = 32;
+
+VX_DEVICE uint32_t logit_key(uint16_t b, int e) {
+  if ((b & 0x7FFFu) == 0) b = 0;                                   // -0 -> +0
+  if ((b & 0x7FFFu) > 0x7F80u) return 0u;                          // NaN: never selected
+  const uint32_t ord = (b & 0x8000u) ? (~uint32_t(b) & 0xFFFFu) : (uint32_t(b) | 0x8000u);
+  return (ord << 16) | (0xFFFFu - uint32_t(e));
+}
+
+VX_DEVICE float key_logit(uint32_t key) {
+  const uint32_t ord = key >> 16;
+  const uint32_t b = (ord & 0x8000u) ? (ord & 0x7FFFu) : (~ord & 0xFFFFu);
+  return bf16_to_f32(uint16_t(b));
+}
+
+template <int PER, bool COHERENT>
+__device__ __forceinline__ void topk_row(const uint16_t* lr, int E, int k, int32_t* inds, uint16_t* scores,
+                                         uint16_t* weights, uint16_t* mass) {
+  const int lane = threadIdx.x & 31;
+  // Lane owns experts lane*PER .. lane*PER+PER-1 and fetches them with one
+  // or a few vector loads, all issued before any is used (a chain of 2-byte
+  // loads waited on one by one cost microseconds).  Logits written by other
+  // CTAs of the same launch are read past L1.
+  const int e0 = lane * PER;
+  uint32_t raw[PER / 2];
+  constexpr int kVec = PER >= 8 ? 8 : 4;   // bf16 per vector load
+  const bool vec = e0 + PER <= E && E % kVec == 0 && (reinterpret_cast<uintptr_t>(lr) & (2 * kVec - 1)) == 0;
+  if (vec) {
+    if constexpr (PER >= 8) {
+      const uint4* p = reinterpret_cast<const uint4*>(lr + e0);
+      uint4 q[PER / 8];
+#pragma unroll
+      for (int v = 0; v < PER / 8; ++v) q[v] = COHERENT ? __ldcg(p + v) : p[v];
+#pragma unroll
+      for (int v = 0; v < PER / 8; ++v) {
+        raw[4 * v] = q[v].x;
+        raw[4 * v + 1] = q[v].y;
+        raw[4 * v + 2] = q[v].z;
+        raw[4 * v + 3] = q[v].w;
+      }
+    } else {
+      const uint2 q = COHERENT ? __ldcg(reinterpret_cast<const uint2*>(lr + e0))
+                               : *reinterpret_cast<const uint2*>(lr + e0);
+      raw[0] = q.x;
+      raw[1] = q.y;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < PER; j += 2) {
+      const uint32_t lo = e0 + j < E ? (COHERENT ? __ldcg(lr + e0 + j) : lr[e0 + j]) : 0u;
+      const uint32_t hi = e0 + j + 1 < E ? (COHERENT ? __ldcg(lr + e0 + j + 1) : lr[e0 + j + 1]) : 0u;
+      raw[j / 2] = lo | (hi << 16);
+    }
+  }
+  uint32_t key[PER];
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int e = e0 + j;
+    const uint16_t b = uint16_t(raw[j / 2] >> (16 * (j & 1)));
+    key[j] = e < E ? logit_key(b, e) : 0u;
+    if (e < E) m = fmaxf(m, bf16_to_f32(b));
+  }
+  m = warp_max(m);
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < PER; ++j)
+    if (e0 + j < E) s += expf(__fsub_rn(key_logit(key[j]), m));
+  s = warp_sum<32>(s);
+  const float inv = __fdiv_rn(1.0f, s);
+
+  uint32_t lm = 0;
+#pragma unroll
+  for (int j = 0; j < PER; ++j) lm = max(lm, key[j]);
+  uint32_t my_key = 0;
+  for (int r = 0; r < k; ++r) {
+    const uint32_t g = __reduce_max_sync(0xFFFFFFFFu, lm);
+    if (lane == r) my_key = g;
+    if (lm == g) {   // the owner: drop the selected key, refresh the local max
+      lm = 0;
+#pragma unroll
+      for (int j = 0; j < PER; ++j) {
+        if (key[j] == g) key[j] = 0;
+        lm = max(lm, key[j]);
+      }
+    }
+  }
+  const int my_i = int(0xFFFFu - (my_key & 0xFFFFu));
+  const float my_p = bf16r(__fmul_rn(expf(__fsub_rn(key_logit(my_key), m)), inv));
+  float tot = 0.f;
+  for (int r = 0; r < k; ++r) tot = __fadd_rn(tot, __shfl_sync(0xFFFFFFFFu, my_p, r));
+  // mass and renorm (blend 1.0): norm = mass + 1.0*(sum - mass), in bf16.
+  const float msum = bf16r(tot);
+  const float diff = bf16r(__fsub_rn(msum, msum));
+  const float norm = bf16r(__fadd_rn(msum, bf16r(diff)));
+  if (lane < k) {
+    inds[lane] = my_i;
+    if (scores) scores[lane] = f32_to_bf16(my_p);
+    weights[lane] = f32_to_bf16(bf16r(__fdiv_rn(my_p, norm)));
+  }
+  if (mass && lane == 0) *mass = f32_to_bf16(msum);
+}
+
+}  // namespace vx
+
+namespace vx {
+
+// The same routing split in two, for callers that need the ids before the
+// weights: topk_select writes the top-k ids of one token (lane r < k holds
+// the r-th selection, the order and tie rule of topk_row); topk_weights later
+// writes the renormalised weights of given ids with exactly topk_row's
+// arithmetic (per-lane sums over the lane's PER experts, then the same warp
+// butterfly), so both halves together reproduce topk_row bit for bit.
+template <int PER, bool COHERENT>
+__device__ __forceinline__ void topk_load(const uint16_t* lr, int E, uint32_t (&raw)[PER / 2]) {
+  const int lane = threadIdx.x & 31;
+  const int e0 = lane * PER;
+  constexpr int kVec = PER >= 8 ? 8 : 4;
+  const bool vec = e0 + PER <= E && E % kVec == 0 && (reinterpret_cast<uintptr_t>(lr) & (2 * kVec - 1)) == 0;
+  if (vec) {
+    if constexpr (PER >= 8) {
+      const uint4* p = reinterpret_cast<const uint4*>(lr + e0);
+      uint4 q[PER / 8];
+#pragma unroll
+      for (int v = 0; v < PER / 8; ++v) q[v] = COHERENT ? __ldcg(p + v) : p[v];
+#pragma unroll
+      for (int v = 0; v < PER / 8; ++v) {
+        raw[4 * v] = q[v].x;
+        raw[4 * v + 1] = q[v].y;
+        raw[4 * v + 2] = q[v].z;
+        raw[4 * v + 3] = q[v].w;
+      }
+    } else {
+      const uint2 q = COHERENT ? __ldcg(reinterpret_cast<const uint2*>(lr + e0))
+                               : *reinterpret_cast<const uint2*>(lr + e0);
+      raw[0] = q.x;
+      raw[1] = q.y;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < PER; j += 2) {
+      const uint32_t lo = e0 + j < E ? (COHERENT ? __ldcg(lr + e0 + j) : lr[e0 + j]) : 0u;
+      const uint32_t hi = e0 + j + 1 < E ? (COHERENT ? __ldcg(lr + e0 + j + 1) : lr[e0 + j + 1]) : 0u;
+      raw[j / 2] = lo | (hi << 16);
+    }
+  }
+}
+
+template <int PER, bool COHERENT>
+__device__ __forceinline__ void topk_select(const uint16_t* lr, int E, int k, int32_t* inds) {
+  const int lane = threadIdx.x & 31;
+  const int e0 = lane * PER;
+  uint32_t raw[PER / 2];
+  topk_load<PER, COHERENT>(lr, E, raw);
+  uint32_t key[PER];
+  uint32_t lm = 0;
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int e = e0 + j;
+    key[j] = e < E ? logit_key(uint16_t(raw[j / 2] >> (16 * (j & 1))), e) : 0u;
+    lm = max(lm, key[j]);
+  }
+  uint32_t my_key = 0;
+  for (int r = 0; r < k; ++r) {
+    const uint32_t g = __reduce_max_sync(0xFFFFFFFFu, lm);
+    if (lane == r) my_key = g;
+    if (lm == g) {   // the owner: drop the selected key, refresh the local max
+      lm = 0;
+#pragma unroll
+      for (int j = 0; j < PER; ++j) {
+        if (key[j] == g) key[j] = 0;
+        lm = max(lm, key[j]);
+      }
+    }
+  }
+  if (lane < k) inds[lane] = int(0xFFFFu - (my_key & 0xFFFFu));
+}
+
+template <int PER, bool COHERENT>
+__device__ __forceinline__ void topk_weights(const uint16_t* lr, int E, int k, const int32_t* inds,
+                                             uint16_t* weights) {
+  const int lane = threadIdx.x & 31;
+  const int e0 = lane * PER;
+  uint32_t raw[PER / 2];
+  topk_load<PER, COHERENT>(lr, E, raw);
+  uint32_t key[PER];
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int e = e0 + j;
+    const uint16_t b = uint16_t(raw[j / 2] >> (16 * (j & 1)));
+    key[j] = e < E ? logit_key(b, e) : 0u;
+    if (e < E) m = fmaxf(m, bf16_to_f32(b));
+  }
+  m = warp_max(m);
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < PER; ++j)
+    if (e0 + j < E) s += expf(__fsub_rn(key_logit(key[j]), m));
+  s = warp_sum<32>(s);
+  const float inv = __fdiv_rn(1.0f, s);
+  // the selected expert's key, as topk_select held it (0 for an id out of range)
+  const int my_i = lane < k ? inds[lane] : -1;
+  const uint32_t my_key =
+      (my_i >= 0 && my_i < E) ? logit_key(COHERENT ? __ldcg(lr + my_i) : lr[my_i], my_i) : 0u;
+  const float my_p = bf16r(__fmul_rn(expf(__fsub_rn(key_logit(my_key), m)), inv));
+  float tot = 0.f;
+  for (int r = 0; r < k; ++r) tot = __fadd_rn(tot, __shfl_sync(0xFFFFFFFFu, my_p, r));
+  const float msum = bf16r(tot);
+  const float diff = bf16r(__fsub_rn(msum, msum));
+  const float norm = bf16r(__fadd_rn(msum, bf16r(diff)));
+  if (lane < k) weights[lane] = f32_to_bf16(bf16r(__fdiv_rn(my_p, norm)));
+}
+
+}  // namespace vx
