@@ -296,6 +296,20 @@ int vx_ep_experts(const vx_ep_comm* comm, int32_t T, const vx_moe_weights* W, vo
 int vx_ep_combine(const vx_ep_comm* comm, int32_t T, const int32_t* inds, const uint16_t* shared,
                   const uint16_t* shared_gate, uint16_t* y, void* stream);
 
+/* Combine of already projected values, the reference's generic helper
+ * weighted_combine (metal_runtime.py:145-191): y[t, :] = sum_s out[t, sel, :]
+ * * scores[t, s] with sel = routes[t, s] when the outputs hold all n_out
+ * experts of a token (out [T, n_out, d]), else sel = s (routes NULL, out
+ * [T, k, d], n_out == k).  dtype VX_DTYPE_BF16 or VX_DTYPE_F32 for outputs,
+ * scores and y alike; bf16 products are rounded to bf16, the slot sum runs in
+ * float32 in slot order and is rounded once.  Routes outside [0, n_out) add
+ * nothing and are counted in *error_count (device int32, may be NULL). */
+#define VX_DTYPE_BF16 0
+#define VX_DTYPE_F32 1
+int vx_weighted_combine(const void* outputs, int32_t dtype, int32_t n_out, const int32_t* routes,
+                        const void* scores, int64_t T, int32_t k, int32_t d, void* y,
+                        int32_t* error_count, void* stream);
+
 /* RMSNorm in float32 with a bf16 gain, bf16 out (patch_rmsnorm.py:96-120). */
 int vx_rmsnorm(const uint16_t* x, const uint16_t* gain, int32_t T, int32_t d,
                float eps, uint16_t* y, void* stream);

@@ -57,7 +57,17 @@ def test_ep_single_rank_equals_block(transport, packed):
         for T in (1, 5, 64, 256):
             x = torch.randn((T, w.hidden), device=dev).to(torch.bfloat16)
             y = layer(x)
-            ref = vxmoe.moe_block(x, w)
+            # the expert-parallel step runs the multi-kernel pipeline; the block
+            # runs batches of at most four tokens as the single cooperative
+            # launch (another float32 summation order), so its reference here
+            # is the block with the grouped GEMV kernels forced
+            old = w.expert_path
+            if T <= 4:
+                w.expert_path = vxmoe._lib.PATH_GEMV
+            try:
+                ref = vxmoe.moe_block(x, w)
+            finally:
+                w.expert_path = old
             torch.cuda.synchronize()
             np.testing.assert_array_equal(_bits(y), _bits(ref))
         if layer.exchange is not None:

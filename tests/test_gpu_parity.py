@@ -452,3 +452,30 @@ def test_errors_raise_reference_exception_types(small_params):
     with pytest.raises(ValueError):
         vxmoe.gather_qmm(bf16_t(np.zeros((1, 1, p.hidden), np.float32)), *bank_t(p.gate),
                          rhs_indices=np.array([40], np.int32))
+
+
+def test_weighted_combine_on_the_device(golden_dir):
+    """The executor's combine-only form on CUDA tensors runs the library's
+    combine kernel: the reference helper's unit values (float32), and bf16
+    slot and all-expert forms against the array expression it replaces."""
+    import vxmoe
+    g = np.load(os.path.join(golden_dir, "combine.npz"))
+    f32 = lambda a: torch.from_numpy(np.ascontiguousarray(np.asarray(a, np.float32))).to(DEV)
+    got = vxmoe.weighted_combine(f32(g["eo2"]), torch.from_numpy(g["r2"]).to(DEV), f32(g["sc2"]))
+    np.testing.assert_array_equal(got.cpu().numpy(), g["c2"])
+    got = vxmoe.weighted_combine(f32(g["slot"]), torch.from_numpy(g["r3"]).to(DEV), f32(g["sc3"]))
+    np.testing.assert_array_equal(got.cpu().numpy(), g["c3"])
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(3)
+    T, k, E, d = 37, 10, 24, 2048
+    out = torch.randn((T, E, d), device=DEV, generator=gen).to(torch.bfloat16)
+    routes = torch.stack([torch.randperm(E, device=DEV, generator=gen)[:k] for _ in range(T)]).int()
+    scores = torch.rand((T, k), device=DEV, generator=gen).to(torch.bfloat16)
+    y = vxmoe.weighted_combine(out, routes, scores)
+    sel = torch.take_along_dim(out, routes[..., None].long(), dim=-2)
+    ref = (sel.float() * scores.float()[..., None]).to(torch.bfloat16).float().sum(-2)   # bf16 products
+    assert ulp_diff_bf16(np32(y), np32(ref.to(torch.bfloat16))).max() <= 1
+    y_slot = vxmoe.weighted_combine(sel.contiguous(), routes, scores)
+    assert torch.equal(y_slot.view(torch.int16), y.view(torch.int16))
+    with pytest.raises(ValueError):
+        vxmoe.weighted_combine(out, routes + E, scores)

@@ -1009,6 +1009,18 @@ int vx_ep_combine(const vx_ep_comm* comm, int32_t T, const int32_t* inds, const 
   return VX_OK;
 }
 
+int vx_weighted_combine(const void* outputs, int32_t dtype, int32_t n_out, const int32_t* routes,
+                        const void* scores, int64_t T, int32_t k, int32_t d, void* y, int32_t* error_count,
+                        void* stream) {
+  if (dtype != VX_DTYPE_BF16 && dtype != VX_DTYPE_F32) return VX_EINVAL_DTYPE;
+  if (T < 0 || T > 0x7FFFFFFF || k < 1 || d < 0 || n_out < 1 || (!routes && n_out != k)) return VX_EINVAL_SHAPE;
+  if (T == 0 || d == 0) return VX_OK;
+  if (!outputs || !scores || !y) return VX_EINVAL_SHAPE;
+  cudaError_t e = launch_weighted_combine(outputs, n_out, routes, scores, T, k, d, dtype == VX_DTYPE_BF16, y,
+                                          error_count, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? VX_OK : vx_cuda_fail(e);
+}
+
 int vx_rmsnorm(const uint16_t* x, const uint16_t* gain, int32_t T, int32_t d, float eps, uint16_t* y,
                void* stream) {
   if (T < 0 || d <= 0) return VX_EINVAL_SHAPE;

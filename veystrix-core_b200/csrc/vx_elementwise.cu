@@ -234,4 +234,56 @@ cudaError_t launch_dequant(const vx_q4& bank, int expert, float* out, cudaStream
   return cudaGetLastError();
 }
 
+// Combine of already projected values, the reference's generic helper
+// (models/flashnext/metal_runtime.py:145-191): y[t] = sum_s out[t, sel(s)] *
+// score[t, s], sel(s) = routes[t, s] when the outputs hold every expert (n_out
+// rows per token), else the slot itself.  Products in the element type (bf16
+// products rounded to bf16), summed in float32 in slot order, one rounding to
+// the element type - what the array expression computes on bf16 or float32
+// arrays.  Routes outside [0, n_out) contribute nothing and are counted in
+// *err (may be null).
+template <bool BF16>
+__global__ void __launch_bounds__(256) weighted_combine_kernel(const void* __restrict__ outputs, int n_out,
+                                                               const int32_t* __restrict__ routes,
+                                                               const void* __restrict__ scores, int64_t T, int k,
+                                                               int d, void* __restrict__ y, int32_t* err) {
+  const int64_t t = blockIdx.x;
+  const int col = blockIdx.y * blockDim.x + threadIdx.x;
+  if (t >= T || col >= d) return;
+  float acc = 0.f;
+  for (int s = 0; s < k; ++s) {
+    const int e = routes ? routes[t * k + s] : s;
+    if (e < 0 || e >= n_out) {
+      if (col == 0 && err) atomicAdd(err, 1);
+      continue;
+    }
+    const int64_t i = (t * n_out + e) * int64_t(d) + col;
+    if (BF16) {
+      const float v = bf16_to_f32(static_cast<const uint16_t*>(outputs)[i]);
+      const float w = bf16_to_f32(static_cast<const uint16_t*>(scores)[t * k + s]);
+      acc = __fadd_rn(acc, bf16r(__fmul_rn(v, w)));
+    } else {
+      const float v = static_cast<const float*>(outputs)[i];
+      const float w = static_cast<const float*>(scores)[t * k + s];
+      acc = __fadd_rn(acc, __fmul_rn(v, w));
+    }
+  }
+  if (BF16)
+    static_cast<uint16_t*>(y)[t * d + col] = f32_to_bf16(acc);
+  else
+    static_cast<float*>(y)[t * d + col] = acc;
+}
+
+cudaError_t launch_weighted_combine(const void* outputs, int n_out, const int32_t* routes, const void* scores,
+                                    int64_t T, int k, int d, bool bf16, void* y, int32_t* err,
+                                    cudaStream_t st) {
+  if (T == 0 || d == 0) return cudaSuccess;
+  dim3 grid(unsigned(T), unsigned((d + 255) / 256));
+  if (bf16)
+    weighted_combine_kernel<true><<<grid, 256, 0, st>>>(outputs, n_out, routes, scores, T, k, d, y, err);
+  else
+    weighted_combine_kernel<false><<<grid, 256, 0, st>>>(outputs, n_out, routes, scores, T, k, d, y, err);
+  return cudaGetLastError();
+}
+
 }  // namespace vx

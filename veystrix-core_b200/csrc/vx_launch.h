@@ -310,6 +310,9 @@ cudaError_t launch_combine_partial(const uint16_t* yd, int64_t ldy, const int32_
                                    cudaStream_t st);
 cudaError_t launch_unpermute(const uint16_t* yd, int64_t ldy, const int32_t* inverse, int T,
                              int k, int d, uint16_t* out, cudaStream_t st);
+cudaError_t launch_weighted_combine(const void* outputs, int n_out, const int32_t* routes, const void* scores,
+                                    int64_t T, int k, int d, bool bf16, void* y, int32_t* err,
+                                    cudaStream_t st);
 cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* gain, int T, int d, float eps,
                            uint16_t* y, cudaStream_t st);
 cudaError_t launch_swiglu(const uint16_t* g, const uint16_t* u, uint16_t* out, int64_t n,

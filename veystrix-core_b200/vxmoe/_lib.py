@@ -21,6 +21,9 @@ VX_ETIMEOUT = 5
 VX_EWORKSPACE = 6
 VX_EUNSUPPORTED = 7
 
+VX_DTYPE_BF16 = 0
+VX_DTYPE_F32 = 1
+
 c_int32 = ctypes.c_int32
 c_int64 = ctypes.c_int64
 c_size_t = ctypes.c_size_t
@@ -118,6 +121,7 @@ SIGNATURES = {
                                      ctypes.POINTER(VxMoEWeights), P, c_size_t, P]),
     "vx_ep_combine": (ctypes.c_int, [ctypes.POINTER(VxEpComm), c_int32, P, P, P, P, P]),
     "vx_rmsnorm": (ctypes.c_int, [P, P, c_int32, c_int32, c_float, P, P]),
+    "vx_weighted_combine": (ctypes.c_int, [P, c_int32, c_int32, P, P, c_int64, c_int32, c_int32, P, P, P]),
     "vx_profile_enable": (ctypes.c_int, [ctypes.c_int]),
     "vx_profile_read": (ctypes.c_int, [ctypes.c_int, ctypes.c_char_p, ctypes.c_int,
                                        ctypes.POINTER(ctypes.c_double),

@@ -69,7 +69,11 @@ def probe_capabilities(backend: Any = None) -> Capabilities:
 def weighted_combine(expert_outputs, routes, scores):
     """``sum(selected * scores[..., None], axis=-2)`` where ``selected`` is
     the slot form or, when outputs hold every expert, the routed experts
-    (``metal_runtime.py:145-191``).  Torch tensors stay on their device."""
+    (``metal_runtime.py:145-191``).  CUDA tensors (bf16 or float32) run the
+    library's combine kernel (vx_weighted_combine); host arrays are combined
+    on the host, as the reference helper does for NumPy arrays."""
+    if isinstance(expert_outputs, torch.Tensor) and expert_outputs.is_cuda:
+        return _weighted_combine_cuda(expert_outputs, routes, scores)
     if isinstance(expert_outputs, np.ndarray):
         out, r, s = expert_outputs, np.asarray(routes), np.asarray(scores)
         take = lambda a, i: np.take_along_axis(a, i[..., None], axis=-2)
@@ -95,6 +99,42 @@ def weighted_combine(expert_outputs, routes, scores):
     else:
         raise ValueError(f"expert_outputs shape {oshape} does not match routes {rshape}")
     return (sel * s[..., None]).sum(-2)
+
+
+def _weighted_combine_cuda(out: torch.Tensor, routes, scores) -> torch.Tensor:
+    from . import _lib
+    dev = out.device
+    r = routes if isinstance(routes, torch.Tensor) else torch.as_tensor(np.asarray(routes))
+    s = scores if isinstance(scores, torch.Tensor) else torch.as_tensor(np.asarray(scores))
+    oshape, rshape, sshape = tuple(out.shape), tuple(r.shape), tuple(s.shape)
+    if len(oshape) < 2 or len(rshape) == 0:
+        raise ValueError("expert_outputs and routes need at least one dimension")
+    if sshape != rshape:
+        raise ValueError("routes and scores must have identical shapes")
+    if out.dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError(f"expert_outputs must be bfloat16 or float32, got {out.dtype}")
+    k, d = int(rshape[-1]), int(oshape[-1])
+    lead = rshape[:-1]
+    T = int(np.prod(lead)) if lead else 1
+    if oshape[:-1] == rshape:
+        n_out, r_dev = k, None
+    elif len(oshape) == len(rshape) + 1 and oshape[:-2] == lead and oshape[-2] >= k:
+        n_out = int(oshape[-2])
+        r_dev = r.to(device=dev, dtype=torch.int32).reshape(T, k).contiguous()
+        if r_dev.numel() and (int(r_dev.min()) < 0 or int(r_dev.max()) >= n_out):
+            raise ValueError("routes contain an expert outside expert_outputs")
+    else:
+        raise ValueError(f"expert_outputs shape {oshape} does not match routes {rshape}")
+    o = out.reshape(T, n_out, d).contiguous()
+    sc = s.to(device=dev, dtype=out.dtype).reshape(T, k).contiguous()
+    y = torch.empty((T, d), dtype=out.dtype, device=dev)
+    dtype = _lib.VX_DTYPE_BF16 if out.dtype == torch.bfloat16 else _lib.VX_DTYPE_F32
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    _lib.check(_lib.load().vx_weighted_combine(o.data_ptr(), dtype, n_out,
+                                               None if r_dev is None else r_dev.data_ptr(),
+                                               sc.data_ptr(), T, k, d, y.data_ptr(), None, stream),
+               "weighted_combine")
+    return y.reshape(*lead, d)
 
 
 def _as_projection(value, device) -> ops.Q4Projection:
