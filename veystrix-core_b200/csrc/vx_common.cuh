@@ -105,6 +105,19 @@ VX_DEVICE uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   return r;
 }
 
+// 16-byte read-only load that asks L2 to keep the line (evict-last policy):
+// the router's rows - 2 MiB per layer, read by every token - stay resident
+// while the expert records stream through L2 with an evict-first policy.
+VX_DEVICE uint4 ldg_keep(const void* p) {
+  uint64_t pol;
+  asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p), "l"(pol));
+  return v;
+}
+
 VX_DEVICE uint4 ldg_nc(const void* p) {
   uint4 v;
   asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"

@@ -544,7 +544,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const __grid_con
       for (int i = 0; i < kBatch; ++i) {
         const int s = sb + i;
         const int kk = s * 32 + c * 8;
-        wa[i] = (s < s1 && row_live) ? ldg_nc(ra + kk) : zero;
+        wa[i] = (s < s1 && row_live) ? ldg_keep(ra + kk) : zero;
         xb[i] = (s < s1 && tx < T) ? __ldg(reinterpret_cast<const uint4*>(rx + kk)) : zero;
       }
 #pragma unroll
@@ -780,31 +780,37 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const __grid_con
       const int b0 = pl.L, b1 = pl.L + sr, b2 = G - pl.n_dt;
       const int64_t tot_pre = int64_t(pl.L) * logit_w + int64_t(ns_total) * task_w + int64_t(pl.n_dt) * down_w;
       const int64_t target = (tot_pre + int64_t(nr_total) * task_w) / G;
+      // breakpoints of the piecewise-constant loads, sorted once
+      int pts[5] = {0, b0, b1, b2, G};
+      for (int x = 1; x < 5; ++x)
+        for (int y = x; y > 0 && pts[y] < pts[y - 1]; --y) {
+          const int t = pts[y];
+          pts[y] = pts[y - 1];
+          pts[y - 1] = t;
+        }
+      int64_t piece[4];
+      for (int x = 0; x < 4; ++x) {
+        const int lo = pts[x];
+        const int64_t load = (lo < b0 ? logit_w : int64_t(lo < b1 ? sq + 1 : sq) * task_w) + (lo >= b2 ? down_w : 0);
+        piece[x] = max(int64_t(0), target - load);
+      }
       // free capacity of the CTAs in [0, c)
       auto cum_cap = [&](int c) -> int64_t {
         int64_t sum = 0;
-        // walk the sorted breakpoints: on each piece the load is constant
-        int pts[5] = {0, b0, b1, b2, G};   // loads are constant between sorted points
-        for (int x = 1; x < 5; ++x)          // insertion sort of 5 points
-          for (int y = x; y > 0 && pts[y] < pts[y - 1]; --y) {
-            const int t = pts[y];
-            pts[y] = pts[y - 1];
-            pts[y - 1] = t;
-          }
         for (int x = 0; x < 4; ++x) {
           const int lo = pts[x], hi = min(pts[x + 1], c);
-          if (hi <= lo) continue;
-          const int64_t load = (lo < b0 ? logit_w : int64_t(lo < b1 ? sq + 1 : sq) * task_w) +
-                               (lo >= b2 ? down_w : 0);
-          sum += int64_t(hi - lo) * max(int64_t(0), target - load);
+          if (hi > lo) sum += int64_t(hi - lo) * piece[x];
         }
         return sum;
       };
       const int64_t cap_tot = cum_cap(G), c_lo = cum_cap(int(blockIdx.x)), c_hi = cum_cap(int(blockIdx.x) + 1);
       int first, last;
       if (cap_tot > 0) {
-        first = int((c_lo * nr_total + cap_tot / 2) / cap_tot);
-        last = int((c_hi * nr_total + cap_tot / 2) / cap_tot);
+        // correctly rounded double division: the same in every CTA, monotone in c
+        const double inv = double(nr_total) / double(cap_tot);
+        first = int(floor(double(c_lo) * inv + 0.5));
+        last = int(floor(double(c_hi) * inv + 0.5));
+        if (int(blockIdx.x) == G - 1) last = nr_total;
       } else {
         first = int(blockIdx.x) * nr_total / G;
         last = (int(blockIdx.x) + 1) * nr_total / G;

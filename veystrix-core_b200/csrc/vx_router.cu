@@ -45,8 +45,8 @@ __global__ void __launch_bounds__(32 * kRouterSlices) router_logits_kernel(
   float d[4] = {0.f, 0.f, 0.f, 0.f};
   for (int s = s0; s < s1; ++s) {
     const int k = s * 32 + c * 8;
-    const uint4 wa = ea < E ? ldg_nc(ra + k) : make_uint4(0, 0, 0, 0);
-    const uint4 wb = eb < E ? ldg_nc(rb + k) : make_uint4(0, 0, 0, 0);
+    const uint4 wa = ea < E ? ldg_keep(ra + k) : make_uint4(0, 0, 0, 0);
+    const uint4 wb = eb < E ? ldg_keep(rb + k) : make_uint4(0, 0, 0, 0);
     const uint4 xb = tx < T ? __ldg(reinterpret_cast<const uint4*>(rx + k)) : make_uint4(0, 0, 0, 0);
     mma16816(d, wa.x, wb.x, wa.y, wb.y, xb.x, xb.y);
     mma16816(d, wa.z, wb.z, wa.w, wb.w, xb.z, xb.w);
@@ -220,8 +220,8 @@ __global__ void __launch_bounds__(32 * kRouterSlices) router_fused_kernel(
     for (int i = 0; i < kBatch; ++i) {
       const int s = sb + i;
       const int kk = s * 32 + c * 8;
-      wa[i] = (s < s1 && ea < E) ? ldg_nc(ra + kk) : zero;
-      wb[i] = (s < s1 && eb < E) ? ldg_nc(rb + kk) : zero;
+      wa[i] = (s < s1 && ea < E) ? ldg_keep(ra + kk) : zero;
+      wb[i] = (s < s1 && eb < E) ? ldg_keep(rb + kk) : zero;
       xb[i] = (s < s1 && tx < T) ? __ldg(reinterpret_cast<const uint4*>(rx + kk)) : zero;
     }
 #pragma unroll
