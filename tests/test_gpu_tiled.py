@@ -1,8 +1,10 @@
 """The tiled expert pool on the GPU: the packing kernel writes the oracle's
 record layout byte for byte, and every entry point that streams the pool
-returns bit-identical results to the same weights in the MLX layout (the two
-GEMV variants share their arithmetic; only the way bytes reach shared memory
-differs), and stays within the oracle tolerance."""
+returns the same routing as the same weights in the MLX layout and outputs
+that differ only by float32 summation (the tiled gate/up GEMV unpacks to f16
+q * 2^-24 against power-of-two-scaled activations, the MLX-layout kernel to
+bf16 128 + q: the same exact products), and stays within the oracle
+tolerance."""
 from __future__ import annotations
 
 import numpy as np
@@ -10,7 +12,7 @@ import pytest
 import torch
 
 import vxmoe_oracle as O
-from helpers import bank_t, bf16_t, np32, weights_from_oracle
+from helpers import assert_same_products, bank_t, bf16_t, np32, weights_from_oracle
 
 pytestmark = pytest.mark.gpu
 
@@ -52,7 +54,7 @@ def _pair(p, shared=True, down_rows=32):
     dict(seed=13, experts=24, hidden=512, inter=160, shared_inter=224, top_k=8),  # Is != I
 ])
 @pytest.mark.parametrize("down_rows", [32, 16])
-def test_tiled_block_bit_identical_to_mlx_layout(cfg, down_rows):
+def test_tiled_block_matches_mlx_layout(cfg, down_rows):
     import vxmoe
     p = O.make_params(**cfg)
     plain, tiled = _pair(p, down_rows=down_rows)
@@ -62,7 +64,8 @@ def test_tiled_block_bit_identical_to_mlx_layout(cfg, down_rows):
         y1, i1, w1 = vxmoe.moe_block(x, tiled, return_routing=True)
         torch.cuda.synchronize()
         np.testing.assert_array_equal(i0.cpu().numpy(), i1.cpu().numpy())
-        np.testing.assert_array_equal(_bits(y0), _bits(y1), err_msg=f"T={T}")
+        np.testing.assert_array_equal(_bits(w0), _bits(w1))
+        assert_same_products(y1, y0, f"T={T}")
 
 
 def test_tiled_block_production_against_oracle():
@@ -80,7 +83,7 @@ def test_tiled_block_production_against_oracle():
         assert O.normwise_error(np32(y), ref) <= 1.5 * O.normwise_error(out.y, ref) + 2e-3
 
 
-def test_tiled_executor_paths_bit_identical():
+def test_tiled_executor_paths_match_mlx_layout():
     import vxmoe
     p = O.make_params(seed=21, experts=32, hidden=256, inter=64, shared_inter=64, top_k=4)
     plain, tiled = _pair(p, shared=False)
@@ -93,12 +96,12 @@ def test_tiled_executor_paths_bit_identical():
         a = vxmoe.moe_experts(x, routes, plain, **kw)
         b = vxmoe.moe_experts(x, routes, tiled, **kw)
         torch.cuda.synchronize()
-        np.testing.assert_array_equal(_bits(a), _bits(b))
+        assert_same_products(b, a, f"moe_experts {sorted(kw)}")
     half = torch.where(routes < 16, routes, torch.full_like(routes, -1))
     a = vxmoe.moe_experts_partial(x, half, scores, plain)
     b = vxmoe.moe_experts_partial(x, half, scores, tiled)
     torch.cuda.synchronize()
-    np.testing.assert_array_equal(a.cpu().numpy(), b.cpu().numpy())
+    assert_same_products(b, a, "moe_experts_partial")
 
 
 def test_pool_shape_mismatch_is_rejected():

@@ -9,8 +9,8 @@
 
 namespace vx {
 
-// Bounded mbarrier waits: after this many polls the waiter gives up and the
-// kernel records an error bit instead of spinning forever.
+// Bounded mbarrier waits: after a second (or this many polls) the waiter
+// gives up and the kernel records an error bit instead of waiting forever.
 constexpr uint32_t kSpinLimit = 1u << 24;
 
 // {128 + (w & 15), 128 + ((w >> 16) & 15)} as bf16x2 (exact): one lop3 with
@@ -72,10 +72,49 @@ VX_DEVICE bool mbar_try(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Waits with an iteration limit; false when the limit ran out.
+// try_wait with a suspend-time hint: a thread whose phase is not complete
+// sleeps in the barrier (woken when the phase completes, or after `ns`)
+// instead of polling, so waiting warps leave the issue slots to the warps
+// that compute.
+VX_DEVICE bool mbar_try_sleep(uint32_t bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+VX_DEVICE uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+constexpr uint32_t kWaitSleepNs = 4000;
+constexpr uint64_t kWaitLimitNs = 1000000000ull;   // one second
+
+// Bounded wait for warps that share the SM with computing warps: false when
+// a second went by without the phase completing.
 VX_DEVICE bool mbar_wait(uint32_t bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i)
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_sleep(bar, parity, kWaitSleepNs)) return true;
+    if (global_ns() - t0 > kWaitLimitNs) return false;
+  }
+  return false;
+}
+
+// Bounded polling wait for a single-thread role on a pipeline's critical
+// path (a producer or an MMA issuer): no sleep, so no wake-up latency; one
+// thread polling costs the other warps little issue bandwidth.
+VX_DEVICE bool mbar_wait_spin(uint32_t bar, uint32_t parity) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (mbar_try(bar, parity)) return true;
+    if ((i & 255) == 255 && global_ns() - t0 > kWaitLimitNs) return false;
+  }
   return false;
 }
 

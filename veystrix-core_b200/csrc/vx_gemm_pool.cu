@@ -160,7 +160,7 @@ __global__ void __launch_bounds__(kPoolThreads, 1) gemm_pool_kernel(const __grid
         for (int ch = 0; ch < k.nch; ++ch, ++ic) {
           const int r = ic % RS;
           const uint32_t ph = uint32_t(ic / RS) & 1u;
-          if (!mbar_wait(smem_u32(&rempty[r]), ph ^ 1u)) timed_out = true;
+          if (!mbar_wait_spin(smem_u32(&rempty[r]), ph ^ 1u)) timed_out = true;
           const uint32_t bar = smem_u32(&rfull[r]);
           mbar_expect(bar, uint32_t(nrec * rec_bytes));
           for (int i = 0; i < nrec; ++i)
@@ -181,7 +181,7 @@ __global__ void __launch_bounds__(kPoolThreads, 1) gemm_pool_kernel(const __grid
         for (int at = 0; at < 2 * k.nch; ++at, ++ib) {
           const int b = ib % BS;
           const uint32_t ph = uint32_t(ib / BS) & 1u;
-          if (!mbar_wait(smem_u32(&bempty[b]), ph ^ 1u)) timed_out = true;
+          if (!mbar_wait_spin(smem_u32(&bempty[b]), ph ^ 1u)) timed_out = true;
           const uint32_t bar = smem_u32(&bfull[b]);
           mbar_expect(bar, uint32_t(bn * 128));
           tma_load_2d(sb(b), tm, at * 64, k.p0, bar);
@@ -198,7 +198,7 @@ __global__ void __launch_bounds__(kPoolThreads, 1) gemm_pool_kernel(const __grid
         const int buf = j & 1;
         const uint32_t tph = uint32_t(j >> 1) & 1u;
         ++j;
-        if (!mbar_wait(smem_u32(&tmem_empty[buf]), tph ^ 1u)) timed_out = true;
+        if (!mbar_wait_spin(smem_u32(&tmem_empty[buf]), tph ^ 1u)) timed_out = true;
         tc_fence_after();
         const uint32_t d0 = tmem + buf * C::kAccCols;
         const uint32_t idesc = mma_idesc((k.cnt + 15) & ~15);
@@ -207,12 +207,12 @@ __global__ void __launch_bounds__(kPoolThreads, 1) gemm_pool_kernel(const __grid
           for (int st = 0; st < C::kStagesPerChunk; ++st, ++ia) {
             const int s = ia % AS;
             const uint32_t ph = uint32_t(ia / AS) & 1u;
-            if (!mbar_wait(smem_u32(&afull[s]), ph)) timed_out = true;
+            if (!mbar_wait_spin(smem_u32(&afull[s]), ph)) timed_out = true;
             int bs[APS];
 #pragma unroll
             for (int at = 0; at < APS; ++at, ++ib) {
               bs[at] = ib % BS;
-              if (!mbar_wait(smem_u32(&bfull[bs[at]]), uint32_t(ib / BS) & 1u)) timed_out = true;
+              if (!mbar_wait_spin(smem_u32(&bfull[bs[at]]), uint32_t(ib / BS) & 1u)) timed_out = true;
             }
             tc_fence_after();
             // the two accumulators alternate MMA by MMA, so neither waits on

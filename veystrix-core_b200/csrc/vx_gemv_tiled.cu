@@ -1,10 +1,14 @@
 // Grouped Q4 GEMV over the tiled expert pool (sm_100a).
 //
-// Same arithmetic as the MLX-layout kernel (vx_gemv_mma.cu: mma.sync
-// m16n8k16 with the block-diagonal B, nibbles unpacked to 128+q by one lop3,
-// MLX's qmv formula per group folded into the epilogue), but every operand
-// arrives by bulk copy from records laid out in the order the warp consumes
-// them.
+// The MLX-layout kernel's scheme (vx_gemv_mma.cu: mma.sync m16n8k16 with the
+// block-diagonal B, MLX's qmv formula per group folded into the epilogue),
+// but every operand arrives by bulk copy from records laid out in the order
+// the warp consumes them.  The down projection unpacks nibbles to bf16 128+q
+// by one lop3 (and a shift) per pair, as the MLX-layout kernel does; the
+// gate/up projections, which read act_records_kernel's f16 records, unpack
+// to f16 subnormals q * 2^-24 and 16q * 2^-24 by one mask per pair and one
+// shift per word (the kernel is bound by the ALU pipe, and the unpack is most
+// of its ALU work).  Both forms give exact products q * x.
 //
 // Weight records (the pool, re-tiled once at load time).  One record = one
 // warp's 128-input chunk of one row tile:
@@ -32,6 +36,8 @@
 // tasks, so the copies of the next task start while the current one is
 // being consumed.  Records out of range (rows >= out, groups >= in/32) hold
 // zeros and add exactly zero.
+#include <cuda_fp16.h>
+
 #include <type_traits>
 
 #include "vx_async.cuh"
@@ -112,6 +118,8 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
     gemv_tiled_kernel(const __grid_constant__ TiledArgs a) {
   chain_wait();
   constexpr int NP = GATEUP ? 2 : 1;
+  // gate/up reads act_records_kernel's f16 records; down reads h in bf16
+  constexpr bool F16 = GATEUP && kActF16;
   constexpr int kRec = NP * MT * kTileRecordUnit;
   constexpr int kWBytes = NP * MT * 1024;
   constexpr int kXOff = kRec;                       // [token][kActRecord]
@@ -218,7 +226,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
       parity_bits ^= 1u << st_use;
 
       uint32_t bq[NQ][16];
-      float xs[NQ][2];
+      float xs[NQ][2], xinv[NQ];
 #pragma unroll
       for (int q = 0; q < NQ; ++q) {
         const bool live = xa[q] != 0xFFFFFFFFu;
@@ -239,6 +247,11 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
             mma16816(d, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u, bq[q][2 * mm], bq[q][2 * mm + 1]);
           xs[q][0] = d[0];
           xs[q][1] = d[1];
+        } else if (F16) {
+          const uint2 v = lds64(st + xsa[q]);
+          xs[q][0] = __uint_as_float(v.x);
+          xs[q][1] = __uint_as_float(v.y);
+          xinv[q] = __uint_as_float(lds64(st + xsa[q] - (c & 1) * 8 + 16).x);
         } else {
           const uint2 v = lds64(st + xsa[q]);
           xs[q][0] = __uint_as_float(v.x);
@@ -261,6 +274,22 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
 #pragma unroll
           for (int mm = 0; mm < 8; mm += 2) {
             const int wi = mm >> 1;
+            if constexpr (F16) {
+              // four masks and one shift per word: f16 subnormals q * 2^-24
+              // (f0 f1 h0 h1) and 16q * 2^-24 (f2 f3 h2 h3, against B rows
+              // k >= 8, whose activations are stored / 16)
+              const uint32_t g8 = ag[wi] >> 8, e8 = a8[wi] >> 8;
+              const uint32_t f0 = ag[wi] & 0x000F000Fu, f1 = a8[wi] & 0x000F000Fu;
+              const uint32_t f2 = ag[wi] & 0x00F000F0u, f3 = a8[wi] & 0x00F000F0u;
+              const uint32_t h0 = g8 & 0x000F000Fu, h1 = e8 & 0x000F000Fu;
+              const uint32_t h2 = g8 & 0x00F000F0u, h3 = e8 & 0x00F000F0u;
+#pragma unroll
+              for (int q = 0; q < NQ; ++q) {
+                mma16816_f16(d[q], f0, f1, f2, f3, bq[q][2 * mm], bq[q][2 * mm + 1]);
+                mma16816_f16(d[q], h0, h1, h2, h3, bq[q][2 * mm + 2], bq[q][2 * mm + 3]);
+              }
+              continue;
+            }
             const uint32_t f0 = nib_pair128(ag[wi]), f1 = nib_pair128(a8[wi]);
             const uint32_t f2 = nib_pair128(ag[wi] >> 4), f3 = nib_pair128(a8[wi] >> 4);
             const uint32_t h0 = nib_pair128(ag[wi] >> 8), h1 = nib_pair128(a8[wi] >> 8);
@@ -280,6 +309,18 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
             const float s1 = __uint_as_float(sw[2 * h] & 0xFFFF0000u);
             const float b0 = __uint_as_float(sw[2 * h + 1] << 16);
             const float b1 = __uint_as_float(sw[2 * h + 1] & 0xFFFF0000u);
+            if constexpr (F16) {
+#pragma unroll
+              for (int q = 0; q < NQ; ++q) {
+                float v = acc[p][m][q][h];
+                v = fmaf(s0, d[q][2 * h] * xinv[q], v);
+                v = fmaf(b0, xs[q][0], v);
+                v = fmaf(s1, d[q][2 * h + 1] * xinv[q], v);
+                v = fmaf(b1, xs[q][1], v);
+                acc[p][m][q][h] = v;
+              }
+              continue;
+            }
             // bias - 128*scale: the lop3 operands carry q + 128.
             const float c0 = fmaf(-128.f, s0, b0);
             const float c1 = fmaf(-128.f, s1, b1);
@@ -347,13 +388,29 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
   if (timed_out && a.err) atomicOr(a.err, 0x100);
 }
 
-// ---- activation records ------------------------------------------------------
+// ---- activation records ----------------------------------------------------
 
-// One thread per 8-input block of a (position, chunk): reads the token's x,
-// writes the block in B order at lane-order slot (i*4 + c) and, for the first
-// block of each group, the group sum - computed exactly as the MLX-layout
-// path computes it (left-to-right over 8 inputs, then (s0+s1)+(s2+s3)), so the
-// two paths stay bit-identical.
+// One thread per 8-input block of a (position, chunk); the record's 16 blocks
+// are 16 consecutive threads.  The block goes to lane-order slot (i*4 + c) in
+// B order (words (x0,x4) (x1,x5) (x2,x6) (x3,x7)) as f16, for the f16 unpack
+// of the gate/up GEMV (kActF16), whose weights enter the MMA as f16
+// subnormals q * 2^-24 (nibbles at bits 0-3) or 16q * 2^-24 (bits 4-7, no
+// shift):
+//
+//   * the record is scaled by 2^e, e chosen from its largest |x| so that it
+//     lands in [2^13, 2^14): every bf16 input converts exactly (f16 keeps 11
+//     significant bits) unless it is 2^-23 of the largest or smaller;
+//   * words 1 and 3 of each slot meet the 16q weights (B rows k = 8..15 of
+//     an MMA): those values are stored divided by 16 (exact), so every
+//     product is q * x * 2^(e-24);
+//   * the tail holds the plain sum of each group's 32 inputs at kActXsum +
+//     4g (left to right over 8 inputs, then (s0+s1)+(s2+s3)), for the bias
+//     term, and 2^(24-e) at kActXsum + 16.
+//
+// A group's GEMV term is s * D * 2^(24-e) + b * sum, D the MMA sum: exact
+// products and an fp32 sum with no offset to cancel.  e stays at or above
+// -103 so that 2^(24-e) is a finite float: a record whose largest |x| is
+// 2^117 or more saturates to infinity.
 __global__ void act_records_kernel(const uint16_t* __restrict__ x, int64_t ldx, int K,
                                    const int32_t* __restrict__ src_rows, const int32_t* __restrict__ n_rows,
                                    int64_t rows, unsigned char* __restrict__ act) {
@@ -372,25 +429,43 @@ __global__ void act_records_kernel(const uint16_t* __restrict__ x, int64_t ldx, 
     const int64_t r = src_rows ? int64_t(__ldg(src_rows + p)) : p;
     v = *reinterpret_cast<const uint4*>(x + r * ldx + blk * 8);
   }
-  float s = 0.f;
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  float xv[8];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    s += __uint_as_float(w[j] << 16);
-    s += __uint_as_float(w[j] & 0xFFFF0000u);
+    xv[2 * j] = __uint_as_float(w[j] << 16);
+    xv[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+  }
+  float s = 0.f, m = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    s += xv[j];
+    m = fmaxf(m, fabsf(xv[j]));
   }
   s += __shfl_xor_sync(0xFFFFFFFFu, s, 1);
   s += __shfl_xor_sync(0xFFFFFFFFu, s, 2);
+#pragma unroll
+  for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+  int e = 0;
+  if (m > 0.f && isfinite(m)) {
+    int E;
+    frexpf(m, &E);   // m in [2^(E-1), 2^E)
+    e = max(14 - E, -103);
+  }
   if (!live) return;
   const int ch = blk >> 4, c = (blk >> 2) & 3, ib = blk & 3;
   unsigned char* rec = act + (int64_t(ch) * rows + p) * kActRecord;
+  uint16_t h[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) h[j] = __half_as_ushort(__float2half_rn(ldexpf(xv[j], (j & 1) ? e - 4 : e)));
   uint4 o;
-  o.x = prmt(v.x, v.z, 0x5410);   // (x0, x4)
-  o.y = prmt(v.x, v.z, 0x7632);   // (x1, x5)
-  o.z = prmt(v.y, v.w, 0x5410);   // (x2, x6)
-  o.w = prmt(v.y, v.w, 0x7632);   // (x3, x7)
+  o.x = h[0] | (uint32_t(h[4]) << 16);   // (x0, x4)
+  o.y = h[1] | (uint32_t(h[5]) << 16);   // (x1, x5) / 16: B rows k >= 8
+  o.z = h[2] | (uint32_t(h[6]) << 16);   // (x2, x6)
+  o.w = h[3] | (uint32_t(h[7]) << 16);   // (x3, x7) / 16
   *reinterpret_cast<uint4*>(rec + (ib * 4 + c) * 16) = o;
   if (ib == 0) *reinterpret_cast<float*>(rec + kActXsum + c * 4) = inside ? s : 0.f;
+  if (blk % 16 == 0) *reinterpret_cast<float*>(rec + kActXsum + 16) = ldexpf(1.f, 24 - e);
 }
 
 cudaError_t launch_act_records(const uint16_t* x, int64_t ldx, int K, const int32_t* src_rows,

@@ -97,6 +97,10 @@ constexpr int kTiledItemChunk = 4;
 // The 320-byte pitch puts the two tokens a B operand reads on disjoint banks.
 constexpr int kActRecord = 320;
 constexpr int kActXsum = 256;
+// act_records_kernel writes f16 records (scaled by a power of two per
+// record); the gate/up GEMV reads them with the f16 unpack.  h records
+// (down's input) stay bf16 with group sums formed on the tensor pipe.
+constexpr bool kActF16 = true;
 
 struct TiledArgs {
   int32_t* err;                 // bit 8 set when a pipeline wait ran out (may be null)
