@@ -597,6 +597,9 @@ def main():
     if world > 1:
         import datetime
         import torch.distributed as dist
+        # NCCL's communicator set-up lines (rank count per communicator) in the log
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
@@ -749,6 +752,14 @@ def main():
     stages = _lib.profile_read()
     _lib.profile_enable(False)
     barrier()
+    # under expert parallelism every rank's stage times (its timeline: router,
+    # dispatch, the wait for the other ranks' rows, the shard's kernels,
+    # combine), gathered on rank 0
+    per_rank_stages = None
+    if dist is not None:
+        mine = {k: round(v[1], 5) for k, v in stages.items()}
+        per_rank_stages = [None] * world
+        dist.all_gather_object(per_rank_stages, mine)
 
     # the two north-star shapes on the same rotating pools (single GPU)
     extra = None
@@ -828,6 +839,8 @@ def main():
         "clocks": clocks,
         "gpu_launches": launches_per_step * K,
     }
+    if per_rank_stages is not None:
+        line["stages_ms_per_rank"] = per_rank_stages
     if extra is not None:
         line.update(extra)
     print(json.dumps(line), flush=True)

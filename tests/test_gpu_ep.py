@@ -19,11 +19,11 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def _weights(dev, E=64, d=512, I=256):
+def _weights(dev, E=64, d=512, I=256, top_k=8):
     import vxmoe
     g = torch.Generator(device=dev)
     g.manual_seed(11)
-    return vxmoe.MoEWeights.random(E, d, I, I, 8, device=dev, generator=g)
+    return vxmoe.MoEWeights.random(E, d, I, I, top_k, device=dev, generator=g)
 
 
 def _bits(t):
@@ -185,6 +185,69 @@ def _worker(rank, port, q):
         q.put((rank, "ok", (worst, same_min, agree, errors), ""))
     except Exception as exc:
         q.put((rank, "error", repr(exc), traceback.format_exc()))
+
+
+def _worker_c4(rank, port, q):
+    """The C4 shape on two ranks: production width (512 experts, d = 2048,
+    I = 512, top-10) on the packed pool, 2,048 tokens per rank, so each
+    shard's experts run the tcgen05 GEMM; the peer transport sized for the
+    whole batch.  Compared with the single-GPU block on the full weights."""
+    try:
+        import torch.distributed as dist
+        import vxmoe
+        from vxmoe import ep as E
+        dev = torch.device("cuda", rank)
+        torch.cuda.set_device(dev)
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        dist.init_process_group("nccl", rank=rank, world_size=2,
+                                timeout=datetime.timedelta(seconds=120), device_id=dev)
+        w = _weights(dev, E=512, d=2048, I=512, top_k=10)
+        w.pack()
+        shard = E.shard_weights(w, rank, 2)
+        shard.pack()
+        ep = E.ExpertParallelMoE(shard, w.num_experts, transport="p2p", capacity=2048)
+        g = torch.Generator(device=dev)
+        g.manual_seed(300 + rank)
+        x = torch.randn((2048, w.hidden), device=dev, generator=g).to(torch.bfloat16)
+        y = ep(x)
+        ref = vxmoe.moe_block(x, w)
+        torch.cuda.synchronize()
+        yn, rn = y.float().cpu().numpy(), ref.float().cpu().numpy()
+        worst = float(np.linalg.norm(yn - rn) / np.linalg.norm(rn))
+        same = float(np.mean(_bits(y) == _bits(ref)))
+        errors = ep.exchange.errors()
+        E.close_exchanges()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, "ok", (worst, same, errors), ""))
+    except Exception as exc:
+        q.put((rank, "error", repr(exc), traceback.format_exc()))
+
+
+def _run_two(target, port):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=target, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=600) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=60)
+    return res
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs two GPUs")
+def test_ep_two_gpus_c4_shape_match_single_gpu_block():
+    for rank, status, a, b in _run_two(_worker_c4, 29671):
+        assert status == "ok", b
+        worst, same, errors = a
+        assert errors == 0, f"rank {rank}: a wait ran out ({errors})"
+        # the same per-expert GEMMs and the same slot-order combine: almost every bit
+        assert worst < 1e-3, f"rank {rank} normwise difference {worst}"
+        assert same > 0.95, f"rank {rank} only {same:.3f} identical"
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
