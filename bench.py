@@ -599,7 +599,6 @@ def main():
         import torch.distributed as dist
         # NCCL's communicator set-up lines (rank count per communicator) in the log
         os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))

@@ -933,6 +933,7 @@ int vx_ep_dispatch(const vx_ep_comm* comm, const uint16_t* x, int32_t T, const i
   if (T == 0) return VX_OK;
   if (!x || !inds || !weights || !aligned16(x)) return VX_EINVAL_SHAPE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  profile_mark(st, "");
   cudaError_t e = launch_ep_dispatch(a, x, inds, weights, st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
   profile_mark(st, "ep_dispatch");
@@ -976,6 +977,7 @@ int vx_ep_experts(const vx_ep_comm* comm, int32_t T, const vx_moe_weights* W, vo
   if (T == 0) return VX_OK;
   if (!workspace || workspace_bytes < vx_ep_experts_workspace(comm, T, W)) return VX_EWORKSPACE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  profile_mark(st, "");
   const int rows = T * comm->world;
   Carver c(workspace);
   ExpertScratch es = carve_experts(c, rows, dm);
@@ -1003,6 +1005,7 @@ int vx_ep_combine(const vx_ep_comm* comm, int32_t T, const int32_t* inds, const 
   if (T == 0) return VX_OK;
   if (!inds || !y) return VX_EINVAL_SHAPE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  profile_mark(st, "");
   cudaError_t e = launch_ep_combine(a, inds, shared, shared_gate, y, st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
   profile_mark(st, "ep_combine");
