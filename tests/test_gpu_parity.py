@@ -245,6 +245,33 @@ def test_router_full_production(prod_params):
     assert ulp_diff_bf16(np32(r.shared_gate), O.sigmoid_bf16(z)).max() <= 1
 
 
+@pytest.mark.parametrize("biased", [False, True])
+def test_router_tiled_prefill_equals_fused(prod_params, biased):
+    """Batches of 256 tokens or more take the tiled logits kernel and the
+    separate softmax/top-k kernel; smaller ones the fused single launch.  The
+    two sum the logits in the same order, so a 600-token batch must give the
+    bits of the same tokens routed in 200-token pieces: logits, ids, weights
+    and the shared-expert gate."""
+    import vxmoe
+    p = prod_params
+    w = weights_from_oracle(p)
+    if biased:
+        bias = np.zeros(512, np.float32)
+        bias[np.random.default_rng(4).choice(512, 32, replace=False)] = 2.0
+        w.router_bias = torch.from_numpy(bias).to(torch.bfloat16).to(DEV)
+    x = bf16_t(O.make_x(8, 600, 2048))
+    whole = vxmoe.router(x, w)
+    parts = [vxmoe.router(x[a:a + 200], w) for a in (0, 200, 400)]
+    torch.cuda.synchronize()
+    for name in ("logits", "inds", "weights", "shared_gate"):
+        got = getattr(whole, name)
+        exp = torch.cat([getattr(r, name) for r in parts])
+        np.testing.assert_array_equal(got.view(torch.int16).cpu().numpy() if got.dtype == torch.bfloat16
+                                      else got.cpu().numpy(),
+                                      exp.view(torch.int16).cpu().numpy() if exp.dtype == torch.bfloat16
+                                      else exp.cpu().numpy(), err_msg=name)
+
+
 # ---------------------------------------------------------------- permutation
 
 @pytest.mark.parametrize("P,E,skew", [(0, 8, False), (1, 8, False), (10, 512, False),

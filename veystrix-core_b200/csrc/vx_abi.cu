@@ -609,18 +609,24 @@ size_t vx_router_workspace(int32_t T, const vx_moe_weights* W) {
   return c.size();
 }
 
-// One launch: logits, top-k and renorm by the last CTA of each token block,
-// and the shared-expert gate (vx_router.cu router_fused_kernel).
+// Decode-sized batches: one launch - logits, top-k and renorm by the last CTA
+// of each token block, and the shared-expert gate (vx_router.cu
+// router_fused_kernel).  Prefill-sized batches: the tiled logits kernel and
+// the softmax/top-k kernel (the same bits).
 static int router_impl(const uint16_t* x, int T, const vx_moe_weights* W, const BlockDims& dm,
                        uint16_t* logits, int32_t* inds, uint16_t* weights, uint16_t* sg,
                        int32_t* counters, cudaStream_t st, const PermSmallArgs* perm = nullptr,
                        bool counters_zeroed = false) {
   profile_mark(st, "");
   const bool gate = sg && W->shared_expert_gate.w;
-  cudaError_t e = launch_router_fused(x, T, W->router_w, dm.E, dm.d, dm.k,
-                                      gate ? &W->shared_expert_gate : nullptr, logits, inds, weights,
-                                      gate ? sg : nullptr, counters, perm, W->router_bias, st,
-                                      counters_zeroed);
+  cudaError_t e;
+  if (!perm && router_tiled_fits(T, dm.d))   // prefill-sized batch: tiled logits, then top-k
+    e = launch_router_tiled(x, T, W->router_w, dm.E, dm.d, dm.k, gate ? &W->shared_expert_gate : nullptr,
+                            logits, inds, weights, gate ? sg : nullptr, W->router_bias, st);
+  else
+    e = launch_router_fused(x, T, W->router_w, dm.E, dm.d, dm.k, gate ? &W->shared_expert_gate : nullptr,
+                            logits, inds, weights, gate ? sg : nullptr, counters, perm, W->router_bias, st,
+                            counters_zeroed);
   if (e != cudaSuccess) return vx_cuda_fail(e);
   profile_mark(st, "router");
   return VX_OK;

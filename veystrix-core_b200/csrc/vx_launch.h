@@ -230,6 +230,15 @@ cudaError_t launch_softmax_topk(const uint16_t* logits, int T, int E, int k, int
 // caller cleared them earlier on the stream (counters_zeroed).
 inline int64_t router_counters(int64_t T) { return (T + 7) / 8 + 1; }
 struct PermSmallArgs;
+// Prefill-sized batches (T >= kRouterTiledMinT, K <= 2048): logits by
+// 64 x 64 tiles staged in shared memory (the same bits as the fused kernel),
+// then the softmax/top-k kernel; the shared-expert gate in an extra CTA
+// column.  No counters, no permutation.
+constexpr int kRouterTiledMinT = 256;
+bool router_tiled_fits(int T, int K);
+cudaError_t launch_router_tiled(const uint16_t* x, int T, const uint16_t* wg, int E, int K, int k,
+                                const vx_q4* seg, uint16_t* logits, int32_t* inds, uint16_t* weights,
+                                uint16_t* sg, const uint16_t* bias, cudaStream_t st);
 cudaError_t launch_router_fused(const uint16_t* x, int T, const uint16_t* wg, int E, int K, int k,
                                 const vx_q4* seg, uint16_t* logits, int32_t* inds, uint16_t* weights,
                                 uint16_t* sg, int32_t* counters, const PermSmallArgs* perm,
