@@ -232,8 +232,8 @@ inline int64_t router_counters(int64_t T) { return (T + 7) / 8 + 1; }
 struct PermSmallArgs;
 // Prefill-sized batches (T >= kRouterTiledMinT, K <= 2048): logits by
 // 64 x 64 tiles staged in shared memory (the same bits as the fused kernel),
-// then the softmax/top-k kernel; the shared-expert gate in an extra CTA
-// column.  No counters, no permutation.
+// then the softmax/top-k kernel and the shared-expert gate kernel.  No
+// counters, no permutation.
 constexpr int kRouterTiledMinT = 256;
 bool router_tiled_fits(int T, int K);
 cudaError_t launch_router_tiled(const uint16_t* x, int T, const uint16_t* wg, int E, int K, int k,

@@ -11,7 +11,7 @@
 // The result depends only on the ids, never on scheduling.
 //
 // Decode-sized inputs run all three phases in one CTA.  Prefill-sized inputs
-// (more than kPermMultiMin ids) split the ids into slices of kPermSlice: one
+// (more than kPermMultiMin ids) split the ids into slices (perm_slice): one
 // CTA per slice counts, one CTA scans the per-slice counts into per-slice
 // starting positions (slice order = flat order, so the sort stays stable),
 // and one CTA per slice scatters.
@@ -215,18 +215,28 @@ __global__ void __launch_bounds__(256) permute_small_kernel(
   perm_small(a, ids, P);
 }
 
-// ---- prefill-sized inputs: slices of kPermSlice ids -------------------------
+// ---- prefill-sized inputs: slices of perm_slice(P) ids ----------------------
 
-constexpr int kPermSlice = 8192;
+// Slices of 1,024 ids (one scatter chunk per CTA) up to 262,144 ids, then
+// the smallest multiple of 1,024 that keeps the count at most 256: enough
+// CTAs to cover the GPU at prefill sizes, and few enough slices for the
+// scan's per-expert walk over them.
 constexpr int64_t kPermMultiMin = 16384;
+
+static int64_t perm_slice(int64_t P) {
+  const int64_t unit = kPermThreads;
+  const int64_t mult = (P + unit * 256 - 1) / (unit * 256);
+  return unit * (mult > 1 ? mult : 1);
+}
 
 int64_t permute_scratch_ints(int64_t P, int E) {
   if (P <= kPermMultiMin) return 0;
-  return ((P + kPermSlice - 1) / kPermSlice) * int64_t(E);
+  return ((P + perm_slice(P) - 1) / perm_slice(P)) * int64_t(E);
 }
 
 __global__ void __launch_bounds__(kPermThreads) permute_count_kernel(const int32_t* __restrict__ ids,
-                                                                     int64_t P, int E, int32_t* __restrict__ blk,
+                                                                     int64_t P, int64_t slice, int E,
+                                                                     int32_t* __restrict__ blk,
                                                                      int32_t* __restrict__ err) {
   chain_begin();
   extern __shared__ int counts[];
@@ -234,8 +244,8 @@ __global__ void __launch_bounds__(kPermThreads) permute_count_kernel(const int32
   for (int e = threadIdx.x; e < E; e += kPermThreads) counts[e] = 0;
   if (threadIdx.x == 0) s_bad = 0;
   __syncthreads();
-  const int64_t lo = int64_t(blockIdx.x) * kPermSlice;
-  const int64_t hi = lo + kPermSlice < P ? lo + kPermSlice : P;
+  const int64_t lo = int64_t(blockIdx.x) * slice;
+  const int64_t hi = lo + slice < P ? lo + slice : P;
   const int bad = perm_count(ids, lo, hi, E, counts, &s_bad);
   for (int e = threadIdx.x; e < E; e += kPermThreads) blk[int64_t(blockIdx.x) * E + e] = counts[e];
   if (threadIdx.x == 0 && err && bad) atomicAdd(err, bad);
@@ -270,9 +280,9 @@ __global__ void __launch_bounds__(kPermThreads) permute_scan_kernel(
 }
 
 __global__ void __launch_bounds__(kPermThreads) permute_scatter_kernel(
-    const int32_t* __restrict__ ids, int64_t P, int E, int k_div, const int32_t* __restrict__ src_map,
-    const int32_t* __restrict__ blk, int32_t* __restrict__ order, int32_t* __restrict__ inverse,
-    int32_t* __restrict__ src_rows) {
+    const int32_t* __restrict__ ids, int64_t P, int64_t slice, int E, int k_div,
+    const int32_t* __restrict__ src_map, const int32_t* __restrict__ blk, int32_t* __restrict__ order,
+    int32_t* __restrict__ inverse, int32_t* __restrict__ src_rows) {
   chain_begin();
   extern __shared__ int smem[];
   int* running = smem;          // [E]
@@ -280,8 +290,8 @@ __global__ void __launch_bounds__(kPermThreads) permute_scatter_kernel(
   for (int e = threadIdx.x; e < E; e += kPermThreads) running[e] = blk[int64_t(blockIdx.x) * E + e];
   for (int i = threadIdx.x; i < kPermWarps * E; i += kPermThreads) hist[i] = 0;
   __syncthreads();
-  const int64_t lo = int64_t(blockIdx.x) * kPermSlice;
-  const int64_t hi = lo + kPermSlice < P ? lo + kPermSlice : P;
+  const int64_t lo = int64_t(blockIdx.x) * slice;
+  const int64_t hi = lo + slice < P ? lo + slice : P;
   perm_scatter(ids, lo, hi, E, k_div, src_map, running, hist, order, inverse, src_rows);
 }
 
@@ -307,9 +317,10 @@ cudaError_t launch_permute(const int32_t* ids, int64_t P, int E, int shared_item
                           shared_items, k_div, src_map, order, inverse, offsets, active, n_active,
                           src_rows, err, item_chunk, items, n_items);
   }
-  const int nb = int((P + kPermSlice - 1) / kPermSlice);
+  const int64_t slice = perm_slice(P);
+  const int nb = int((P + slice - 1) / slice);
   cudaError_t e = launch_chained(permute_count_kernel, dim3(nb), dim3(kPermThreads),
-                                 size_t(E) * sizeof(int), st, ids, P, E, blk, err);
+                                 size_t(E) * sizeof(int), st, ids, P, slice, E, blk, err);
   if (e != cudaSuccess) return e;
   e = launch_chained(permute_scan_kernel, dim3(1), dim3(kPermThreads), size_t(E) * 2 * sizeof(int), st,
                      nb, E, shared_items, blk, offsets, active, n_active, src_rows, item_chunk, items,
@@ -318,8 +329,8 @@ cudaError_t launch_permute(const int32_t* ids, int64_t P, int E, int shared_item
   const size_t smem = size_t(E) * (1 + kPermWarps) * sizeof(int);
   e = set_smem(reinterpret_cast<const void*>(permute_scatter_kernel), smem);
   if (e != cudaSuccess) return e;
-  return launch_chained(permute_scatter_kernel, dim3(nb), dim3(kPermThreads), smem, st, ids, P, E, k_div,
-                        src_map, blk, order, inverse, src_rows);
+  return launch_chained(permute_scatter_kernel, dim3(nb), dim3(kPermThreads), smem, st, ids, P, slice, E,
+                        k_div, src_map, blk, order, inverse, src_rows);
 }
 
 // Items of a gather_qmm call: item i = b*M + m has key rhs[b] and x row

@@ -299,118 +299,98 @@ __global__ void __launch_bounds__(32 * kRouterSlices) router_fused_kernel(
 // ---- prefill-sized batches: logits of a 64-expert x 64-token tile per CTA --
 // The fused kernel's tiles (16 experts x 8 tokens) re-read the router matrix
 // from L2 once per 8 tokens: at 2,048 tokens that is 512 MB of L2 traffic for
-// a 2 MB matrix.  Here a CTA stages one K slice of 64 expert rows and 64
-// token rows in shared memory (cp.async, double-buffered) and reuses each
-// row 4 or 16 times from there.  The arithmetic is the fused kernel's, in
-// its order: K cut into the same 8 slices of `per` 32-input steps, each
-// slice's MMAs (the same fragments: lane (g, c) takes inputs 8c..8c+7 of a
-// step from expert rows g, g+8 and token row g) summed from zero, the slice
-// sums added in slice order, then the bf16 rounding and the bias - so the
-// logits equal the fused kernel's bit for bit.  CTA column nEB computes the
-// shared-expert gate of its 64 tokens, as the fused kernel's extra column.
+// a 2 MB matrix.  Here a CTA stages 64 expert rows and 64 token rows, four
+// 32-input steps at a time (cp.async, double-buffered, 68 KB: three CTAs per
+// SM), and reuses each row 4 or 16 times from shared memory.  The arithmetic
+// is the fused kernel's, in its order: K cut into the same 8 slices of `per`
+// steps, each slice's MMAs (the same fragments: lane (g, c) takes inputs
+// 8c..8c+7 of a step from expert rows g, g+8 and token row g) summed from
+// zero, the slice sums (empty slices' zeros included) added in slice order,
+// then the bf16 rounding and the bias - so the logits equal the fused
+// kernel's bit for bit.
 constexpr int kRtRows = 64;   // experts and tokens per CTA tile
+constexpr int kRtSteps = 4;   // 32-input steps per staged chunk
+constexpr int kRtLd = kRtSteps * 32 + 8;   // bf16 per staged row (16-byte pad)
+constexpr size_t kRtSmem = size_t(2) * 2 * kRtRows * kRtLd * sizeof(uint16_t);
 
 __global__ void __launch_bounds__(256) router_tiled_kernel(const uint16_t* __restrict__ x, int T,
                                                            const uint16_t* __restrict__ wg, int E, int K,
-                                                           vx_q4 seg, uint16_t* __restrict__ logits,
-                                                           uint16_t* __restrict__ sg,
+                                                           uint16_t* __restrict__ logits,
                                                            const uint16_t* __restrict__ bias) {
   chain_begin();
-  const int nEB = (E + kRtRows - 1) / kRtRows;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t0 = blockIdx.y * kRtRows;
-  if (int(blockIdx.x) == nEB) {
-    // shared expert gate: warp w -> tokens t0 + 8w .. t0 + 8w + 7 (the fused kernel's arithmetic)
-    if (!sg || !seg.w) return;
-    const int G = K / 32;
-    for (int i = 0; i < 8; ++i) {
-      const int t = t0 + warp * 8 + i;
-      if (t >= T) break;
-      const uint16_t* xr = x + int64_t(t) * K;
-      float acc = 0.f;
-      for (int g = lane; g < G; g += 32) {
-        const uint4 w = __ldg(reinterpret_cast<const uint4*>(seg.w) + g);
-        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-        float q = 0.f, xs = 0.f;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const uint4 xv = __ldg(reinterpret_cast<const uint4*>(xr + g * 32 + c * 8));
-          const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-          for (int n = 0; n < 8; ++n) {
-            const float v = __uint_as_float((n & 1) ? (xw[n >> 1] & 0xFFFF0000u) : (xw[n >> 1] << 16));
-            q = fmaf(float(nibble(ws[c], n)), v, q);
-            xs += v;
-          }
-        }
-        acc += fmaf(bf16_to_f32(seg.scales[g]), q, bf16_to_f32(seg.biases[g]) * xs);
-      }
-      acc = warp_sum<32>(acc);
-      if (lane == 0) sg[t] = f32_to_bf16(sigmoid_bf16(bf16r(acc)));
-    }
-    return;
-  }
+  const int t0 = blockIdx.y * kRtRows, e0 = blockIdx.x * kRtRows;
   extern __shared__ __align__(16) unsigned char rt_smem[];
+  uint16_t* sw = reinterpret_cast<uint16_t*>(rt_smem);   // [2][64][kRtLd] expert rows
+  uint16_t* sx = sw + 2 * kRtRows * kRtLd;               // [2][64][kRtLd] token rows
   const int steps = K / 32;
-  const int per = (steps + kRouterSlices - 1) / kRouterSlices;   // 32-input steps per slice
-  const int width = per * 32;                                    // inputs per slice
-  const int ld = width + 8;                                      // bf16 per staged row (16-byte pad)
-  uint16_t* sw = reinterpret_cast<uint16_t*>(rt_smem);           // [2][64][ld] expert rows
-  uint16_t* sx = sw + 2 * kRtRows * ld;                          // [2][64][ld] token rows
-  const int e0 = blockIdx.x * kRtRows;
-  auto load = [&](int sl, int b) {
-    const int k0 = sl * width;
-    const int kw = min(width, K - k0);
-    if (kw <= 0) return;
-    const int chunks = kw / 8;
+  const int per = (steps + kRouterSlices - 1) / kRouterSlices;   // steps per slice
+  // stage steps c0 .. c0+n-1 into buffer b
+  auto load = [&](int c0, int n, int b) {
+    const int chunks = n * 4;   // 16-byte pieces per row
     for (int idx = threadIdx.x; idx < kRtRows * chunks; idx += blockDim.x) {
       const int r = idx / chunks, ch = idx - r * chunks;
       const int e = e0 + r, t = t0 + r;
-      const uint32_t dw = smem_u32(sw + (b * kRtRows + r) * ld + ch * 8);
-      const uint32_t dx = smem_u32(sx + (b * kRtRows + r) * ld + ch * 8);
-      cp16_if(dw, e < E ? wg + int64_t(e) * K + k0 + ch * 8 : wg, e < E ? 16 : 0, true);
-      cp16_if(dx, t < T ? x + int64_t(t) * K + k0 + ch * 8 : x, t < T ? 16 : 0, true);
+      const int k = c0 * 32 + ch * 8;
+      cp16_if(smem_u32(sw + (b * kRtRows + r) * kRtLd + ch * 8), e < E ? wg + int64_t(e) * K + k : wg,
+              e < E ? 16 : 0, true);
+      cp16_if(smem_u32(sx + (b * kRtRows + r) * kRtLd + ch * 8), t < T ? x + int64_t(t) * K + k : x,
+              t < T ? 16 : 0, true);
     }
+  };
+  // the chunk after (sl, c0): the next steps of the slice, else the first
+  // step of the next slice that has any (sl = kRouterSlices: none)
+  auto next_chunk = [&](int& sl, int& c0) {
+    c0 += kRtSteps;
+    if (c0 < min(steps, (sl + 1) * per)) return;
+    for (++sl; sl < kRouterSlices && sl * per >= steps; ++sl) {
+    }
+    c0 = sl * per;
   };
   const int g = lane >> 2, c = lane & 3;
   const int ew = (warp & 3) * 16, tw = (warp >> 2) * 32;
-  float tot[4][4];
+  float tot[4][4], part[4][4];
 #pragma unroll
   for (int j = 0; j < 4; ++j)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) tot[j][i] = 0.f;
-  load(0, 0);
+    for (int i = 0; i < 4; ++i) tot[j][i] = part[j][i] = 0.f;
+  if (steps > 0) load(0, min(kRtSteps, per), 0);
   cp_commit();
+  int q = 0;
   for (int sl = 0; sl < kRouterSlices; ++sl) {
-    const int b = sl & 1;
-    if (sl + 1 < kRouterSlices) load(sl + 1, b ^ 1);
-    cp_commit();
-    cp_wait<1>();
-    __syncthreads();
-    float part[4][4];
+    const int s_end = min(steps, (sl + 1) * per);
+    for (int c0 = sl * per; c0 < s_end; c0 += kRtSteps, ++q) {
+      int nsl = sl, nc0 = c0;
+      next_chunk(nsl, nc0);
+      if (nsl < kRouterSlices) load(nc0, min(kRtSteps, min(steps, (nsl + 1) * per) - nc0), (q + 1) & 1);
+      cp_commit();
+      cp_wait<1>();
+      __syncthreads();
+      const int b = q & 1;
+      const int ns = min(kRtSteps, s_end - c0);
+      const uint16_t* wa_row = sw + (b * kRtRows + ew + g) * kRtLd + c * 8;
+      const uint16_t* wb_row = wa_row + 8 * kRtLd;
+      const uint16_t* x_row = sx + (b * kRtRows + tw + g) * kRtLd + c * 8;
+      for (int ls = 0; ls < ns; ++ls) {
+        const uint4 wa = lds128(smem_u32(wa_row + ls * 32));
+        const uint4 wb = lds128(smem_u32(wb_row + ls * 32));
+        uint4 xb[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+        for (int j = 0; j < 4; ++j) xb[j] = lds128(smem_u32(x_row + j * 8 * kRtLd + ls * 32));
 #pragma unroll
-      for (int i = 0; i < 4; ++i) part[j][i] = 0.f;
-    const int ns = min(steps, (sl + 1) * per) - sl * per;
-    const uint16_t* wa_row = sw + (b * kRtRows + ew + g) * ld + c * 8;
-    const uint16_t* wb_row = wa_row + 8 * ld;
-    const uint16_t* x_row = sx + (b * kRtRows + tw + g) * ld + c * 8;
-    for (int ls = 0; ls < ns; ++ls) {
-      const uint4 wa = lds128(smem_u32(wa_row + ls * 32));
-      const uint4 wb = lds128(smem_u32(wb_row + ls * 32));
+        for (int j = 0; j < 4; ++j) mma16816(part[j], wa.x, wb.x, wa.y, wb.y, xb[j].x, xb[j].y);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint4 xb = lds128(smem_u32(x_row + j * 8 * ld + ls * 32));
-        mma16816(part[j], wa.x, wb.x, wa.y, wb.y, xb.x, xb.y);
-        mma16816(part[j], wa.z, wb.z, wa.w, wb.w, xb.z, xb.w);
+        for (int j = 0; j < 4; ++j) mma16816(part[j], wa.z, wb.z, wa.w, wb.w, xb[j].z, xb[j].w);
       }
+      __syncthreads();   // the buffer is read out before a later load refills it
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) tot[j][i] += part[j][i];
-    __syncthreads();   // the buffer is read out before the next load refills it
+      for (int i = 0; i < 4; ++i) {
+        tot[j][i] += part[j][i];
+        part[j][i] = 0.f;
+      }
   }
   // D[g][2c], D[g][2c+1], D[g+8][2c], D[g+8][2c+1] of each (16 experts, 8 tokens) tile
 #pragma unroll
@@ -434,16 +414,14 @@ cudaError_t launch_router_tiled(const uint16_t* x, int T, const uint16_t* wg, in
                                 uint16_t* sg, const uint16_t* bias, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
   if (k > kMaxK || !router_tiled_fits(T, K)) return cudaErrorInvalidValue;
-  const int steps = K / 32, per = (steps + kRouterSlices - 1) / kRouterSlices;
-  const size_t smem = size_t(2) * 2 * kRtRows * (per * 32 + 8) * sizeof(uint16_t);
-  cudaError_t e = cudaFuncSetAttribute(router_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  cudaError_t e = cudaFuncSetAttribute(router_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(kRtSmem));
   if (e != cudaSuccess) return e;
-  vx_q4 q{};
-  if (seg) q = *seg;
-  const dim3 grid((E + kRtRows - 1) / kRtRows + 1, (T + kRtRows - 1) / kRtRows);
-  e = launch_chained(router_tiled_kernel, grid, dim3(256), smem, st, x, T, wg, E, K, q, logits, sg, bias);
-  if (e != cudaSuccess) return e;
-  return launch_softmax_topk(logits, T, E, k, inds, nullptr, weights, nullptr, st);
+  const dim3 grid((E + kRtRows - 1) / kRtRows, (T + kRtRows - 1) / kRtRows);
+  e = launch_chained(router_tiled_kernel, grid, dim3(256), kRtSmem, st, x, T, wg, E, K, logits, bias);
+  if (e == cudaSuccess) e = launch_softmax_topk(logits, T, E, k, inds, nullptr, weights, nullptr, st);
+  if (e == cudaSuccess && seg && sg) e = launch_shared_gate(x, T, *seg, sg, st);
+  return e;
 }
 
 cudaError_t launch_router_fused(const uint16_t* x, int T, const uint16_t* wg, int E, int K, int k,
