@@ -110,6 +110,16 @@ typedef struct vx_moe_weights {
    * to bf16 again), or NULL.  The skewed-load benchmark configuration adds
    * +2.0 to the logits of its hot experts this way. */
   const uint16_t* router_bias;
+  /* Adaptive top-k (models/flashnext/adaptive_topk.py:44-51, :107-118,
+   * :224-233): with 0 < keep_mass < 1 a token keeps its leading top-k slots
+   * (descending probability) until their share of its top-k probability
+   * mass reaches keep_mass, and at least keep_min of them (clamped to
+   * 1..top_k); its other slots name its first expert with weight 0, so they
+   * add no expert reads, and the weights are renormalised over the kept
+   * mass.  keep_mass 0 (zero-initialised) or >= 1: every slot, the exact
+   * top-k. */
+  double keep_mass;
+  int32_t keep_min;
 } vx_moe_weights;
 
 #define VX_PATH_AUTO 0

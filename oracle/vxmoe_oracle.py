@@ -18,7 +18,9 @@ project):
 * Router: ``softmax(precise=True)`` over the bf16 gate logits, top-k,
   selected scores and their mass (``adaptive_topk.py:59-65``,
   ``compiled.py:60-64``); renormalisation ``scores / mass`` at blend 1.0
-  (``adaptive_topk.py:257-262``).
+  (``adaptive_topk.py:257-262``); adaptive top-k below threshold 1.0: the
+  keep rule ``_keep_for_mass`` and the dropped slots' masking
+  (``adaptive_topk.py:44-51``, ``:107-118``, ``:224-233``).
 * SwiGLU as MLX's bf16 sequence: ``t=exp(|g|)``, ``s=1/(1+t)``,
   ``sigma = g<0 ? s : 1-s``, ``silu=g*sigma``, ``h=silu*u``, every step
   rounded to bf16 (``metal_runtime.py:267-285``;
@@ -272,14 +274,52 @@ def renorm(scores, mass, blend: float = 1.0) -> np.ndarray:
     return bf16_round(scores / norm)
 
 
-def router(x, wg, k: int, logits=None, bias=None) -> RouterOut:
+def keep_for_mass(weights, threshold: float) -> int:
+    """``_keep_for_mass`` (``adaptive_topk.py:44-51``): the number of leading
+    weights whose running share of their sum first reaches ``threshold``,
+    in Python floats, left to right; all of them when none does."""
+    total = sum(float(w) for w in weights)
+    accumulated = 0.0
+    for position, weight in enumerate(weights):
+        accumulated += float(weight) / total
+        if accumulated >= threshold:
+            return position + 1
+    return len(weights)
+
+
+def adaptive_keep(inds, scores, threshold: float, min_keep: int = 1):
+    """Adaptive top-k (``adaptive_topk.py:107-118``, ``:224-233``) on slots in
+    descending order: per token keep = max(min(min_keep, k), keep_for_mass);
+    slots past it name the token's first expert with score 0.  Returns the
+    new ids, the masked scores and the keep counts.  Threshold 1.0 or more
+    keeps every slot."""
+    inds = np.array(inds)
+    scores = f32(scores).copy()
+    T, k = inds.shape
+    keeps = np.full(T, k, dtype=np.int64)
+    if threshold < 1.0:
+        lo = max(1, min(k, int(min_keep)))
+        for t in range(T):
+            keep = max(lo, keep_for_mass(scores[t], threshold))
+            keeps[t] = keep
+            inds[t, keep:] = inds[t, 0]
+            scores[t, keep:] = 0.0
+    return inds, scores, keeps
+
+
+def router(x, wg, k: int, logits=None, bias=None, threshold: float = 1.0, min_keep: int = 1) -> RouterOut:
     """Router chain of ``adaptive_topk.py:59-65`` plus renorm ``:257-262``.
 
     ``logits`` may be supplied (e.g. the device's own logits) to check the
     softmax/top-k stage on identical inputs.  ``bias`` ([E], bf16 values) is
     added to the bf16 logits before softmax/top-k and the sum rounded to bf16
     (the skewed-load benchmark's +2.0 on hot experts); supplied logits are
-    taken as already biased.
+    taken as already biased.  ``threshold`` < 1.0 runs adaptive top-k
+    (``adaptive_keep``): the top-k mass stays the sum over every slot, the
+    renorm divides by the kept mass (blend 1.0).  The slots are in descending
+    logit order (ties by expert id), a descending order of the bf16
+    probabilities; the reference sorts its scores with argsort, whose order
+    among equal bf16 probabilities is its own.
     """
     if logits is None:
         logits = router_logits(x, wg)
@@ -290,8 +330,9 @@ def router(x, wg, k: int, logits=None, bias=None) -> RouterOut:
     inds = topk_order(logits, k)
     scores = np.take_along_axis(probs, inds, axis=-1)
     mass = bf16_round(scores.sum(axis=-1, keepdims=True, dtype=np.float32))
-    weights = renorm(scores, mass, 1.0)
-    return RouterOut(logits, probs, inds, scores, mass, weights)
+    inds, kept, _ = adaptive_keep(inds, scores, threshold, min_keep)
+    weights = renorm(kept, mass, 1.0)
+    return RouterOut(logits, probs, inds, kept, mass, weights)
 
 
 # --------------------------------------------------------------------------
@@ -469,9 +510,9 @@ class BlockOut:
 
 
 def moe_block(x, p: MoEParams, semantics: str = "fused", logits=None,
-              path: str = "decode") -> BlockOut:
+              path: str = "decode", threshold: float = 1.0, min_keep: int = 1) -> BlockOut:
     """The routed sparse-MoE block ``_moe_call`` (``adaptive_topk.py:54-293``)
-    at threshold 1.0 and blend 1.0.
+    at blend 1.0; ``threshold`` < 1.0 runs adaptive top-k (``router``).
 
     ``semantics="fused"`` is the custom-executor combine (float32); the
     ``"generic"`` form is the bf16 combine of the MLX path.  ``path`` picks the
@@ -480,7 +521,7 @@ def moe_block(x, p: MoEParams, semantics: str = "fused", logits=None,
     ``expert_cache.py:2017-2037``, bf16-dequantised tiles).
     """
     x = bf16_round(x)
-    r = router(x, p.router_w, p.top_k, logits=logits)
+    r = router(x, p.router_w, p.top_k, logits=logits, threshold=threshold, min_keep=min_keep)
     shared, sg = shared_parts(x, p, path)
     shared_y = bf16_round(sg * shared)
     yd, h = routed_outputs(x, r.inds, p, path)
@@ -493,15 +534,33 @@ def moe_block(x, p: MoEParams, semantics: str = "fused", logits=None,
     return BlockOut(y, r, shared, sg, shared_y, yd, h)
 
 
-def moe_block_reference_f64(x, p: MoEParams, inds, logits) -> np.ndarray:
+def keeps_of(inds) -> np.ndarray:
+    """Keep counts of an adaptive routing (``adaptive_keep``): a token's top-k
+    ids are distinct, so the first slot after slot 0 that repeats slot 0's
+    expert is the first dropped one."""
+    inds = np.asarray(inds)
+    T, k = inds.shape
+    keeps = np.full(T, k, dtype=np.int64)
+    for t in range(T):
+        rep = np.nonzero(inds[t, 1:] == inds[t, 0])[0]
+        if rep.size:
+            keeps[t] = int(rep[0]) + 1
+    return keeps
+
+
+def moe_block_reference_f64(x, p: MoEParams, inds, logits, keeps=None) -> np.ndarray:
     """Unrounded reference of the block for a fixed routing: every stage in
     float64 from the same bf16 inputs and bf16 router logits.  This is the
-    "fp32 reference" that final outputs are compared with."""
+    "fp32 reference" that final outputs are compared with.  ``keeps``
+    (adaptive top-k): slots past a token's count weigh nothing and the
+    weights renormalise over the kept ones."""
     x = f32(x).astype(np.float64)
     l = f32(logits).astype(np.float64)
     e = np.exp(l - l.max(axis=-1, keepdims=True))
     probs = e / e.sum(axis=-1, keepdims=True)
     sc = np.take_along_axis(probs, inds, axis=-1)
+    if keeps is not None:
+        sc = sc * (np.arange(inds.shape[1])[None, :] < np.asarray(keeps)[:, None])
     w = sc / sc.sum(axis=-1, keepdims=True)
 
     def mlp(xx, gate, up, down):

@@ -622,11 +622,12 @@ static int router_impl(const uint16_t* x, int T, const vx_moe_weights* W, const 
   cudaError_t e;
   if (!perm && router_tiled_fits(T, dm.d))   // prefill-sized batch: tiled logits, then top-k
     e = launch_router_tiled(x, T, W->router_w, dm.E, dm.d, dm.k, gate ? &W->shared_expert_gate : nullptr,
-                            logits, inds, weights, gate ? sg : nullptr, W->router_bias, st);
+                            logits, inds, weights, gate ? sg : nullptr, W->router_bias, st, W->keep_mass,
+                            W->keep_min);
   else
     e = launch_router_fused(x, T, W->router_w, dm.E, dm.d, dm.k, gate ? &W->shared_expert_gate : nullptr,
                             logits, inds, weights, gate ? sg : nullptr, counters, perm, W->router_bias, st,
-                            counters_zeroed);
+                            counters_zeroed, W->keep_mass, W->keep_min);
   if (e != cudaSuccess) return vx_cuda_fail(e);
   profile_mark(st, "router");
   return VX_OK;
@@ -789,6 +790,8 @@ int vx_moe_block(const uint16_t* x, int32_t T, const vx_moe_weights* W, uint16_t
     a.x = x;
     a.router_w = W->router_w;
     a.router_bias = W->router_bias;
+    a.keep_mass = W->keep_mass;
+    a.keep_min = W->keep_min;
     if (dm.shared) a.seg = W->shared_expert_gate;
     a.gu_rec = static_cast<const unsigned char*>(pl.gate_up.records);
     a.gu_stride = tile_pool_bytes(1, dm.I, dm.d, 2, pl.gate_up.tile_rows);

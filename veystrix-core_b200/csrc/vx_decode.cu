@@ -687,12 +687,25 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const __grid_con
 
   // ---- routing: top-k ids per token (warp t), then the stable expert sort;
   // the renormalised weights are needed only by the combine and come later
-  if (warp < T) topk_select<PER, true>(a.logits + int64_t(warp) * E, E, k, tb.inds + warp * k);
+  // (adaptive top-k needs the probabilities to pick the kept slots: the
+  // whole of topk_row here, weights included)
+  const bool adapt = a.keep_mass > 0.0 && a.keep_mass < 1.0;
+  if (warp < T) {
+    if (adapt)
+      topk_row<PER, true>(a.logits + int64_t(warp) * E, E, k, tb.inds + warp * k, nullptr, tb.wts + warp * k,
+                          nullptr, a.keep_mass, a.keep_min);
+    else
+      topk_select<PER, true>(a.logits + int64_t(warp) * E, E, k, tb.inds + warp * k);
+  }
   __syncthreads();
   if (warp == 0) {
     const int P = pl.P;
     // ids outside [0, E) (a selection among NaN logits) are dropped, as the
-    // permutation drops them: no position, counted in the error word
+    // permutation drops them: no position, counted in the error word.  A
+    // slot that adaptive top-k dropped (it repeats its token's slot-0 expert
+    // with weight 0; top-k ids are otherwise distinct) gets no position
+    // either, and is no error: its zero-weighted term is left out of the
+    // combine, and an expert never holds more positions than tokens.
     uint32_t kv[2];
     int n_bad = 0;
 #pragma unroll
@@ -700,8 +713,9 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const __grid_con
       const int i = lane + 32 * r;
       const int e = i < P ? tb.inds[i] : -1;
       const bool ok = i < P && e >= 0 && e < E;
+      const bool dropped = ok && adapt && (i % k) != 0 && e == tb.inds[i - i % k];
       n_bad += (i < P && !ok) ? 1 : 0;
-      kv[r] = ok ? (uint32_t(e) << 6) | uint32_t(i) : 0xFFFFFFFFu;
+      kv[r] = ok && !dropped ? (uint32_t(e) << 6) | uint32_t(i) : 0xFFFFFFFFu;
       if (i < P) tb.posof[i] = -1;
     }
     n_bad = __reduce_add_sync(0xFFFFFFFFu, n_bad);
@@ -838,7 +852,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const __grid_con
   // the routing weights (topk_row's arithmetic), off the critical path: the
   // down owners need them for the combine, CTA 0 writes them out
   if (pl.td >= 0 || (blockIdx.x == 0 && a.w_out)) {
-    if (warp < T)
+    if (warp < T && !adapt)
       topk_weights<PER, true>(a.logits + int64_t(warp) * E, E, k, tb.inds + warp * k, tb.wts + warp * k);
     __syncthreads();
     if (blockIdx.x == 0 && a.w_out)

@@ -222,7 +222,7 @@ cudaError_t launch_shared_gate(const uint16_t* x, int T, const vx_q4& seg, uint1
                                cudaStream_t st);
 cudaError_t launch_softmax_topk(const uint16_t* logits, int T, int E, int k, int32_t* inds,
                                 uint16_t* scores, uint16_t* weights, uint16_t* mass,
-                                cudaStream_t st);
+                                cudaStream_t st, double keep_mass = 0.0, int keep_min = 1);
 // Logits, top-k/renorm, (seg != null) the shared-expert gate and (perm !=
 // null; T*k <= kPermSmall) the expert sort of the routes in one launch;
 // bias (bf16 [E] or null) is added to the bf16 logits; counters:
@@ -238,11 +238,13 @@ constexpr int kRouterTiledMinT = 256;
 bool router_tiled_fits(int T, int K);
 cudaError_t launch_router_tiled(const uint16_t* x, int T, const uint16_t* wg, int E, int K, int k,
                                 const vx_q4* seg, uint16_t* logits, int32_t* inds, uint16_t* weights,
-                                uint16_t* sg, const uint16_t* bias, cudaStream_t st);
+                                uint16_t* sg, const uint16_t* bias, cudaStream_t st, double keep_mass = 0.0,
+                                int keep_min = 1);
 cudaError_t launch_router_fused(const uint16_t* x, int T, const uint16_t* wg, int E, int K, int k,
                                 const vx_q4* seg, uint16_t* logits, int32_t* inds, uint16_t* weights,
                                 uint16_t* sg, int32_t* counters, const PermSmallArgs* perm,
-                                const uint16_t* bias, cudaStream_t st, bool counters_zeroed = false);
+                                const uint16_t* bias, cudaStream_t st, bool counters_zeroed = false,
+                                double keep_mass = 0.0, int keep_min = 1);
 
 // The whole block for at most kDecodeMaxT tokens in one cooperative launch
 // (vx_decode.cu): weights from the tiled pool (gate/up records of 16 rows,
@@ -273,6 +275,8 @@ struct DecodeArgs {
   uint16_t* w_out;                    // may be null
   uint64_t wait_ns;
   int smem_bytes;                     // set by the launcher
+  double keep_mass;                   // adaptive top-k (vx_moe_weights.keep_mass)
+  int keep_min;
 };
 
 bool decode_supported(int T, int E, int d, int k, int I, int Is, int gu_tile_rows, int dn_tile_rows);

@@ -121,12 +121,13 @@ __global__ void __launch_bounds__(256) softmax_topk_kernel(const uint16_t* __res
                                                            int32_t* __restrict__ inds,
                                                            uint16_t* __restrict__ scores,
                                                            uint16_t* __restrict__ weights,
-                                                           uint16_t* __restrict__ mass) {
+                                                           uint16_t* __restrict__ mass, double keep_mass,
+                                                           int keep_min) {
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (t >= T) return;
   topk_row<PER, false>(logits + int64_t(t) * E, E, k, inds + int64_t(t) * k,
                        scores ? scores + int64_t(t) * k : nullptr, weights + int64_t(t) * k,
-                       mass ? mass + t : nullptr);
+                       mass ? mass + t : nullptr, keep_mass, keep_min);
 }
 
 template <class F>
@@ -140,12 +141,13 @@ static void per_width(int E, F&& f) {
 
 cudaError_t launch_softmax_topk(const uint16_t* logits, int T, int E, int k, int32_t* inds,
                                 uint16_t* scores, uint16_t* weights, uint16_t* mass,
-                                cudaStream_t st) {
+                                cudaStream_t st, double keep_mass, int keep_min) {
   if (T == 0) return cudaSuccess;
   if (k > kMaxK) return cudaErrorInvalidValue;
   const int grid = (T + 7) / 8;
   per_width(E, [&](auto per) {
-    softmax_topk_kernel<decltype(per)::value><<<grid, 256, 0, st>>>(logits, T, E, k, inds, scores, weights, mass);
+    softmax_topk_kernel<decltype(per)::value>
+        <<<grid, 256, 0, st>>>(logits, T, E, k, inds, scores, weights, mass, keep_mass, keep_min);
   });
   return cudaGetLastError();
 }
@@ -165,7 +167,7 @@ __global__ void __launch_bounds__(32 * kRouterSlices) router_fused_kernel(
     const uint16_t* __restrict__ x, int T, const uint16_t* __restrict__ wg, int E, int K, int k, vx_q4 seg,
     uint16_t* __restrict__ logits, int32_t* __restrict__ inds, uint16_t* __restrict__ weights,
     uint16_t* __restrict__ sg, int32_t* __restrict__ counters, PermSmallArgs perm,
-    const uint16_t* __restrict__ bias) {
+    const uint16_t* __restrict__ bias, double keep_mass, int keep_min) {
   chain_begin();
   const int nEB = (E + 15) / 16;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -270,7 +272,7 @@ __global__ void __launch_bounds__(32 * kRouterSlices) router_fused_kernel(
   const int t = t0 + warp;
   if (t < T)
     topk_row<PER, true>(logits + int64_t(t) * E, E, k, inds + int64_t(t) * k, nullptr, weights + int64_t(t) * k,
-                        nullptr);
+                        nullptr, keep_mass, keep_min);
   if (perm.order) {
     // decode-sized batch: the last token block to finish also sorts the
     // routes by expert, saving the permutation's own launch.  Second arrival
@@ -411,7 +413,8 @@ bool router_tiled_fits(int T, int K) { return T >= kRouterTiledMinT && K <= 2048
 
 cudaError_t launch_router_tiled(const uint16_t* x, int T, const uint16_t* wg, int E, int K, int k,
                                 const vx_q4* seg, uint16_t* logits, int32_t* inds, uint16_t* weights,
-                                uint16_t* sg, const uint16_t* bias, cudaStream_t st) {
+                                uint16_t* sg, const uint16_t* bias, cudaStream_t st, double keep_mass,
+                                int keep_min) {
   if (T == 0) return cudaSuccess;
   if (k > kMaxK || !router_tiled_fits(T, K)) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(router_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -419,7 +422,8 @@ cudaError_t launch_router_tiled(const uint16_t* x, int T, const uint16_t* wg, in
   if (e != cudaSuccess) return e;
   const dim3 grid((E + kRtRows - 1) / kRtRows, (T + kRtRows - 1) / kRtRows);
   e = launch_chained(router_tiled_kernel, grid, dim3(256), kRtSmem, st, x, T, wg, E, K, logits, bias);
-  if (e == cudaSuccess) e = launch_softmax_topk(logits, T, E, k, inds, nullptr, weights, nullptr, st);
+  if (e == cudaSuccess)
+    e = launch_softmax_topk(logits, T, E, k, inds, nullptr, weights, nullptr, st, keep_mass, keep_min);
   if (e == cudaSuccess && seg && sg) e = launch_shared_gate(x, T, *seg, sg, st);
   return e;
 }
@@ -427,7 +431,8 @@ cudaError_t launch_router_tiled(const uint16_t* x, int T, const uint16_t* wg, in
 cudaError_t launch_router_fused(const uint16_t* x, int T, const uint16_t* wg, int E, int K, int k,
                                 const vx_q4* seg, uint16_t* logits, int32_t* inds, uint16_t* weights,
                                 uint16_t* sg, int32_t* counters, const PermSmallArgs* perm,
-                                const uint16_t* bias, cudaStream_t st, bool counters_zeroed) {
+                                const uint16_t* bias, cudaStream_t st, bool counters_zeroed,
+                                double keep_mass, int keep_min) {
   if (T == 0) return cudaSuccess;
   if (k > kMaxK) return cudaErrorInvalidValue;
   const int nTB = (T + 7) / 8, nEB = (E + 15) / 16;
@@ -446,7 +451,7 @@ cudaError_t launch_router_fused(const uint16_t* x, int T, const uint16_t* wg, in
   dim3 grid(nEB + 1, nTB);
   per_width(E, [&](auto per) {
     e = launch_chained(router_fused_kernel<decltype(per)::value>, grid, dim3(32 * kRouterSlices), 0, st, x, T,
-                       wg, E, K, k, q, logits, inds, weights, sg, counters, pa, bias);
+                       wg, E, K, k, q, logits, inds, weights, sg, counters, pa, bias, keep_mass, keep_min);
   });
   return e;
 }

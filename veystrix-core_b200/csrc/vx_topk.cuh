@@ -31,9 +31,34 @@ VX_DEVICE float key_logit(uint32_t key) {
   return bf16_to_f32(uint16_t(b));
 }
 
+// Adaptive top-k (models/flashnext/adaptive_topk.py:44-51, :107-118,
+// :224-233): a token keeps the smallest number of its leading slots whose
+// share of its top-k probability mass reaches keep_mass - the running sum of
+// p_r / sum(p), in double precision and slot order, as the reference's
+// Python loop computes it - and at least keep_min (clamped to 1..k).
+// keep_mass outside (0, 1) keeps every slot.  Lane r holds slot r's
+// probability; every lane returns the same count.
+__device__ __forceinline__ int topk_keep(float my_p, int k, double keep_mass, int keep_min) {
+  if (!(keep_mass > 0.0 && keep_mass < 1.0)) return k;
+  double total = 0.0;
+  for (int r = 0; r < k; ++r) total += double(__shfl_sync(0xFFFFFFFFu, my_p, r));
+  double acc = 0.0;
+  int keep = k;
+  for (int r = 0; r < k; ++r) {
+    acc += double(__shfl_sync(0xFFFFFFFFu, my_p, r)) / total;
+    if (acc >= keep_mass) {
+      keep = r + 1;
+      break;
+    }
+  }
+  const int lo = keep_min < 1 ? 1 : (keep_min > k ? k : keep_min);
+  return keep > lo ? keep : lo;
+}
+
 template <int PER, bool COHERENT>
 __device__ __forceinline__ void topk_row(const uint16_t* lr, int E, int k, int32_t* inds, uint16_t* scores,
-                                         uint16_t* weights, uint16_t* mass) {
+                                         uint16_t* weights, uint16_t* mass, double keep_mass = 0.0,
+                                         int keep_min = 1) {
   const int lane = threadIdx.x & 31;
   // Lane owns experts lane*PER .. lane*PER+PER-1 and fetches them with one
   // or a few vector loads, all issued before any is used (a chain of 2-byte
@@ -103,18 +128,29 @@ __device__ __forceinline__ void topk_row(const uint16_t* lr, int E, int k, int32
       }
     }
   }
-  const int my_i = int(0xFFFFu - (my_key & 0xFFFFu));
+  int my_i = int(0xFFFFu - (my_key & 0xFFFFu));
   const float my_p = bf16r(__fmul_rn(expf(__fsub_rn(key_logit(my_key), m)), inv));
   float tot = 0.f;
   for (int r = 0; r < k; ++r) tot = __fadd_rn(tot, __shfl_sync(0xFFFFFFFFu, my_p, r));
-  // mass and renorm (blend 1.0): norm = mass + 1.0*(sum - mass), in bf16.
+  // adaptive top-k: slots past the token's keep count repeat slot 0's expert
+  // with probability 0 (every slot is kept unless 0 < keep_mass < 1)
+  const int keep = topk_keep(my_p, k, keep_mass, keep_min);
+  const int id0 = __shfl_sync(0xFFFFFFFFu, my_i, 0);
+  const float kept_p = lane < keep ? my_p : 0.f;
+  if (lane >= keep) my_i = id0;
+  float sel = tot;
+  if (keep < k) {
+    sel = 0.f;
+    for (int r = 0; r < k; ++r) sel = __fadd_rn(sel, __shfl_sync(0xFFFFFFFFu, kept_p, r));
+  }
+  // mass and renorm (blend 1.0): norm = mass + 1.0*(selected - mass), in bf16.
   const float msum = bf16r(tot);
-  const float diff = bf16r(__fsub_rn(msum, msum));
+  const float diff = bf16r(__fsub_rn(bf16r(sel), msum));
   const float norm = bf16r(__fadd_rn(msum, bf16r(diff)));
   if (lane < k) {
     inds[lane] = my_i;
-    if (scores) scores[lane] = f32_to_bf16(my_p);
-    weights[lane] = f32_to_bf16(bf16r(__fdiv_rn(my_p, norm)));
+    if (scores) scores[lane] = f32_to_bf16(kept_p);
+    weights[lane] = f32_to_bf16(bf16r(__fdiv_rn(kept_p, norm)));
   }
   if (mass && lane == 0) *mass = f32_to_bf16(msum);
 }

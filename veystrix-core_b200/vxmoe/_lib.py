@@ -62,6 +62,8 @@ class VxMoEWeights(ctypes.Structure):
         ("pool", ctypes.POINTER(VxMoEPool)),
         ("expert_path", c_int32),
         ("router_bias", c_void_p),
+        ("keep_mass", ctypes.c_double),
+        ("keep_min", c_int32),
     ]
 
 

@@ -220,6 +220,13 @@ class MoEWeights:
         # bf16 [E] added to the bf16 router logits (None: no bias); the
         # skewed-load benchmark puts +2.0 on its hot experts this way
         self.router_bias: Optional[torch.Tensor] = None
+        # adaptive top-k, the layer's threshold and minimum keep
+        # (adaptive_topk.py set_threshold / set_min_keep, per layer as its
+        # _LAYER_THRESHOLDS): below 1.0 a token keeps its leading slots until
+        # they hold this share of its top-k probability mass, at least
+        # min_keep; 1.0 routes every slot (the exact top-k, the default)
+        self.threshold: float = 1.0
+        self.min_keep: int = 1
 
     def pack(self, down_rows: int = 32) -> "MoEWeights":
         """Re-tile the experts into the resident pool the decode kernels
@@ -264,6 +271,7 @@ class MoEWeights:
         if self.router_bias is not None:   # one value per router row (all experts of the layer)
             n_router = int(self.router_w.shape[0]) if self.router_w is not None else self.num_experts
             s.router_bias = _ptr(_bias(self.router_bias, n_router))
+        _set_keep(s, self.threshold, self.min_keep)
         return s
 
     def nbytes_per_expert(self) -> int:
@@ -495,7 +503,18 @@ def router(x: torch.Tensor, weights: MoEWeights) -> RouterOut:
     """Router of the block: bf16 logits, top-k, renormalised weights and the
     shared expert's sigmoid gate."""
     return route(x, weights.router_w, weights.top_k, weights.shared_expert_gate,
-                 router_bias=weights.router_bias)
+                 router_bias=weights.router_bias, threshold=weights.threshold,
+                 min_keep=weights.min_keep)
+
+
+def _set_keep(s: VxMoEWeights, threshold: float, min_keep: int) -> None:
+    """Adaptive top-k settings of a weights struct: keep_mass 0 routes every
+    slot (threshold 1.0 or more, the reference's exact path)."""
+    t = float(threshold)
+    if not (t > 0.0):
+        raise ValueError(f"routing threshold must be positive, got {threshold}")
+    s.keep_mass = t if t < 1.0 else 0.0
+    s.keep_min = max(1, int(min_keep))
 
 
 def _bias(b: torch.Tensor, E: int) -> torch.Tensor:
@@ -510,10 +529,12 @@ def _bias(b: torch.Tensor, E: int) -> torch.Tensor:
 
 def route(x: torch.Tensor, router_w: torch.Tensor, top_k: int,
           shared_expert_gate: Optional[Q4Projection] = None,
-          router_bias: Optional[torch.Tensor] = None) -> RouterOut:
+          router_bias: Optional[torch.Tensor] = None, threshold: float = 1.0,
+          min_keep: int = 1) -> RouterOut:
     """The router from its own tensors: bf16 gate [E, d] and, optionally,
     the Q4 shared-expert gate [1, 1, d/8] and a bf16 logit bias [E] (no
-    expert bank needed)."""
+    expert bank needed).  threshold < 1.0: adaptive top-k (a token's slots
+    past its keep count name its first expert with weight 0)."""
     x = _bf16(x, "x")
     router_w = _bf16(router_w, "router_w")
     E, d = int(router_w.shape[0]), int(router_w.shape[1])
@@ -532,6 +553,7 @@ def route(x: torch.Tensor, router_w: torch.Tensor, top_k: int,
     st.num_experts, st.hidden, st.top_k = E, d, k
     if router_bias is not None:
         st.router_bias = _ptr(_bias(router_bias, E))
+    _set_keep(st, threshold, min_keep)
     lib = _lib.load()
     ws = _WS.get(lib.vx_router_workspace(T, ctypes.byref(st)), dev)
     _lib.check(lib.vx_router(x2.data_ptr(), T, ctypes.byref(st), logits.data_ptr(),
