@@ -598,7 +598,7 @@ def main():
         import datetime
         import torch.distributed as dist
         # NCCL's communicator set-up lines (rank count per communicator) in the log
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ["NCCL_DEBUG"] = "INFO"
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
