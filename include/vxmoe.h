@@ -79,6 +79,16 @@ typedef struct vx_moe_pool {
   vx_q4_tiles down;
   vx_q4_tiles shared_gate_up;
   vx_q4_tiles shared_down;
+  /* Partial residency (models/flashnext/expert_pool.py:42, :123-159;
+   * metal_runtime.py:198-228): when slot_of is not NULL, the routed records
+   * (gate_up, down) hold `slots` experts' records ([slots] records, .experts
+   * == slots) and routed expert e's are those of slot slot_of[e]
+   * (device int32 [num_experts]).  The caller makes every expert a call
+   * routes to resident before the call; an entry outside [0, slots) reads
+   * slot 0 - that expert's output is undefined, its reads stay in bounds.
+   * NULL (zero-initialised): expert e's records at e * stride. */
+  const int32_t* slot_of;
+  int32_t slots;
 } vx_moe_pool;
 
 /* Weights of one MoE block (adaptive_topk.py:54-293).  shared_* banks have

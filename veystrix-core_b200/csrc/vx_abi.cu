@@ -87,8 +87,11 @@ static int check_tiles(const vx_q4_tiles& t, int experts, int out, int in, int n
 
 static int check_pool(const vx_moe_pool* p, int E, int d, int I, int Is, bool shared) {
   int s;
-  if ((s = check_tiles(p->gate_up, E, I, d, 2))) return s;
-  if ((s = check_tiles(p->down, E, d, I, 1))) return s;
+  // a pool of slots holds `slots` experts' records, addressed through slot_of
+  if (p->slot_of && (p->slots < 1 || !aligned16(p->slot_of))) return VX_EINVAL_SHAPE;
+  const int nrec = p->slot_of ? p->slots : E;
+  if ((s = check_tiles(p->gate_up, nrec, I, d, 2))) return s;
+  if ((s = check_tiles(p->down, nrec, d, I, 1))) return s;
   if (shared) {
     if ((s = check_tiles(p->shared_gate_up, 1, Is, d, 2))) return s;
     if ((s = check_tiles(p->shared_down, 1, d, Is, 1))) return s;
@@ -277,6 +280,8 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
       a.err = s.err + 1;
       a.rec_b = static_cast<const unsigned char*>(pl.gate_up.records);
       a.stride_b = tile_pool_bytes(1, dm.I, dm.d, 2, pl.gate_up.tile_rows);
+      a.slot_of = pl.slot_of;
+      a.slots = pl.slots;
       a.rec_s = dm.shared ? static_cast<const unsigned char*>(pl.shared_gate_up.records) : nullptr;
       a.N_b = dm.I;
       a.N_s = dm.Is;
@@ -294,6 +299,8 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
       b.err = s.err + 1;
       b.rec_b = static_cast<const unsigned char*>(pl.down.records);
       b.stride_b = tile_pool_bytes(1, dm.d, dm.I, 1, pl.down.tile_rows);
+      b.slot_of = pl.slot_of;
+      b.slots = pl.slots;
       b.rec_s = dm.shared ? static_cast<const unsigned char*>(pl.shared_down.records) : nullptr;
       b.N_b = b.N_s = dm.d;
       b.K_b = dm.I;
@@ -356,6 +363,8 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
     a.err = s.err + 1;
     a.rec_b = static_cast<const unsigned char*>(pl.gate_up.records);
     a.stride_b = tile_pool_bytes(1, dm.I, dm.d, 2, pl.gate_up.tile_rows);
+    a.slot_of = pl.slot_of;
+    a.slots = pl.slots;
     a.rec_s = dm.shared ? static_cast<const unsigned char*>(pl.shared_gate_up.records) : nullptr;
     a.N_b = dm.I;
     a.N_s = dm.Is;
@@ -374,6 +383,8 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
     b.err = s.err + 1;
     b.rec_b = static_cast<const unsigned char*>(pl.down.records);
     b.stride_b = tile_pool_bytes(1, dm.d, dm.I, 1, pl.down.tile_rows);
+    b.slot_of = pl.slot_of;
+    b.slots = pl.slots;
     b.rec_s = dm.shared ? static_cast<const unsigned char*>(pl.shared_down.records) : nullptr;
     b.N_b = b.N_s = dm.d;
     b.K_b = dm.I;
@@ -797,6 +808,8 @@ int vx_moe_block(const uint16_t* x, int32_t T, const vx_moe_weights* W, uint16_t
     a.gu_stride = tile_pool_bytes(1, dm.I, dm.d, 2, pl.gate_up.tile_rows);
     a.dn_rec = static_cast<const unsigned char*>(pl.down.records);
     a.dn_stride = tile_pool_bytes(1, dm.d, dm.I, 1, pl.down.tile_rows);
+    a.slot_of = pl.slot_of;
+    a.slots = pl.slots;
     a.gu_rec_s = dm.shared ? static_cast<const unsigned char*>(pl.shared_gate_up.records) : nullptr;
     a.dn_rec_s = dm.shared ? static_cast<const unsigned char*>(pl.shared_down.records) : nullptr;
     a.T = T;

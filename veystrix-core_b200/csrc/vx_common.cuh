@@ -138,6 +138,16 @@ VX_DEVICE uint4 ldg_nc(const void* p) {
 // slots hold x0 x4 x1 x5 x2 x6 x3 x7, so one 32-bit word is the bf16x2 pair
 // that meets the nibble pairs (0,4) (1,5) (2,6) (3,7) of a packed word in an
 // MMA fragment.  Returns the slot of logical column `col`.
+// Record index of routed expert e in a tiled pool: its slot when the pool
+// holds only some experts (slot_of non-null; an entry outside [0, slots) -
+// an expert the caller did not make resident - reads slot 0: undefined
+// output, in-bounds reads), else e itself.
+VX_DEVICE int64_t routed_record(const int32_t* slot_of, int slots, int e) {
+  if (!slot_of) return e;
+  const int s = __ldg(slot_of + e);
+  return (s >= 0 && s < slots) ? s : 0;
+}
+
 VX_DEVICE int b_order_col(int col) {
   const int e = col & 7;
   return (col & ~7) | (e < 4 ? 2 * e : 2 * (e - 4) + 1);

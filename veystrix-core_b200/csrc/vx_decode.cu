@@ -380,7 +380,8 @@ VX_DEVICE void ring_fill(const DecodeArgs& a, const DecPlan& pl, const DecTab& t
     if (rg.cur.ph <= 1) {
       // a whole gate/up record: both projections of a 16-row tile
       const GuTask t = rg.cur.ph == 0 ? shared_task(pl, rg.cur.j) : routed_task(pl, rg.cur.j);
-      const unsigned char* rec = t.u < 0 ? a.gu_rec_s : a.gu_rec + int64_t(tb.ex[t.u]) * a.gu_stride;
+      const unsigned char* rec =
+          t.u < 0 ? a.gu_rec_s : a.gu_rec + routed_record(a.slot_of, a.slots, tb.ex[t.u]) * a.gu_stride;
       const unsigned char* src = rec + (int64_t(t.rb) * pl.nch_d + rg.cur.ch) * 2560;
       for (int off = lane * 16; off < 2560; off += 512)
         asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(dst + off),
@@ -390,7 +391,7 @@ VX_DEVICE void ring_fill(const DecodeArgs& a, const DecPlan& pl, const DecTab& t
       // the 16 owned rows of a down record (record tile td / dn_mt, m-tile
       // td % dn_mt): their packed words, then their scales and biases
       const int m = pl.td % pl.dn_mt;
-      const unsigned char* rec = a.dn_rec + int64_t(tb.ex[rg.cur.j]) * a.dn_stride +
+      const unsigned char* rec = a.dn_rec + routed_record(a.slot_of, a.slots, tb.ex[rg.cur.j]) * a.dn_stride +
                                  (int64_t(pl.td / pl.dn_mt) * pl.nch_i + rg.cur.ch) * (pl.dn_mt * 1280);
       for (int off = lane * 16; off < 1280; off += 512) {
         const unsigned char* src = off < 1024 ? rec + m * 1024 + off : rec + pl.dn_mt * 1024 + m * 256 + (off - 1024);

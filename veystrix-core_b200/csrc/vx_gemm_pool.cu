@@ -156,7 +156,8 @@ __global__ void __launch_bounds__(kPoolThreads, 1) gemm_pool_kernel(const __grid
         const int rb_total = (k.N + rec_rows - 1) / rec_rows;
         int nrec = kGemmRows / rec_rows;
         if (rb0 + nrec > rb_total) nrec = rb_total - rb0;
-        const unsigned char* ebase = k.sh ? a.rec_s : a.rec_b + int64_t(k.e) * a.stride_b;
+        const unsigned char* ebase =
+            k.sh ? a.rec_s : a.rec_b + routed_record(a.slot_of, a.slots, k.e) * a.stride_b;
         for (int ch = 0; ch < k.nch; ++ch, ++ic) {
           const int r = ic % RS;
           const uint32_t ph = uint32_t(ic / RS) & 1u;

@@ -159,7 +159,8 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
       if (!decode_task<MT>(a, ti, k)) continue;
       const int rb = k.row0 / (16 * MT);
       inch = (k.K + 127) >> 7;
-      irec = (k.sh ? a.rec_s : a.rec_b + int64_t(k.e) * a.stride_b) + int64_t(rb) * inch * kRec;
+      irec = (k.sh ? a.rec_s : a.rec_b + routed_record(a.slot_of, a.slots, k.e) * a.stride_b) +
+             int64_t(rb) * inch * kRec;
       iact = a.act + int64_t(k.p0) * kActRecord;
       ixbytes = uint32_t(k.cnt) * kActRecord;
       return;

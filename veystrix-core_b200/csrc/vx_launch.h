@@ -118,6 +118,8 @@ struct TiledArgs {
   uint16_t* out;                // projection: plain rows [position][ldo]
   int64_t ldo;
   int tiles_per_item;           // set by the launcher
+  const int32_t* slot_of;       // partial residency: routed expert -> record slot (may be null)
+  int slots;
 };
 
 // x rows (token src_rows[p] for position p < *n_rows, or p when src_rows is
@@ -172,6 +174,8 @@ struct PoolGemmArgs {
   int64_t ldo;
   int row_tiles;                // 128-row tiles per item (set by the launcher)
   int max_tasks;                // upper bound of item x row-tile tasks (set by the launcher)
+  const int32_t* slot_of;       // partial residency: routed expert -> record slot (may be null)
+  int slots;
 };
 
 cudaError_t launch_gemm_pool(bool gateup, PoolGemmArgs a, const uint16_t* x, int64_t rows, int64_t ldx,
@@ -277,6 +281,8 @@ struct DecodeArgs {
   int smem_bytes;                     // set by the launcher
   double keep_mass;                   // adaptive top-k (vx_moe_weights.keep_mass)
   int keep_min;
+  const int32_t* slot_of;             // partial residency: routed expert -> record slot (may be null)
+  int slots;
 };
 
 bool decode_supported(int T, int E, int d, int k, int I, int Is, int gu_tile_rows, int dn_tile_rows);

@@ -20,5 +20,6 @@ from .executor import (  # noqa: F401
     Q4G32Projection,
 )
 from .block import MoEBlock, SwitchGLU, moe_call  # noqa: F401
+from .residency import SlotAssigner, SlotPool  # noqa: F401
 
 __version__ = "0.1.0"

@@ -49,6 +49,7 @@ class VxMoEPool(ctypes.Structure):
     _fields_ = [
         ("gate_up", VxQ4Tiles), ("down", VxQ4Tiles),
         ("shared_gate_up", VxQ4Tiles), ("shared_down", VxQ4Tiles),
+        ("slot_of", c_void_p), ("slots", c_int32),
     ]
 
 

@@ -227,6 +227,10 @@ class MoEWeights:
         # min_keep; 1.0 routes every slot (the exact top-k, the default)
         self.threshold: float = 1.0
         self.min_keep: int = 1
+        # partial residency (vxmoe.residency.SlotPool.attach): the slot pool
+        # holding this layer's routed records, and the layer's key in it
+        self.slot_pool = None
+        self.slot_layer = None
 
     def pack(self, down_rows: int = 32) -> "MoEWeights":
         """Re-tile the experts into the resident pool the decode kernels
@@ -612,6 +616,8 @@ def moe_experts(x: torch.Tensor, routes, weights: MoEWeights, scores=None, share
     sy = None if shared_y is None else _bf16(shared_y.to(torch.bfloat16), "shared_y").reshape(T, d)
     sh = None if shared is None else _bf16(shared.to(torch.bfloat16), "shared").reshape(T, d)
     shg = None if shared_gate is None else _bf16(shared_gate.to(torch.bfloat16), "shared_gate").reshape(T)
+    if weights.slot_pool is not None:   # partially resident: fill the routes' misses
+        weights.slot_pool.ensure(weights, [e for e in torch.unique(r).tolist() if 0 <= e < weights.num_experts])
     st = weights.vx(with_shared=False)
     st.top_k = k
     if path is not None:
@@ -662,6 +668,9 @@ def moe_block(x: torch.Tensor, weights: MoEWeights, return_routing: bool = False
     T = int(x2.shape[0])
     dev = x.device
     k = weights.top_k
+    if weights.slot_pool is not None:   # partially resident: route, then fill the misses
+        r = router(x2, weights)
+        weights.slot_pool.ensure(weights, torch.unique(r.inds).tolist())
     st = weights.vx()
     lib = _lib.load()
     ws = _WS.get(lib.vx_moe_block_workspace(T, ctypes.byref(st)), dev)
