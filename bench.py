@@ -684,22 +684,62 @@ def main():
     barrier()
     ms = max_over_ranks(e0.elapsed_time(e1))
 
-    # end to end: pinned host x -> device -> block -> pinned host y
+    # end to end: pinned host x -> device -> block -> pinned host y, every
+    # step moving its own input and output; the copies run on a copy stream
+    # beside the compute (step i+1's input and step i's output while step i
+    # computes), ordered by events: an input buffer is refilled only after
+    # the step that read it, and a layer's output buffer is read back before
+    # that layer runs again
     hx = xs[W:W + K].cpu().pin_memory()
     hy = torch.empty((K, T, HIDDEN), dtype=torch.bfloat16).pin_memory()
-    dx = torch.empty((T, HIDDEN), dtype=torch.bfloat16, device=dev)
-    for i in range(W):
-        dx.copy_(hx[i % K], non_blocking=True)
-        hy[i % K].copy_(layers[i % len(layers)](dx), non_blocking=True)
+    dxs = [torch.empty((T, HIDDEN), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    cs = torch.cuda.Stream(dev)
+
+    def e2e_steps(n, first):
+        ev_in = [torch.cuda.Event(), torch.cuda.Event()]
+        used = [None, None]
+        out_done = {}
+        with torch.cuda.stream(cs):
+            dxs[0].copy_(hx[0], non_blocking=True)
+            ev_in[0].record(cs)
+        for i in range(n):
+            b = i % 2
+            stream.wait_event(ev_in[b])
+            li = (first + i) % len(layers)
+            if li in out_done:
+                stream.wait_event(out_done[li])
+            y = layers[li](dxs[b])
+            done = torch.cuda.Event()
+            done.record(stream)
+            used[b] = done
+            with torch.cuda.stream(cs):
+                if i + 1 < n:
+                    nb = (i + 1) % 2
+                    if used[nb] is not None:
+                        cs.wait_event(used[nb])
+                    dxs[nb].copy_(hx[(i + 1) % K], non_blocking=True)
+                    ev_in[nb].record(cs)
+                cs.wait_event(done)
+                y.record_stream(cs)
+                hy[i % K].copy_(y, non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(cs)
+                out_done[li] = ev
+        fin = torch.cuda.Event()
+        fin.record(cs)
+        stream.wait_event(fin)
+
+    e2e_steps(W, 0)
     barrier()
     e0.record(stream)
-    for i in range(K):
-        dx.copy_(hx[i], non_blocking=True)
-        y = layers[(W + i) % len(layers)](dx)
-        hy[i].copy_(y, non_blocking=True)
+    e2e_steps(K, W)
     e1.record(stream)
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    # the pipelined copies delivered the step's own output: the last step again
+    again = layers[(W + K - 1) % len(layers)](hx[K - 1].to(dev)).cpu()
+    if not torch.equal(again.view(torch.int16), hy[K - 1].view(torch.int16)):
+        raise RuntimeError("end-to-end pass: the host output differs from a direct call")
 
     # spread of single steps (outside the timed regions): each of up to 200
     # steps between its own pair of events; per step the max over ranks
