@@ -152,6 +152,11 @@ int vx_q4_dequant(const vx_q4* bank, int32_t expert, float* out, void* stream);
  * (nproj 1 or 2, tile_rows 16 or 32); 0 for an invalid shape. */
 size_t vx_q4_tiles_bytes(int32_t experts, int32_t out, int32_t in, int32_t nproj,
                          int32_t tile_rows);
+/* The same for banks quantised with `group_size` inputs per scale/bias pair
+ * (32, or 64: one pair per row per 64 inputs, kept as stored,
+ * metal_runtime.py:770-777 with group_size=64). */
+size_t vx_q4_tiles_bytes_group(int32_t experts, int32_t out, int32_t in, int32_t nproj,
+                               int32_t tile_rows, int32_t group_size);
 /* Re-tile bank a (and b, the up half of a gate/up pair, when nproj == 2;
  * same shape as a) into records (device, 16-byte aligned, records_bytes >=
  * vx_q4_tiles_bytes).  Out-of-range rows and groups are zero-filled.  A

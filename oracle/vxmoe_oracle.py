@@ -643,19 +643,25 @@ def weighted_combine(expert_outputs, routes, scores):
 # checked byte for byte and the round trip back to the MLX arrays is exact.
 
 
-def tile_records(a: Q4Bank, b: Q4Bank | None = None, tile_rows: int = 16) -> np.ndarray:
+def tile_records(a: Q4Bank, b: Q4Bank | None = None, tile_rows: int = 16,
+                 group_size: int = GROUP_SIZE) -> np.ndarray:
     """Records of bank `a` (and `b`, the up half of a gate/up pair) as uint8:
     per (expert, row tile, 128-input chunk) the packed words [p][m][h][g][c]
     (4 words each; row 16m+g+8h, words 4c..4c+3 of the chunk), then the
-    scales/biases [p][m][g][c&1][h]{s_a, s_b, b_a, b_b} of groups 4ch+2(c&1)
-    and +1.  Out-of-range rows and groups are zero."""
+    scales/biases.  Groups of 32: [p][m][g][c&1][h]{s_a, s_b, b_a, b_b} of
+    groups 4ch+2(c&1) and +1.  Groups of 64 (kept as stored):
+    [p][m][g][cb][h]{s, b} of group 2ch+cb.  Out-of-range rows and groups are
+    zero."""
+    if group_size not in (32, 64):
+        raise ValueError("tiled records hold groups of 32 or 64")
     banks = [a] if b is None else [a, b]
     E, out, W = a.w.shape
     K = W * 8
-    G = K // 32
+    G = K // group_size
     MT = tile_rows // 16
     RB = -(-out // tile_rows)
     nch = -(-K // 128)
+    gpc = 128 // group_size          # groups per 128-input chunk
     wparts, sparts = [], []
     for bk in banks:
         w = np.zeros((E, RB * tile_rows, nch * 16), np.uint32)
@@ -663,36 +669,48 @@ def tile_records(a: Q4Bank, b: Q4Bank | None = None, tile_rows: int = 16) -> np.
         # [E, RB, MT, h, g, nch, c, j] -> [E, RB, nch, MT, h, g, c, j]
         w = w.reshape(E, RB, MT, 2, 8, nch, 4, 4).transpose(0, 1, 5, 2, 3, 4, 6, 7)
         wparts.append(w.reshape(E, RB, nch, MT, 1024 // 4))
-        sb = np.zeros((2, E, RB * tile_rows, nch * 4), np.uint16)
+        sb = np.zeros((2, E, RB * tile_rows, nch * gpc), np.uint16)
         sb[0, :, :out, :G] = bf16_bits(bk.scales)
         sb[1, :, :out, :G] = bf16_bits(bk.biases)
-        # [kind, E, RB, MT, h, g, nch, cb, ab] -> [E, RB, nch, MT, g, cb, h, kind, ab]
-        sb = sb.reshape(2, E, RB, MT, 2, 8, nch, 2, 2).transpose(1, 2, 6, 3, 5, 7, 4, 0, 8)
-        sparts.append(sb.reshape(E, RB, nch, MT, 256 // 2))
+        if group_size == 32:
+            # [kind, E, RB, MT, h, g, nch, cb, ab] -> [E, RB, nch, MT, g, cb, h, kind, ab]
+            sb = sb.reshape(2, E, RB, MT, 2, 8, nch, 2, 2).transpose(1, 2, 6, 3, 5, 7, 4, 0, 8)
+        else:
+            # [kind, E, RB, MT, h, g, nch, cb] -> [E, RB, nch, MT, g, cb, h, kind]
+            sb = sb.reshape(2, E, RB, MT, 2, 8, nch, 2).transpose(1, 2, 6, 3, 5, 7, 4, 0)
+        sparts.append(sb.reshape(E, RB, nch, MT, -1))
     wcat = np.concatenate(wparts, axis=3).view(np.uint8).reshape(E, RB, nch, -1)
     scat = np.concatenate(sparts, axis=3).view(np.uint8).reshape(E, RB, nch, -1)
     return np.ascontiguousarray(np.concatenate([wcat, scat], axis=3)).reshape(-1)
 
 
 def untile_records(rec: np.ndarray, experts: int, out: int, inn: int, nproj: int,
-                   tile_rows: int) -> list[tuple[np.ndarray, np.ndarray, np.ndarray]]:
+                   tile_rows: int, group_size: int = GROUP_SIZE
+                   ) -> list[tuple[np.ndarray, np.ndarray, np.ndarray]]:
     """Inverse of tile_records: per projection (w uint32 [E, out, in/8], scale
-    bits, bias bits uint16 [E, out, in/32])."""
+    bits, bias bits uint16 [E, out, in/group_size])."""
     MT = tile_rows // 16
     RB = -(-out // tile_rows)
     nch = -(-inn // 128)
-    per = nproj * MT * 1280
+    sbytes = 256 if group_size == 32 else 128
+    per = nproj * MT * (1024 + sbytes)
     r = np.asarray(rec, np.uint8).reshape(experts, RB, nch, per)
     wb = np.ascontiguousarray(r[..., :nproj * MT * 1024]).view(np.uint32)
     sbb = np.ascontiguousarray(r[..., nproj * MT * 1024:]).view(np.uint16)
     wb = wb.reshape(experts, RB, nch, nproj, MT, 2, 8, 4, 4)
-    sbb = sbb.reshape(experts, RB, nch, nproj, MT, 8, 2, 2, 2, 2)
     res = []
     for p in range(nproj):
         w = wb[:, :, :, p].transpose(0, 1, 3, 4, 5, 2, 6, 7).reshape(experts, RB * tile_rows, nch * 16)
-        # [E, RB, nch, MT, g, cb, h, kind, ab] -> [kind, E, RB, MT, h, g, nch, cb, ab]
-        s = sbb[:, :, :, p].transpose(7, 0, 1, 3, 6, 4, 2, 5, 8).reshape(2, experts, RB * tile_rows, nch * 4)
-        res.append((w[:, :out, :inn // 8], s[0, :, :out, :inn // 32], s[1, :, :out, :inn // 32]))
+        if group_size == 32:
+            sp = sbb.reshape(experts, RB, nch, nproj, MT, 8, 2, 2, 2, 2)[:, :, :, p]
+            # [E, RB, nch, MT, g, cb, h, kind, ab] -> [kind, E, RB, MT, h, g, nch, cb, ab]
+            s = sp.transpose(7, 0, 1, 3, 6, 4, 2, 5, 8).reshape(2, experts, RB * tile_rows, nch * 4)
+        else:
+            sp = sbb.reshape(experts, RB, nch, nproj, MT, 8, 2, 2, 2)[:, :, :, p]
+            # [E, RB, nch, MT, g, cb, h, kind] -> [kind, E, RB, MT, h, g, nch, cb]
+            s = sp.transpose(7, 0, 1, 3, 6, 4, 2, 5).reshape(2, experts, RB * tile_rows, nch * 2)
+        G = inn // group_size
+        res.append((w[:, :out, :inn // 8], s[0, :, :out, :G], s[1, :, :out, :G]))
     return res
 
 

@@ -34,9 +34,11 @@ def test_loaded_layer_equals_in_memory_weights(tmp_path):
 
 
 def test_g64_layer_runs_within_tolerance(tmp_path):
-    """A G64 checkpoint layer (every projection in groups of 64) is expanded
-    to groups of 32 at load time: routing bit-exact against the oracle on the
-    device's logits, outputs within the block tolerance of the G64 oracle."""
+    """A G64 checkpoint layer (every projection in groups of 64) loads with
+    native G64 records (the shared-expert gate expanded to groups of 32):
+    routing bit-exact against the oracle on the device's logits, outputs
+    within the block tolerance of the G64 oracle, and the bits of the same
+    layer loaded with every group expanded to 32."""
     import vxmoe
     from vxmoe import loader as L
     p = O.make_params(seed=63, experts=32, hidden=512, inter=256, shared_inter=128, top_k=4, group_size=64)
@@ -46,13 +48,21 @@ def test_g64_layer_runs_within_tolerance(tmp_path):
     store = L.SafeTensorStore([path])
     assert L.infer_switch_quantization(store, L.layer_prefix(2) + ".switch_mlp") == (64, 4)
     w = L.load_moe_layer(store, 2, top_k=p.top_k, device="cuda")
+    assert w.group_size == 64 and w.pool.group_size == 64
+    assert w.shared_expert_gate.group_size == 32
+    w32 = L.load_moe_layer(store, 2, top_k=p.top_k, device="cuda", native_groups=False)
+    assert w32.group_size == 32
     for T in (3, 200):   # decode GEMV and prefill GEMM
         x = O.make_x(66 + T, T, p.hidden)
         y, inds, _ = vxmoe.moe_block(bf16_t(x), w, return_routing=True)
         logits = np32(vxmoe.router(bf16_t(x), w).logits)
-        out = O.moe_block(x, p, logits=logits)
+        out = O.moe_block(x, p, logits=logits, path="prefill" if T > 3 else "decode")
         np.testing.assert_array_equal(inds.cpu().numpy(), out.router.inds)
         assert O.normwise_error(np32(y), out.y) < 1e-2
+        if T > 3:   # the GEMM path; decode-sized G32 batches take the decode kernel
+            y32 = vxmoe.moe_block(bf16_t(x), w32)
+            np.testing.assert_array_equal(y.view(torch.int16).cpu().numpy(),
+                                          y32.view(torch.int16).cpu().numpy())
 
 
 def test_8bit_layer_is_refused(tmp_path):

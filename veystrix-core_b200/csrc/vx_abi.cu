@@ -61,11 +61,11 @@ struct Carver {
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-static int check_q4(const vx_q4* b, int experts, int out, int in) {
+static int check_q4(const vx_q4* b, int experts, int out, int in, int group = 32) {
   if (!b || !b->w || !b->scales || !b->biases) return VX_EINVAL_SHAPE;
-  if (b->group_size != 32) return VX_EUNSUPPORTED;
+  if (b->group_size != group) return VX_EUNSUPPORTED;
   if ((experts >= 0 && b->experts != experts) || b->out != out || b->in != in) return VX_EINVAL_SHAPE;
-  if (b->in <= 0 || b->in % 32 || b->out <= 0) return VX_EINVAL_SHAPE;
+  if (b->in <= 0 || b->in % group || b->out <= 0) return VX_EINVAL_SHAPE;
   if (!aligned16(b->w)) return VX_EINVAL_SHAPE;
   return VX_OK;
 }
@@ -77,10 +77,10 @@ struct BlockDims {
   int path = VX_PATH_AUTO;   // the weights' expert_path
 };
 
-static int check_tiles(const vx_q4_tiles& t, int experts, int out, int in, int nproj) {
+static int check_tiles(const vx_q4_tiles& t, int experts, int out, int in, int nproj, int group) {
   if (!t.records || !aligned16(t.records)) return VX_EINVAL_SHAPE;
   if (t.experts != experts || t.out != out || t.in != in || t.nproj != nproj) return VX_EINVAL_SHAPE;
-  if (t.group_size != 32) return VX_EUNSUPPORTED;
+  if (t.group_size != group || (group != 32 && group != 64) || in % group) return VX_EUNSUPPORTED;
   if (t.tile_rows != 16 && !(nproj == 1 && t.tile_rows == 32)) return VX_EINVAL_SHAPE;
   return VX_OK;
 }
@@ -90,11 +90,13 @@ static int check_pool(const vx_moe_pool* p, int E, int d, int I, int Is, bool sh
   // a pool of slots holds `slots` experts' records, addressed through slot_of
   if (p->slot_of && (p->slots < 1 || !aligned16(p->slot_of))) return VX_EINVAL_SHAPE;
   const int nrec = p->slot_of ? p->slots : E;
-  if ((s = check_tiles(p->gate_up, nrec, I, d, 2))) return s;
-  if ((s = check_tiles(p->down, nrec, d, I, 1))) return s;
+  // every part of a pool shares one quant group (32, or 64 natively)
+  const int group = p->gate_up.group_size;
+  if ((s = check_tiles(p->gate_up, nrec, I, d, 2, group))) return s;
+  if ((s = check_tiles(p->down, nrec, d, I, 1, group))) return s;
   if (shared) {
-    if ((s = check_tiles(p->shared_gate_up, 1, Is, d, 2))) return s;
-    if ((s = check_tiles(p->shared_down, 1, d, Is, 1))) return s;
+    if ((s = check_tiles(p->shared_gate_up, 1, Is, d, 2, group))) return s;
+    if ((s = check_tiles(p->shared_down, 1, d, Is, 1, group))) return s;
     // one launch serves routed and shared rows: the same row tiling
     if (p->shared_down.tile_rows != p->down.tile_rows) return VX_EINVAL_SHAPE;
   }
@@ -107,18 +109,20 @@ static int check_weights(const vx_moe_weights* W, bool need_router, BlockDims* d
   if (E < 1 || E > 1024 || d <= 0 || d % 32 || k < 1 || k > 16 || k > E) return VX_EINVAL_SHAPE;
   const int I = W->gate.out;
   int s;
-  if ((s = check_q4(&W->gate, E, I, d))) return s;
-  if ((s = check_q4(&W->up, E, I, d))) return s;
-  if ((s = check_q4(&W->down, E, d, I))) return s;
+  // the banks' group: 32, or the pool's native 64 (the banks then give shapes only)
+  const int gb = W->pool && W->pool->gate_up.group_size == 64 ? 64 : 32;
+  if ((s = check_q4(&W->gate, E, I, d, gb))) return s;
+  if ((s = check_q4(&W->up, E, I, d, gb))) return s;
+  if ((s = check_q4(&W->down, E, d, I, gb))) return s;
   if (I % 32) return VX_EINVAL_SHAPE;
   if (need_router && (!W->router_w || !aligned16(W->router_w))) return VX_EINVAL_SHAPE;
   const bool shared = W->shared_gate.w != nullptr;
   int Is = 0;
   if (shared) {
     Is = W->shared_gate.out;
-    if ((s = check_q4(&W->shared_gate, 1, Is, d))) return s;
-    if ((s = check_q4(&W->shared_up, 1, Is, d))) return s;
-    if ((s = check_q4(&W->shared_down, 1, d, Is))) return s;
+    if ((s = check_q4(&W->shared_gate, 1, Is, d, gb))) return s;
+    if ((s = check_q4(&W->shared_up, 1, Is, d, gb))) return s;
+    if ((s = check_q4(&W->shared_down, 1, d, Is, gb))) return s;
     if (Is % 32) return VX_EINVAL_SHAPE;
     if (need_router && (s = check_q4(&W->shared_expert_gate, 1, 1, d))) return s;
   }
@@ -182,6 +186,9 @@ static bool use_decode(int T, const BlockDims& dm) {
   if (dm.path != VX_PATH_AUTO || path_override() != 0) return false;
   if (!dm.pool || !decode_enabled() || expert_path(T, dm) != kPathGemvTiled) return false;
   if (dm.shared && dm.Is != dm.pool->shared_gate_up.out) return false;
+  // the single launch reads records with groups of 32; native G64 records
+  // take the multi-kernel GEMV pipeline
+  if (dm.pool->gate_up.group_size != 32) return false;
   return decode_supported(T, dm.E, dm.d, dm.k, dm.I, dm.shared ? dm.Is : 0, dm.pool->gate_up.tile_rows,
                           dm.pool->down.tile_rows);
 }
@@ -279,9 +286,10 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
       PoolGemmArgs a{};
       a.err = s.err + 1;
       a.rec_b = static_cast<const unsigned char*>(pl.gate_up.records);
-      a.stride_b = tile_pool_bytes(1, dm.I, dm.d, 2, pl.gate_up.tile_rows);
+      a.stride_b = tile_pool_bytes(1, dm.I, dm.d, 2, pl.gate_up.tile_rows, pl.gate_up.group_size);
       a.slot_of = pl.slot_of;
       a.slots = pl.slots;
+      a.group = pl.gate_up.group_size;
       a.rec_s = dm.shared ? static_cast<const unsigned char*>(pl.shared_gate_up.records) : nullptr;
       a.N_b = dm.I;
       a.N_s = dm.Is;
@@ -298,9 +306,10 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
       PoolGemmArgs b{};
       b.err = s.err + 1;
       b.rec_b = static_cast<const unsigned char*>(pl.down.records);
-      b.stride_b = tile_pool_bytes(1, dm.d, dm.I, 1, pl.down.tile_rows);
+      b.stride_b = tile_pool_bytes(1, dm.d, dm.I, 1, pl.down.tile_rows, pl.down.group_size);
       b.slot_of = pl.slot_of;
       b.slots = pl.slots;
+      b.group = pl.down.group_size;
       b.rec_s = dm.shared ? static_cast<const unsigned char*>(pl.shared_down.records) : nullptr;
       b.N_b = b.N_s = dm.d;
       b.K_b = dm.I;
@@ -362,7 +371,7 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
     TiledArgs a{};
     a.err = s.err + 1;
     a.rec_b = static_cast<const unsigned char*>(pl.gate_up.records);
-    a.stride_b = tile_pool_bytes(1, dm.I, dm.d, 2, pl.gate_up.tile_rows);
+    a.stride_b = tile_pool_bytes(1, dm.I, dm.d, 2, pl.gate_up.tile_rows, pl.gate_up.group_size);
     a.slot_of = pl.slot_of;
     a.slots = pl.slots;
     a.rec_s = dm.shared ? static_cast<const unsigned char*>(pl.shared_gate_up.records) : nullptr;
@@ -375,14 +384,14 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
     a.act = s.act;
     a.act_rows = P + Ts;
     a.hrec = s.hrec;
-    e = launch_gemv_tiled(true, pl.gate_up.tile_rows, a, s.max_items, int(s.ldh), st);
+    e = launch_gemv_tiled(true, pl.gate_up.tile_rows, a, s.max_items, int(s.ldh), st, pl.gate_up.group_size);
     if (e != cudaSuccess) return vx_cuda_fail(e);
     profile_mark(st, "gate_up_swiglu");
 
     TiledArgs b{};
     b.err = s.err + 1;
     b.rec_b = static_cast<const unsigned char*>(pl.down.records);
-    b.stride_b = tile_pool_bytes(1, dm.d, dm.I, 1, pl.down.tile_rows);
+    b.stride_b = tile_pool_bytes(1, dm.d, dm.I, 1, pl.down.tile_rows, pl.down.group_size);
     b.slot_of = pl.slot_of;
     b.slots = pl.slots;
     b.rec_s = dm.shared ? static_cast<const unsigned char*>(pl.shared_down.records) : nullptr;
@@ -396,7 +405,7 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
     b.act_rows = P + Ts;
     b.out = s.yd;
     b.ldo = dm.d;
-    e = launch_gemv_tiled(false, pl.down.tile_rows, b, s.max_items, dm.d, st);
+    e = launch_gemv_tiled(false, pl.down.tile_rows, b, s.max_items, dm.d, st, pl.down.group_size);
     if (e != cudaSuccess) return vx_cuda_fail(e);
     profile_mark(st, "down");
     return VX_OK;
@@ -485,28 +494,36 @@ const char* vx_strerror(int status) {
 
 const char* vx_last_cuda_error(void) { return g_cuda_err; }
 
+size_t vx_q4_tiles_bytes_group(int32_t experts, int32_t out, int32_t in, int32_t nproj, int32_t tile_rows,
+                               int32_t group_size) {
+  if (group_size != 32 && group_size != 64) return 0;
+  if (experts < 1 || out < 1 || in < group_size || in % group_size || (nproj != 1 && nproj != 2)) return 0;
+  if (tile_rows != 16 && !(nproj == 1 && tile_rows == 32)) return 0;
+  return size_t(tile_pool_bytes(experts, out, in, nproj, tile_rows, group_size));
+}
+
 size_t vx_q4_tiles_bytes(int32_t experts, int32_t out, int32_t in, int32_t nproj,
                          int32_t tile_rows) {
-  if (experts < 1 || out < 1 || in < 32 || in % 32 || (nproj != 1 && nproj != 2)) return 0;
-  if (tile_rows != 16 && !(nproj == 1 && tile_rows == 32)) return 0;
-  return size_t(tile_pool_bytes(experts, out, in, nproj, tile_rows));
+  return vx_q4_tiles_bytes_group(experts, out, in, nproj, tile_rows, 32);
 }
 
 int vx_q4_tile(const vx_q4* a, const vx_q4* b, int32_t nproj, int32_t tile_rows, void* records,
                size_t records_bytes, void* stream) {
   if (!a) return VX_EINVAL_SHAPE;
-  int s = check_q4(a, -1, a->out, a->in);
+  // the records keep the banks' group: 32, or 64 natively
+  const int group = a->group_size == 64 ? 64 : 32;
+  int s = check_q4(a, -1, a->out, a->in, group);
   if (s) return s;
   if (nproj == 2) {
     if (!b) return VX_EINVAL_SHAPE;
-    if ((s = check_q4(b, a->experts, a->out, a->in))) return s;
+    if ((s = check_q4(b, a->experts, a->out, a->in, group))) return s;
   }
-  const size_t need = vx_q4_tiles_bytes(a->experts, a->out, a->in, nproj, tile_rows);
+  const size_t need = vx_q4_tiles_bytes_group(a->experts, a->out, a->in, nproj, tile_rows, group);
   if (need == 0) return VX_EINVAL_SHAPE;
   if (!records || !aligned16(records)) return VX_EINVAL_SHAPE;
   if (records_bytes < need) return VX_EWORKSPACE;
   cudaError_t e = launch_tile_pack(*a, nproj == 2 ? *b : *a, nproj, tile_rows, records,
-                                   static_cast<cudaStream_t>(stream));
+                                   static_cast<cudaStream_t>(stream), group);
   return e == cudaSuccess ? VX_OK : vx_cuda_fail(e);
 }
 
@@ -805,9 +822,9 @@ int vx_moe_block(const uint16_t* x, int32_t T, const vx_moe_weights* W, uint16_t
     a.keep_min = W->keep_min;
     if (dm.shared) a.seg = W->shared_expert_gate;
     a.gu_rec = static_cast<const unsigned char*>(pl.gate_up.records);
-    a.gu_stride = tile_pool_bytes(1, dm.I, dm.d, 2, pl.gate_up.tile_rows);
+    a.gu_stride = tile_pool_bytes(1, dm.I, dm.d, 2, pl.gate_up.tile_rows, pl.gate_up.group_size);
     a.dn_rec = static_cast<const unsigned char*>(pl.down.records);
-    a.dn_stride = tile_pool_bytes(1, dm.d, dm.I, 1, pl.down.tile_rows);
+    a.dn_stride = tile_pool_bytes(1, dm.d, dm.I, 1, pl.down.tile_rows, pl.down.group_size);
     a.slot_of = pl.slot_of;
     a.slots = pl.slots;
     a.gu_rec_s = dm.shared ? static_cast<const unsigned char*>(pl.shared_gate_up.records) : nullptr;

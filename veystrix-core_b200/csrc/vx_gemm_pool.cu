@@ -140,7 +140,8 @@ __global__ void __launch_bounds__(kPoolThreads, 1) gemm_pool_kernel(const __grid
   const uint32_t tmem = tmem_slot;
   const int total = *a.n_items * a.row_tiles;
   const int rec_rows = a.tile_rows, MT = rec_rows >> 4;
-  const int rec_bytes = NP * MT * kTileRecordUnit;
+  const int sb_unit = tile_unit_bytes(a.group) - 1024;   // scale/bias bytes per (p, m)
+  const int rec_bytes = NP * MT * tile_unit_bytes(a.group);
   bool timed_out = false;
 
   if (warp == 0) {
@@ -256,7 +257,10 @@ __global__ void __launch_bounds__(kPoolThreads, 1) gemm_pool_kernel(const __grid
     const int m = rl >> 4, g = rl & 7, h = (rl >> 3) & 1;
     const uint32_t tq = tmem + (uint32_t(quarter * 32) << 16);
     const uint32_t rrow = ri * rec_bytes + m * 1024 + h * 512 + g * 64;                 // words, p = 0
-    const uint32_t srow = ri * rec_bytes + NP * MT * 1024 + m * 256 + g * 32 + h * 8;  // scales, p = 0
+    // scales, p = 0: groups of 32 {s_a s_b | b_a b_b} per (g, atom) pair of
+    // rows; native G64 one {s | b} word per row and 64 inputs ([g][atom][h])
+    const bool g64 = a.group == 64;
+    const uint32_t srow = ri * rec_bytes + NP * MT * 1024 + m * sb_unit + (g64 ? g * 16 + h * 4 : g * 32 + h * 8);
     int ic = 0, ia = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       PoolTask k;
@@ -288,7 +292,12 @@ __global__ void __launch_bounds__(kPoolThreads, 1) gemm_pool_kernel(const __grid
               const uint32_t wb = rec + rrow + p * MT * 1024 + atom * 32;
               w0 = lds128(wb);
               w1 = lds128(wb + 16);
-              sbv = lds64(rec + srow + p * MT * 256 + atom * 16);
+              if (g64) {
+                const uint32_t wsb = lds32(rec + srow + p * MT * sb_unit + atom * 8);
+                sbv = make_uint2((wsb & 0xFFFFu) | (wsb << 16), (wsb >> 16) | (wsb & 0xFFFF0000u));
+              } else {
+                sbv = lds64(rec + srow + p * MT * sb_unit + atom * 16);
+              }
             }
             const uint32_t s0 = (sbv.x & 0xFFFFu) * 0x10001u, s1 = (sbv.x >> 16) * 0x10001u;
             const uint32_t b0 = (sbv.y & 0xFFFFu) * 0x10001u, b1 = (sbv.y >> 16) * 0x10001u;

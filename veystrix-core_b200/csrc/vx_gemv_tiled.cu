@@ -113,14 +113,15 @@ VX_DEVICE void issue_act(bool leader, uint32_t bar, uint32_t dst_x, const void* 
 // so the heavy stream goes the other way.
 constexpr bool kWeightsByLsu = true;
 
-template <bool GATEUP, int MT, bool XMMA, int STAGES, int WARPS>
+template <bool GATEUP, int MT, bool XMMA, int STAGES, int WARPS, int GS>
 __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
     gemv_tiled_kernel(const __grid_constant__ TiledArgs a) {
   chain_wait();
   constexpr int NP = GATEUP ? 2 : 1;
   // gate/up reads act_records_kernel's f16 records; down reads h in bf16
   constexpr bool F16 = GATEUP && kActF16;
-  constexpr int kRec = NP * MT * kTileRecordUnit;
+  constexpr int kRec = NP * MT * tile_unit_bytes(GS);
+  constexpr int kSbUnit = tile_unit_bytes(GS) - 1024;   // scale/bias bytes per (p, m)
   constexpr int kWBytes = NP * MT * 1024;
   constexpr int kXOff = kRec;                       // [token][kActRecord]
   constexpr int kStage = kRec + kTiledItemChunk * kActRecord;
@@ -302,8 +303,21 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
               mma16816(d[q], h0, h1, h2, h3, bq[q][2 * mm + 2], bq[q][2 * mm + 3]);
             }
           }
-          const uint4 sb = lds128(st + kWBytes + (p * MT + m) * 256 + (g * 2 + (c & 1)) * 16);
-          const uint32_t sw[4] = {sb.x, sb.y, sb.z, sb.w};
+          uint32_t sw[4];
+          if constexpr (GS == 64) {
+            // one {s | b} per row: groups 2(c&1) and 2(c&1)+1 share it
+            const uint2 sb = lds64(st + kWBytes + (p * MT + m) * kSbUnit + (g * 2 + (c & 1)) * 8);
+            sw[0] = (sb.x & 0xFFFFu) * 0x10001u;
+            sw[1] = (sb.x >> 16) * 0x10001u;
+            sw[2] = (sb.y & 0xFFFFu) * 0x10001u;
+            sw[3] = (sb.y >> 16) * 0x10001u;
+          } else {
+            const uint4 sb = lds128(st + kWBytes + (p * MT + m) * kSbUnit + (g * 2 + (c & 1)) * 16);
+            sw[0] = sb.x;
+            sw[1] = sb.y;
+            sw[2] = sb.z;
+            sw[3] = sb.w;
+          }
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const float s0 = __uint_as_float(sw[2 * h] << 16);
@@ -481,10 +495,12 @@ cudaError_t launch_act_records(const uint16_t* x, int64_t ldx, int K, const int3
 // ---- pool packing -----------------------------------------------------------
 
 // One thread per 16-byte unit of the pool.  a: first (or only) projection,
-// b: second projection of a gate/up pair.
-__global__ void tile_pack_kernel(vx_q4 a, vx_q4 b, int NP, int MT, int RB, int nch, uint4* out,
+// b: second projection of a gate/up pair.  gs: the banks' quant group, 32
+// ({s_a s_b | b_a b_b} per row pair and group pair) or 64 (native G64: one
+// {s | b} word per row and 64 inputs, [g][c&1][h]).
+__global__ void tile_pack_kernel(vx_q4 a, vx_q4 b, int NP, int MT, int RB, int nch, int gs, uint4* out,
                                  int64_t units) {
-  const int per_rec = NP * MT * (kTileRecordUnit / 16);
+  const int per_rec = NP * MT * (tile_unit_bytes(gs) / 16);
   for (int64_t u = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; u < units;
        u += int64_t(gridDim.x) * blockDim.x) {
     const int64_t rec = u / per_rec;
@@ -508,6 +524,29 @@ __global__ void tile_pack_kernel(vx_q4 a, vx_q4 b, int NP, int MT, int RB, int n
         v.z = w0 + 2 < W ? src[w0 + 2] : 0u;
         v.w = w0 + 3 < W ? src[w0 + 3] : 0u;
       }
+    } else if (gs == 64) {
+      // 8 units per (p, m): unit g holds {cb 0: row g, row g+8}{cb 1: ...}
+      const int o2 = off - NP * MT * 64;
+      const int pm = o2 / 8, g = o2 % 8;
+      const int p = pm / MT, m = pm % MT;
+      const vx_q4& bk = p ? b : a;
+      const int G = bk.in / 64;
+      uint32_t wd[4];
+#pragma unroll
+      for (int cb = 0; cb < 2; ++cb)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int row = rb * 16 * MT + 16 * m + g + 8 * h;
+          const int gi = 2 * ch + cb;
+          uint32_t sv = 0, bv = 0;
+          if (row < bk.out && gi < G) {
+            const int64_t idx = (e * bk.out + row) * G + gi;
+            sv = bk.scales[idx];
+            bv = bk.biases[idx];
+          }
+          wd[2 * cb + h] = sv | (bv << 16);
+        }
+      v = make_uint4(wd[0], wd[1], wd[2], wd[3]);
     } else {
       const int o2 = off - NP * MT * 64;
       const int pm = o2 / 16, q = o2 % 16;
@@ -535,34 +574,34 @@ __global__ void tile_pack_kernel(vx_q4 a, vx_q4 b, int NP, int MT, int RB, int n
   }
 }
 
-int64_t tile_pool_bytes(int64_t experts, int out, int in, int nproj, int tile_rows) {
+int64_t tile_pool_bytes(int64_t experts, int out, int in, int nproj, int tile_rows, int group) {
   const int64_t RB = (out + tile_rows - 1) / tile_rows;
   const int64_t nch = (in + 127) / 128;
-  return experts * RB * nch * int64_t(nproj) * (tile_rows / 16) * kTileRecordUnit;
+  return experts * RB * nch * int64_t(nproj) * (tile_rows / 16) * tile_unit_bytes(group);
 }
 
 cudaError_t launch_tile_pack(const vx_q4& a, const vx_q4& b, int nproj, int tile_rows, void* out,
-                             cudaStream_t st) {
+                             cudaStream_t st, int group) {
   const int MT = tile_rows / 16;
   const int RB = (a.out + tile_rows - 1) / tile_rows;
   const int nch = (a.in + 127) / 128;
-  const int64_t units = tile_pool_bytes(a.experts, a.out, a.in, nproj, tile_rows) / 16;
+  const int64_t units = tile_pool_bytes(a.experts, a.out, a.in, nproj, tile_rows, group) / 16;
   if (units == 0) return cudaSuccess;
   int64_t blocks = (units + 255) / 256;
   if (blocks > int64_t(sm_count()) * 32) blocks = int64_t(sm_count()) * 32;
-  tile_pack_kernel<<<int(blocks), 256, 0, st>>>(a, nproj == 2 ? b : a, nproj, MT, RB, nch,
+  tile_pack_kernel<<<int(blocks), 256, 0, st>>>(a, nproj == 2 ? b : a, nproj, MT, RB, nch, group,
                                                 static_cast<uint4*>(out), units);
   return cudaGetLastError();
 }
 
 // ---- launcher ----------------------------------------------------------------
 
-template <bool GATEUP, int MT, bool XMMA, int STAGES, int WARPS>
+template <bool GATEUP, int MT, bool XMMA, int STAGES, int WARPS, int GS>
 static cudaError_t launch_tiled_v(TiledArgs a, int64_t tasks, cudaStream_t st) {
   constexpr int NP = GATEUP ? 2 : 1;
-  constexpr int kStage = NP * MT * kTileRecordUnit + kTiledItemChunk * kActRecord;
+  constexpr int kStage = NP * MT * tile_unit_bytes(GS) + kTiledItemChunk * kActRecord;
   const size_t smem = size_t(WARPS) * STAGES * kStage;
-  auto kern = gemv_tiled_kernel<GATEUP, MT, XMMA, STAGES, WARPS>;
+  auto kern = gemv_tiled_kernel<GATEUP, MT, XMMA, STAGES, WARPS, GS>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (err != cudaSuccess) return err;
   // persistent: two resident CTAs per SM for the 8-warp shape, one otherwise
@@ -580,26 +619,35 @@ static cudaError_t launch_tiled_v(TiledArgs a, int64_t tasks, cudaStream_t st) {
 constexpr int kDeepStages = 8;
 constexpr int kDeepWarps = 4;
 
-template <bool GATEUP, int MT, bool XMMA>
+template <bool GATEUP, int MT, bool XMMA, int GS>
 static cudaError_t launch_tiled_t(TiledArgs a, int max_items, int max_out, cudaStream_t st) {
   a.tiles_per_item = (max_out + 16 * MT - 1) / (16 * MT);
   const int64_t tasks = int64_t(max_items) * a.tiles_per_item;
   // (a task with only a few chunks, as down's 4, gains nothing from the depth)
   if (tasks <= int64_t(sm_count()) * kDeepWarps && (a.K_b + 127) / 128 >= kDeepStages)
-    return launch_tiled_v<GATEUP, MT, XMMA, kDeepStages, kDeepWarps>(a, tasks, st);
-  return launch_tiled_v<GATEUP, MT, XMMA, kTiledStages, kTiledWarps>(a, tasks, st);
+    return launch_tiled_v<GATEUP, MT, XMMA, kDeepStages, kDeepWarps, GS>(a, tasks, st);
+  return launch_tiled_v<GATEUP, MT, XMMA, kTiledStages, kTiledWarps, GS>(a, tasks, st);
+}
+
+template <int GS>
+static cudaError_t launch_gemv_tiled_g(bool gateup, int tile_rows, const TiledArgs& a, int max_items,
+                                       int max_out, cudaStream_t st) {
+  if (gateup) {
+    if (tile_rows != 16) return cudaErrorInvalidValue;
+    return launch_tiled_t<true, 1, false, GS>(a, max_items, max_out, st);
+  }
+  if (tile_rows == 32) return launch_tiled_t<false, 2, true, GS>(a, max_items, max_out, st);
+  if (tile_rows == 16) return launch_tiled_t<false, 1, true, GS>(a, max_items, max_out, st);
+  return cudaErrorInvalidValue;
 }
 
 // gate/up: activation records carry the group sums; the single projection
-// (down) sums its input h on the tensor pipe.
+// (down) sums its input h on the tensor pipe.  group: the records' quant
+// group (32, or 64 for native G64 records).
 cudaError_t launch_gemv_tiled(bool gateup, int tile_rows, const TiledArgs& a, int max_items,
-                              int max_out, cudaStream_t st) {
-  if (gateup) {
-    if (tile_rows != 16) return cudaErrorInvalidValue;
-    return launch_tiled_t<true, 1, false>(a, max_items, max_out, st);
-  }
-  if (tile_rows == 32) return launch_tiled_t<false, 2, true>(a, max_items, max_out, st);
-  if (tile_rows == 16) return launch_tiled_t<false, 1, true>(a, max_items, max_out, st);
+                              int max_out, cudaStream_t st, int group) {
+  if (group == 64) return launch_gemv_tiled_g<64>(gateup, tile_rows, a, max_items, max_out, st);
+  if (group == 32) return launch_gemv_tiled_g<32>(gateup, tile_rows, a, max_items, max_out, st);
   return cudaErrorInvalidValue;
 }
 

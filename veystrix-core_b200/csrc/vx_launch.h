@@ -85,6 +85,10 @@ cudaError_t launch_gemv_mma(bool gateup, const MmaArgs& a, int max_items, int ma
 // Tiled expert pool: bytes of one record per (projection, 16-row m-tile) and
 // 128-input chunk: 1024 of packed words + 256 of scales and biases.
 constexpr int kTileRecordUnit = 1280;
+// Bytes of one (projection, 16-row tile, 128-input chunk) record unit: 1,024
+// of packed words, then the scale/bias pairs - 256 bytes for groups of 32,
+// 128 for native groups of 64 (one pair per row and 64 inputs).
+__host__ __device__ constexpr int tile_unit_bytes(int group) { return group == 64 ? 1152 : kTileRecordUnit; }
 
 // Tokens per work item of the tiled GEMV: two B operands of two tokens each
 // share every unpacked weight fragment.
@@ -176,6 +180,7 @@ struct PoolGemmArgs {
   int max_tasks;                // upper bound of item x row-tile tasks (set by the launcher)
   const int32_t* slot_of;       // partial residency: routed expert -> record slot (may be null)
   int slots;
+  int group;                    // records' quant group: 32 or 64 (native G64 pairs)
 };
 
 cudaError_t launch_gemm_pool(bool gateup, PoolGemmArgs a, const uint16_t* x, int64_t rows, int64_t ldx,
@@ -183,11 +188,11 @@ cudaError_t launch_gemm_pool(bool gateup, PoolGemmArgs a, const uint16_t* x, int
 cudaError_t launch_gather_border(const uint16_t* x, int64_t ldx, int K, const int32_t* src_rows,
                                  const int32_t* n_rows, int64_t rows, uint16_t* out, cudaStream_t st);
 
-int64_t tile_pool_bytes(int64_t experts, int out, int in, int nproj, int tile_rows);
+int64_t tile_pool_bytes(int64_t experts, int out, int in, int nproj, int tile_rows, int group = 32);
 cudaError_t launch_tile_pack(const vx_q4& a, const vx_q4& b, int nproj, int tile_rows, void* out,
-                             cudaStream_t st);
+                             cudaStream_t st, int group = 32);
 cudaError_t launch_gemv_tiled(bool gateup, int tile_rows, const TiledArgs& a, int max_items,
-                              int max_out, cudaStream_t st);
+                              int max_out, cudaStream_t st, int group = 32);
 
 // Upper bound of the number of work items for P routed positions over E
 // experts plus Ts shared-expert positions.

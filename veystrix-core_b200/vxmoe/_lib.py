@@ -90,6 +90,7 @@ SIGNATURES = {
     "vx_strerror": (ctypes.c_char_p, [ctypes.c_int]),
     "vx_last_cuda_error": (ctypes.c_char_p, []),
     "vx_q4_tiles_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32, c_int32]),
+    "vx_q4_tiles_bytes_group": (c_size_t, [c_int32, c_int32, c_int32, c_int32, c_int32, c_int32]),
     "vx_q4_tile": (ctypes.c_int, [ctypes.POINTER(VxQ4), ctypes.POINTER(VxQ4), c_int32, c_int32,
                                   P, c_size_t, P]),
     "vx_q4_dequant": (ctypes.c_int, [ctypes.POINTER(VxQ4), c_int32, P, P]),

@@ -211,7 +211,7 @@ def shard_weights(w: "ops.MoEWeights", rank: int, world: int) -> "ops.MoEWeights
     sl = slice(rank * El, (rank + 1) * El)
 
     def part(p):
-        return ops.Q4Projection(p.weight[sl], p.scales[sl], p.biases[sl])
+        return ops.Q4Projection(p.weight[sl], p.scales[sl], p.biases[sl], p.group_size)
 
     out = ops.MoEWeights(part(w.gate), part(w.up), part(w.down), router_w=w.router_w,
                          shared_gate=w.shared_gate, shared_up=w.shared_up,

@@ -14,8 +14,9 @@ The checkpoint layout is the one the reference's Flash-Next loader reads
 The quantization of each layer is inferred from its tensor shapes, as the
 reference does per layer (``infer_switch_quantization``, loader.py:379-401),
 because converted checkpoints may mix layouts.  The kernels take 4-bit codes
-in groups of 32; coarser groups (64, ...) are expanded to that form at load
-time (Q4Projection.from_group), other layouts are rejected with ValueError.
+in groups of 32, or of 64 kept as stored in the tiled records; other
+multiples of 32 (128, ...) are expanded to groups of 32 at load time
+(Q4Projection.from_group), other layouts are rejected with ValueError.
 
 The reader is a small safetensors parser (8-byte little-endian header length,
 a JSON header, then the raw tensors); tensors are memory-mapped and copied to
@@ -149,23 +150,28 @@ def moe_layers(store: SafeTensorStore) -> List[int]:
     return sorted(out)
 
 
-def _proj(store: SafeTensorStore, prefix: str, device) -> "ops.Q4Projection":
+def _proj(store: SafeTensorStore, prefix: str, device, native: bool = False) -> "ops.Q4Projection":
     """One 4-bit projection; a coarser grouping (64, 128 ...) is expanded to
-    the kernels' groups of 32 (Q4Projection.from_group)."""
+    the kernels' groups of 32 (Q4Projection.from_group), except groups of 64
+    when `native` is set, which stay as stored."""
     inputs = int(store.shape(f"{prefix}.weight")[-1]) * 8
     groups = int(store.shape(f"{prefix}.scales")[-1])
     if groups <= 0 or inputs % groups:
         raise ValueError(f"{prefix}: {inputs} inputs do not split into {groups} groups")
     return ops.Q4Projection.from_group(store.tensor(f"{prefix}.weight", device),
                                        store.tensor(f"{prefix}.scales", device),
-                                       store.tensor(f"{prefix}.biases", device), inputs // groups)
+                                       store.tensor(f"{prefix}.biases", device), inputs // groups,
+                                       native=native)
 
 
 def load_moe_layer(store: SafeTensorStore, index: int, top_k: int, device=None,
-                   pack: bool = True) -> "ops.MoEWeights":
+                   pack: bool = True, native_groups: bool = True) -> "ops.MoEWeights":
     """The routed MoE block of decoder layer `index` as MoEWeights (routed
     experts, shared expert and its gate, router), packed into the tiled pool
-    unless `pack` is False.  `top_k` is the model's num_experts_per_tok."""
+    unless `pack` is False.  `top_k` is the model's num_experts_per_tok.
+    With `native_groups` a G64 layer keeps its scale/bias pairs as stored
+    (half the metadata bytes; always packed, the kernels read G64 from the
+    tiled records only); otherwise they are expanded to groups of 32."""
     device = torch.device(device) if device is not None else torch.device("cuda")
     mlp = layer_prefix(index)
     sw = f"{mlp}.switch_mlp"
@@ -176,17 +182,25 @@ def load_moe_layer(store: SafeTensorStore, index: int, top_k: int, device=None,
         raise ValueError(f"layer {index}: {bits}-bit codes in groups of {group}; the kernels take 4-bit "
                          "codes in groups of a multiple of 32")
     shared = f"{mlp}.shared_expert.gate_proj.weight" in store
+    # native only when every bank bound for the tiled pool (routed, and the
+    # shared expert stored beside them) has groups of 64
+    nat = native_groups and group == ops.NATIVE_GROUP
+    for q in [f"{sw}.{part}" for part in ("gate_proj", "up_proj", "down_proj")] + \
+            ([f"{mlp}.shared_expert.{part}" for part in ("gate_proj", "up_proj", "down_proj")]
+             if shared else []):
+        inputs = int(store.shape(f"{q}.weight")[-1]) * 8
+        nat = nat and int(store.shape(f"{q}.scales")[-1]) * group == inputs
     w = ops.MoEWeights(
-        _proj(store, f"{sw}.gate_proj", device), _proj(store, f"{sw}.up_proj", device),
-        _proj(store, f"{sw}.down_proj", device),
+        _proj(store, f"{sw}.gate_proj", device, nat), _proj(store, f"{sw}.up_proj", device, nat),
+        _proj(store, f"{sw}.down_proj", device, nat),
         router_w=store.tensor(f"{mlp}.gate.weight", device),
-        shared_gate=_proj(store, f"{mlp}.shared_expert.gate_proj", device) if shared else None,
-        shared_up=_proj(store, f"{mlp}.shared_expert.up_proj", device) if shared else None,
-        shared_down=_proj(store, f"{mlp}.shared_expert.down_proj", device) if shared else None,
+        shared_gate=_proj(store, f"{mlp}.shared_expert.gate_proj", device, nat) if shared else None,
+        shared_up=_proj(store, f"{mlp}.shared_expert.up_proj", device, nat) if shared else None,
+        shared_down=_proj(store, f"{mlp}.shared_expert.down_proj", device, nat) if shared else None,
         shared_expert_gate=(_proj(store, f"{mlp}.shared_expert_gate", device)
                             if f"{mlp}.shared_expert_gate.weight" in store else None),
         top_k=top_k, device=device)
-    return w.pack() if pack else w
+    return w.pack() if pack and w.pool is None else w
 
 
 # --------------------------------------------------------------------------

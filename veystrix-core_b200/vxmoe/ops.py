@@ -18,6 +18,7 @@ from . import _lib
 from ._lib import VxMoEWeights, VxQ4
 
 GROUP_SIZE = 32
+NATIVE_GROUP = 64   # the one coarser grouping the tiled records keep as stored
 BITS = 4
 
 
@@ -88,11 +89,15 @@ _WS = _Workspace()
 class Q4Projection:
     """Packed expert rows of one projection (``Q4G32Projection``,
     ``models/flashnext/metal_runtime.py:39-45``): weight uint32
-    [experts, out, in/8], scales/biases bf16 [experts, out, in/32]."""
+    [experts, out, in/8], scales/biases bf16 [experts, out, in/group_size].
+    group_size is 32, or 64 for a bank kept in its checkpoint grouping
+    (``from_group(..., native=True)``), which the kernels read only from a
+    tiled pool."""
 
     weight: torch.Tensor
     scales: torch.Tensor
     biases: torch.Tensor
+    group_size: int = GROUP_SIZE
 
     @property
     def experts(self) -> int:
@@ -106,7 +111,8 @@ class Q4Projection:
     def in_features(self) -> int:
         return int(self.weight.shape[2]) * 8
 
-    def validate(self, group_size: int = GROUP_SIZE) -> None:
+    def validate(self, group_size: Optional[int] = None) -> None:
+        group_size = self.group_size if group_size is None else int(group_size)
         w, s, b = self.weight, self.scales, self.biases
         for name, t in (("weight", w), ("scales", s), ("biases", b)):
             _require_cuda(t, name)
@@ -118,25 +124,33 @@ class Q4Projection:
             raise TypeError("Q4 scales and biases must be bfloat16")
         if w.dim() != 3:
             raise ValueError(f"weight shape {tuple(w.shape)} must be [experts, out, in/8]")
+        if group_size <= 0 or (w.shape[2] * 8) % group_size:
+            raise ValueError(f"{w.shape[2] * 8} inputs do not split into groups of {group_size}")
         meta = (w.shape[0], w.shape[1], w.shape[2] * 8 // group_size)
         if tuple(s.shape) != meta or tuple(b.shape) != meta:
             raise ValueError(f"Q4/G{group_size} scales and biases have an invalid shape")
 
     def vx(self) -> VxQ4:
         return VxQ4(self.weight.data_ptr(), self.scales.data_ptr(), self.biases.data_ptr(),
-                    self.experts, self.out_features, self.in_features, GROUP_SIZE)
+                    self.experts, self.out_features, self.in_features, self.group_size)
 
     @staticmethod
     def from_group(weight: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
-                   group_size: int) -> "Q4Projection":
+                   group_size: int, native: bool = False) -> "Q4Projection":
         """A projection quantized in groups of `group_size` (a multiple of
         32, e.g. the G64 checkpoints of models/flashnext/metal_runtime.py:
-        950-971) in the kernels' group-32 form: every scale and bias is
-        repeated for each 32-input group it covers.  Each dequantized weight
-        scale*q + bias is unchanged; a GEMV's float sums run per 32 inputs
-        instead of per group, within the block tolerance of the G64 result."""
+        950-971).  With `native` a G64 bank is kept as stored (one scale/bias
+        pair per 64 inputs; the tiled records carry it that way).  Otherwise
+        it takes the kernels' group-32 form: every scale and bias is repeated
+        for each 32-input group it covers.  Each dequantized weight
+        scale*q + bias is the same either way, and so are the kernels'
+        products: their sums run per 32 inputs in both forms."""
         if group_size % GROUP_SIZE or group_size <= 0:
             raise ValueError(f"group size {group_size} is not a multiple of {GROUP_SIZE}")
+        if native and group_size == NATIVE_GROUP:
+            p = Q4Projection(weight, scales, biases, NATIVE_GROUP)
+            p.validate()
+            return p
         r = group_size // GROUP_SIZE
         if r > 1:
             scales = scales.repeat_interleave(r, dim=-1).contiguous()
@@ -205,6 +219,14 @@ class MoEWeights:
         self.device = self.gate.weight.device
         for p in self.projections():
             p.validate()
+        # routed and shared banks share one grouping: 32, or 64 kept natively
+        # (read from the tiled pool only); the shared-expert gate is group 32
+        self.group_size = self.gate.group_size
+        banks = [p for p in self.projections() if p is not self.shared_expert_gate]
+        if any(p.group_size != self.group_size for p in banks):
+            raise ValueError("routed and shared banks must share one group size")
+        if self.shared_expert_gate is not None and self.shared_expert_gate.group_size != GROUP_SIZE:
+            raise ValueError(f"the shared-expert gate takes groups of {GROUP_SIZE}")
         E, I, d = self.num_experts, self.gate.out_features, self.hidden
         if self.up.weight.shape != self.gate.weight.shape:
             raise ValueError("gate and up projection widths must match")
@@ -231,6 +253,9 @@ class MoEWeights:
         # holding this layer's routed records, and the layer's key in it
         self.slot_pool = None
         self.slot_layer = None
+        if self.group_size != GROUP_SIZE:
+            # native G64 banks are read from the tiled records only
+            self.pack()
 
     def pack(self, down_rows: int = 32) -> "MoEWeights":
         """Re-tile the experts into the resident pool the decode kernels
@@ -286,24 +311,26 @@ class MoEWeights:
     @staticmethod
     def random(num_experts=512, hidden=2048, inter=512, shared_inter=512, top_k=10,
                device=None, generator=None, router_experts=None,
-               router_generator=None) -> "MoEWeights":
+               router_generator=None, group_size: int = GROUP_SIZE) -> "MoEWeights":
         """Synthetic weights with the benchmark distributions: codes uniform
         in 0..15, scale = bf16(|N(0, 0.02)|/8), bias = -8*scale, router
         bf16 N(0, 0.02).  An expert-parallel shard passes the full expert
         count as `router_experts` and a generator shared by all ranks as
-        `router_generator` (router and shared expert are replicated)."""
+        `router_generator` (router and shared expert are replicated).
+        group_size 64 makes native G64 banks (packed at construction); the
+        shared-expert gate stays group 32."""
         device = torch.device(device) if device is not None else torch.device("cuda")
         g = generator
         gr = router_generator if router_generator is not None else generator
         n_router = router_experts if router_experts is not None else num_experts
 
-        def bank(E, out, inn):
+        def bank(E, out, inn, gs=group_size):
             w = torch.randint(-2**31, 2**31 - 1, (E, out, inn // 8), dtype=torch.int32,
                               device=device, generator=g).view(torch.uint32)
-            s = (torch.randn((E, out, inn // GROUP_SIZE), device=device, generator=g).abs()
+            s = (torch.randn((E, out, inn // gs), device=device, generator=g).abs()
                  * 0.02 / 8).to(torch.bfloat16)
             b = (s.float() * -8.0).to(torch.bfloat16)
-            return Q4Projection(w, s, b)
+            return Q4Projection(w, s, b, gs)
 
         gate = bank(num_experts, inter, hidden)
         up = bank(num_experts, inter, hidden)
@@ -312,7 +339,7 @@ class MoEWeights:
         router = (torch.randn((n_router, hidden), device=device, generator=g) * 0.02).to(torch.bfloat16)
         sh = [bank(1, shared_inter, hidden), bank(1, shared_inter, hidden), bank(1, hidden, shared_inter)] \
             if shared_inter else [None, None, None]
-        seg = bank(1, 1, hidden) if shared_inter else None
+        seg = bank(1, 1, hidden, GROUP_SIZE) if shared_inter else None
         return MoEWeights(gate, up, down, router, *sh, seg, top_k=top_k, device=device,
                           check_router=n_router == num_experts)
 
@@ -322,10 +349,11 @@ def tile_bank(a: Q4Projection, b: Optional[Q4Projection] = None, tile_rows: int 
     pair) in the tiled pool layout, uint8 on a's device."""
     nproj = 1 if b is None else 2
     lib = _lib.load()
-    n = lib.vx_q4_tiles_bytes(a.experts, a.out_features, a.in_features, nproj, tile_rows)
+    n = lib.vx_q4_tiles_bytes_group(a.experts, a.out_features, a.in_features, nproj, tile_rows,
+                                    a.group_size)
     if n == 0:
         raise ValueError(f"no tiled layout for {a.out_features}x{a.in_features}, "
-                         f"nproj {nproj}, tile_rows {tile_rows}")
+                         f"nproj {nproj}, tile_rows {tile_rows}, group {a.group_size}")
     rec = torch.empty(n, dtype=torch.uint8, device=a.weight.device)
     qa = a.vx()
     qb = b.vx() if b is not None else None
@@ -345,6 +373,7 @@ class TiledPool:
         if down_rows not in (16, 32):
             raise ValueError("down_rows must be 16 or 32")
         self.down_rows = down_rows
+        self.group_size = w.group_size
         self.gate_up = tile_bank(w.gate, w.up, 16)
         self.down = tile_bank(w.down, None, down_rows)
         self.shapes = {"gate_up": (w.num_experts, w.intermediate, w.hidden, 2, 16),
@@ -360,7 +389,8 @@ class TiledPool:
         for name, (E, out, inn, nproj, rows) in self.shapes.items():
             t = getattr(self._struct, name)
             t.records = getattr(self, name).data_ptr()
-            t.experts, t.out, t.in_, t.group_size, t.nproj, t.tile_rows = E, out, inn, GROUP_SIZE, nproj, rows
+            t.experts, t.out, t.in_, t.nproj, t.tile_rows = E, out, inn, nproj, rows
+            t.group_size = self.group_size
             setattr(self._struct, name, t)
 
     def vx(self) -> "_lib.VxMoEPool":
@@ -381,8 +411,8 @@ def dequantize(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
     ``metal_runtime.py:770-777``); w may be [out, in/8] or [E, out, in/8]."""
     if w.dim() == 2:
         w, scales, biases = w[None], scales[None], biases[None]
-    p = Q4Projection(w.contiguous(), scales.contiguous(), biases.contiguous())
-    p.validate(group_size)
+    p = Q4Projection(w.contiguous(), scales.contiguous(), biases.contiguous(), int(group_size))
+    p.validate()
     out = torch.empty((p.out_features, p.in_features), dtype=torch.float32, device=w.device)
     q = p.vx()
     _lib.check(_lib.load().vx_q4_dequant(ctypes.byref(q), int(expert), out.data_ptr(),

@@ -94,9 +94,9 @@ class SlotAssigner:
         return gone
 
 
-def _tile_bytes(out: int, inn: int, nproj: int, tile_rows: int) -> int:
-    """Bytes of one expert's tiled records (``vx_q4_tiles_bytes`` for one expert)."""
-    return int(_lib.load().vx_q4_tiles_bytes(1, out, inn, nproj, tile_rows))
+def _tile_bytes(out: int, inn: int, nproj: int, tile_rows: int, group_size: int) -> int:
+    """Bytes of one expert's tiled records (``vx_q4_tiles_bytes_group`` for one expert)."""
+    return int(_lib.load().vx_q4_tiles_bytes_group(1, out, inn, nproj, tile_rows, group_size))
 
 
 class _Layer:
@@ -111,17 +111,21 @@ class SlotPool:
     """`slots` experts' tiled records on the device, shared by the layers
     attached to it (``attach``).  Records of one slot: gate/up interleaved
     in 16-row tiles, then down in `down_rows`-row tiles, the layout of
-    ``MoEWeights.pack``."""
+    ``MoEWeights.pack``.  Every layer of a pool shares its quant grouping
+    (`group_size` 32, or 64 for native G64 records)."""
 
-    def __init__(self, slots: int, hidden: int, intermediate: int, down_rows: int = 32, device=None):
+    def __init__(self, slots: int, hidden: int, intermediate: int, down_rows: int = 32, device=None,
+                 group_size: int = 32):
         if down_rows not in (16, 32):
             raise ValueError("down_rows must be 16 or 32")
         self.device = torch.device(device) if device is not None else torch.device("cuda")
         self.hidden, self.intermediate, self.down_rows = int(hidden), int(intermediate), int(down_rows)
-        self.gu_stride = _tile_bytes(self.intermediate, self.hidden, 2, 16)
-        self.dn_stride = _tile_bytes(self.hidden, self.intermediate, 1, down_rows)
+        self.group_size = int(group_size)
+        self.gu_stride = _tile_bytes(self.intermediate, self.hidden, 2, 16, self.group_size)
+        self.dn_stride = _tile_bytes(self.hidden, self.intermediate, 1, down_rows, self.group_size)
         if self.gu_stride == 0 or self.dn_stride == 0:
-            raise ValueError(f"no tiled layout for hidden {hidden}, intermediate {intermediate}")
+            raise ValueError(f"no tiled layout for hidden {hidden}, intermediate {intermediate}, "
+                             f"group {group_size}")
         self.assigner = SlotAssigner(slots)
         self.gate_up = torch.zeros(int(slots) * self.gu_stride, dtype=torch.uint8, device=self.device)
         self.down = torch.zeros(int(slots) * self.dn_stride, dtype=torch.uint8, device=self.device)
@@ -139,6 +143,8 @@ class SlotPool:
         expert resident yet).  The shared expert stays on the device."""
         if w.hidden != self.hidden or w.intermediate != self.intermediate:
             raise ValueError("layer shapes differ from the slot pool's")
+        if w.group_size != self.group_size:
+            raise ValueError(f"layer groups of {w.group_size} differ from the slot pool's {self.group_size}")
         if getattr(w, "slot_pool", None) is not None:
             raise ValueError("the layer is already attached to a slot pool")
         if w.pool is None or w.pool.down_rows != self.down_rows:
@@ -151,7 +157,7 @@ class SlotPool:
         for name in ("gate", "up", "down"):
             p = getattr(w, name)
             setattr(w, name, type(p)(p.weight.cpu().pin_memory(), p.scales.cpu().pin_memory(),
-                                     p.biases.cpu().pin_memory()))
+                                     p.biases.cpu().pin_memory(), p.group_size))
         w.pool.gate_up = self.gate_up
         w.pool.down = self.down
         table = torch.full((E,), -1, dtype=torch.int32, device=self.device)
