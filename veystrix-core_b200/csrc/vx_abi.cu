@@ -213,6 +213,11 @@ static DecodeScratch carve_decode(Carver& c, int T, const BlockDims& dm) {
   return s;
 }
 
+// Words of s.err, cleared before each call's expert pipeline: [0] dropped
+// ids, [1] pipeline timeouts, [2] [3] the task counters of the gate/up and
+// down GEMVs (tasks handed out dynamically).
+constexpr int kErrWords = 4;
+
 // extra_zeroed: ints placed right after s.err, so that one memset clears
 // both (the block call keeps the router's arrival counters there).
 static ExpertScratch carve_experts(Carver& c, int T, const BlockDims& dm, int extra_zeroed = 0) {
@@ -225,7 +230,7 @@ static ExpertScratch carve_experts(Carver& c, int T, const BlockDims& dm, int ex
   s.active = c.take<int32_t>(dm.E + 1);
   s.n_active = c.take<int32_t>(1);
   s.src_rows = c.take<int32_t>(P + Ts);
-  s.err = c.take<int32_t>(2 + extra_zeroed);   // [0] dropped ids, [1] pipeline timeouts
+  s.err = c.take<int32_t>(kErrWords + extra_zeroed);
   s.max_items = max_items_bound(P, dm.E, int(Ts));
   s.items = c.take<int32_t>(3 * int64_t(s.max_items));
   s.n_items = c.take<int32_t>(1);
@@ -241,6 +246,7 @@ static ExpertScratch carve_experts(Carver& c, int T, const BlockDims& dm, int ex
     s.xb = c.take<uint16_t>((P + Ts) * dm.d);   // x gathered into sorted order
   } else if (path == kPathGemvTiled) {
     s.act = c.take<unsigned char>(act_record_bytes(dm.d, P + Ts));
+    s.h = c.take<uint16_t>((P + Ts) * s.ldh);
     s.hrec = c.take<unsigned char>(act_record_bytes(int(s.ldh), P + Ts));
   } else {
     s.h = c.take<uint16_t>((P + Ts) * s.ldh);
@@ -267,7 +273,7 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
   const int Ts = dm.shared ? T : 0;
   cudaError_t e = cudaSuccess;
   if (!err_zeroed) {
-    e = cudaMemsetAsync(s.err, 0, 2 * sizeof(int32_t), st);
+    e = cudaMemsetAsync(s.err, 0, kErrWords * sizeof(int32_t), st);
     if (e != cudaSuccess) return vx_cuda_fail(e);
   }
   const ExpertPath path = expert_path(T, dm);
@@ -358,8 +364,10 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
   if (path == kPathGemvTiled) {
     // activation records of the sorted positions (valid count: offsets[E+1])
     e = launch_act_records(x, dm.d, dm.d, s.src_rows, s.offsets + dm.E + 1, P + Ts, s.act, st);
-    if (e == cudaSuccess && (dm.I % 128 || dm.Is % 128))   // zero chunk padding of h
-      e = cudaMemsetAsync(s.hrec, 0, size_t(act_record_bytes(int(s.ldh), P + Ts)), st);
+    // h records are built over ldh = max(I, Is) columns: when the routed and
+    // shared widths differ, the narrower rows' columns up to ldh must read 0
+    if (e == cudaSuccess && dm.shared && dm.I != dm.Is)
+      e = cudaMemsetAsync(s.h, 0, size_t(P + Ts) * size_t(s.ldh) * sizeof(uint16_t), st);
   } else {
     e = launch_xprep(x, T, dm.d, s.xb, s.xs, s.ldxs, st);
   }
@@ -383,10 +391,15 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
     a.n_items = s.n_items;
     a.act = s.act;
     a.act_rows = P + Ts;
-    a.hrec = s.hrec;
+    a.out = s.h;
+    a.ldo = s.ldh;
+    a.task_ctr = s.err + 2;
     e = launch_gemv_tiled(true, pl.gate_up.tile_rows, a, s.max_items, int(s.ldh), st, pl.gate_up.group_size);
     if (e != cudaSuccess) return vx_cuda_fail(e);
     profile_mark(st, "gate_up_swiglu");
+    e = launch_act_records(s.h, s.ldh, int(s.ldh), nullptr, s.offsets + dm.E + 1, P + Ts, s.hrec, st);
+    if (e != cudaSuccess) return vx_cuda_fail(e);
+    profile_mark(st, "h_records");
 
     TiledArgs b{};
     b.err = s.err + 1;
@@ -403,6 +416,7 @@ static int run_experts(const uint16_t* x, int T, const int32_t* routes, const vx
     b.n_items = s.n_items;
     b.act = s.hrec;
     b.act_rows = P + Ts;
+    b.task_ctr = s.err + 3;
     b.out = s.yd;
     b.ldo = dm.d;
     e = launch_gemv_tiled(false, pl.down.tile_rows, b, s.max_items, dm.d, st, pl.down.group_size);
@@ -858,11 +872,11 @@ int vx_moe_block(const uint16_t* x, int32_t T, const vx_moe_weights* W, uint16_t
   uint16_t* sg = c.take<uint16_t>(T);
   const int n_counters = int(router_counters(T));
   ExpertScratch es = carve_experts(c, T, dm, n_counters);
-  int32_t* counters = es.err + 2;
+  int32_t* counters = es.err + kErrWords;
   if (!inds) inds = inds_ws;
   if (!weights) weights = w_ws;
   // one memset clears the error words and the router's arrival counters
-  cudaError_t e = cudaMemsetAsync(es.err, 0, size_t(2 + n_counters) * sizeof(int32_t), st);
+  cudaError_t e = cudaMemsetAsync(es.err, 0, size_t(kErrWords + n_counters) * sizeof(int32_t), st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
   // A decode-sized batch (at most kPermSmall routes) is sorted by expert in
   // the router's last CTA.
@@ -1020,7 +1034,7 @@ int vx_ep_experts(const vx_ep_comm* comm, int32_t T, const vx_moe_weights* W, vo
   const int rows = T * comm->world;
   Carver c(workspace);
   ExpertScratch es = carve_experts(c, rows, dm);
-  cudaError_t e = cudaMemsetAsync(es.err, 0, 2 * sizeof(int32_t), st);
+  cudaError_t e = cudaMemsetAsync(es.err, 0, kErrWords * sizeof(int32_t), st);
   if (e != cudaSuccess) return vx_cuda_fail(e);
   e = launch_ep_wait_dispatch(a, st);
   if (e != cudaSuccess) return vx_cuda_fail(e);

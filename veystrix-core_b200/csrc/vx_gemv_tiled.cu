@@ -2,13 +2,14 @@
 //
 // The MLX-layout kernel's scheme (vx_gemv_mma.cu: mma.sync m16n8k16 with the
 // block-diagonal B, MLX's qmv formula per group folded into the epilogue),
-// but every operand arrives by bulk copy from records laid out in the order
-// the warp consumes them.  The down projection unpacks nibbles to bf16 128+q
-// by one lop3 (and a shift) per pair, as the MLX-layout kernel does; the
-// gate/up projections, which read act_records_kernel's f16 records, unpack
-// to f16 subnormals q * 2^-24 and 16q * 2^-24 by one mask per pair and one
-// shift per word (the kernel is bound by the ALU pipe, and the unpack is most
-// of its ALU work).  Both forms give exact products q * x.
+// but every operand arrives by copies from records laid out in the order
+// the warp consumes them.  Both passes read act_records_kernel's f16 records
+// (x for gate/up, h for down) and unpack the nibbles to f16 subnormals
+// q * 2^-24 and 16q * 2^-24 by one mask per pair and one shift per word (the
+// kernel is bound by the ALU pipe, and the unpack is most of its ALU work);
+// the products q * x are exact.  (The bf16 128 + q unpack by one lop3 and a
+// shift per pair, with the group sums formed on the tensor pipe, remains for
+// bf16 records without sums: kActF16 false.)
 //
 // Weight records (the pool, re-tiled once at load time).  One record = one
 // warp's 128-input chunk of one row tile:
@@ -113,22 +114,29 @@ VX_DEVICE void issue_act(bool leader, uint32_t bar, uint32_t dst_x, const void* 
 // so the heavy stream goes the other way.
 constexpr bool kWeightsByLsu = true;
 
+// Depth of the per-warp task queue from producer to consumer: the producer
+// runs at most STAGES - 1 records (so as many tasks) ahead.
+constexpr int kTaskFifo = 16;
+
 template <bool GATEUP, int MT, bool XMMA, int STAGES, int WARPS, int GS>
 __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
     gemv_tiled_kernel(const __grid_constant__ TiledArgs a) {
   chain_wait();
   constexpr int NP = GATEUP ? 2 : 1;
   // gate/up reads act_records_kernel's f16 records; down reads h in bf16
-  constexpr bool F16 = GATEUP && kActF16;
+  constexpr bool F16 = kActF16;
   constexpr int kRec = NP * MT * tile_unit_bytes(GS);
   constexpr int kSbUnit = tile_unit_bytes(GS) - 1024;   // scale/bias bytes per (p, m)
   constexpr int kWBytes = NP * MT * 1024;
   constexpr int kXOff = kRec;                       // [token][kActRecord]
   constexpr int kStage = kRec + kTiledItemChunk * kActRecord;
   static_assert(kStage % 128 == 0, "stage size");
+  static_assert(STAGES < kTaskFifo, "task queue depth");
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) uint64_t bars[WARPS][STAGES];
   __shared__ __align__(16) uint32_t zero16[4];
+  // tasks from the producer cursor to the consumer, in issue order (-1: end)
+  __shared__ int tfifo[WARPS][kTaskFifo];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   if (threadIdx.x < 4) zero16[threadIdx.x] = 0u;
@@ -149,13 +157,29 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
   const int64_t act_pitch = a.act_rows * kActRecord;   // bytes per chunk of activations
 
   // ---- producer cursor: task ti, chunk ci ----
+  // The first wave is static (task = global warp index); later tasks come
+  // from a.task_ctr in the order warps ask, so a warp whose tasks ran short
+  // (one-token items) takes more of them.  Lane 0 asks one task ahead: the
+  // atomic's latency hides behind a whole task.
   int ti = blockIdx.x * WARPS + warp, ci = 0;
+  const bool dyn = a.task_ctr != nullptr;
+  int tnext = 0;
+  if (dyn && lane == 0) tnext = atomicAdd(a.task_ctr, 1);
+  auto advance = [&]() {
+    if (dyn) {
+      ti = nw + __shfl_sync(0xFFFFFFFFu, tnext, 0);
+      if (lane == 0) tnext = atomicAdd(a.task_ctr, 1);
+    } else {
+      ti += nw;
+    }
+  };
+  int qt = 0;   // tasks pushed to tfifo
   int inch = 0;
   uint32_t ixbytes = 0;
   const unsigned char* irec = nullptr;
   const unsigned char* iact = nullptr;
   auto seek = [&]() {   // first valid task at or after ti
-    for (; ti < total; ti += nw) {
+    for (; ti < total; advance()) {
       TiledTask k;
       if (!decode_task<MT>(a, ti, k)) continue;
       const int rb = k.row0 / (16 * MT);
@@ -164,8 +188,10 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
              int64_t(rb) * inch * kRec;
       iact = a.act + int64_t(k.p0) * kActRecord;
       ixbytes = uint32_t(k.cnt) * kActRecord;
+      tfifo[warp][qt++ % kTaskFifo] = ti;   // every lane writes the same value
       return;
     }
+    tfifo[warp][qt++ % kTaskFifo] = -1;
   };
   int st_issue = 0, st_use = 0;
   uint32_t parity_bits = 0;   // bit s: parity expected next on stage s
@@ -185,7 +211,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
     st_issue = st_issue == STAGES - 1 ? 0 : st_issue + 1;
     if (++ci == inch) {
       ci = 0;
-      ti += nw;
+      advance();
       seek();
     }
   };
@@ -377,13 +403,10 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
           const int row = k.row0 + 16 * m + g + 8 * h;
           if (row >= k.N) continue;
           if (GATEUP) {
-            // h is the down projection's input: store it as an activation record
+            // h, the down projection's input, as plain rows (its f16 records
+            // need the largest |h| of each 128 rows, from other tasks)
             const float v = silu_mul_bf16(bf16r(acc[0][m][q][h]), bf16r(acc[NP - 1][m][q][h]));
-            const int e8 = row & 7;
-            const int slot = e8 < 4 ? 2 * e8 : 2 * (e8 - 4) + 1;
-            const int64_t off = (row >> 7) * act_pitch + pos * kActRecord +
-                                ((((row >> 3) & 3) * 4 + ((row >> 5) & 3)) * 16) + slot * 2;
-            *reinterpret_cast<uint16_t*>(a.hrec + off) = f32_to_bf16(v);
+            a.out[pos * a.ldo + row] = f32_to_bf16(v);
           } else {
             a.out[pos * a.ldo + row] = f32_to_bf16(acc[0][m][q][h]);
           }
@@ -391,9 +414,11 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
     }
   };
 
-  for (int t = blockIdx.x * WARPS + warp; t < total; t += nw) {
+  for (int qh = 0;; ++qh) {
+    const int t = tfifo[warp][qh % kTaskFifo];   // written by this lane in seek()
+    if (t < 0) break;
     TiledTask k;
-    if (!decode_task<MT>(a, t, k)) continue;   // warp-uniform
+    decode_task<MT>(a, t, k);   // a valid task (seek() skips the others)
     if (k.cnt > 2)
       run(k, std::integral_constant<int, 2>());
     else
@@ -408,9 +433,9 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
 // One thread per 8-input block of a (position, chunk); the record's 16 blocks
 // are 16 consecutive threads.  The block goes to lane-order slot (i*4 + c) in
 // B order (words (x0,x4) (x1,x5) (x2,x6) (x3,x7)) as f16, for the f16 unpack
-// of the gate/up GEMV (kActF16), whose weights enter the MMA as f16
-// subnormals q * 2^-24 (nibbles at bits 0-3) or 16q * 2^-24 (bits 4-7, no
-// shift):
+// of the GEMV (kActF16; x rows for gate/up, h rows for down), whose weights
+// enter the MMA as f16 subnormals q * 2^-24 (nibbles at bits 0-3) or
+// 16q * 2^-24 (bits 4-7, no shift):
 //
 //   * the record is scaled by 2^e, e chosen from its largest |x| so that it
 //     lands in [2^13, 2^14): every bf16 input converts exactly (f16 keeps 11
@@ -636,8 +661,8 @@ static cudaError_t launch_gemv_tiled_g(bool gateup, int tile_rows, const TiledAr
     if (tile_rows != 16) return cudaErrorInvalidValue;
     return launch_tiled_t<true, 1, false, GS>(a, max_items, max_out, st);
   }
-  if (tile_rows == 32) return launch_tiled_t<false, 2, true, GS>(a, max_items, max_out, st);
-  if (tile_rows == 16) return launch_tiled_t<false, 1, true, GS>(a, max_items, max_out, st);
+  if (tile_rows == 32) return launch_tiled_t<false, 2, !kActF16, GS>(a, max_items, max_out, st);
+  if (tile_rows == 16) return launch_tiled_t<false, 1, !kActF16, GS>(a, max_items, max_out, st);
   return cudaErrorInvalidValue;
 }
 

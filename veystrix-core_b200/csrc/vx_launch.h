@@ -102,8 +102,9 @@ constexpr int kTiledItemChunk = 4;
 constexpr int kActRecord = 320;
 constexpr int kActXsum = 256;
 // act_records_kernel writes f16 records (scaled by a power of two per
-// record); the gate/up GEMV reads them with the f16 unpack.  h records
-// (down's input) stay bf16 with group sums formed on the tensor pipe.
+// record) of x (gate/up's input) and of h (down's input, from the plain h
+// rows the gate/up pass writes); both GEMV passes read them with the f16
+// unpack.
 constexpr bool kActF16 = true;
 
 struct TiledArgs {
@@ -117,13 +118,14 @@ struct TiledArgs {
   const int32_t* items;         // [n][3] expert, first position, count (<= kTiledItemChunk)
   const int32_t* n_items;
   const unsigned char* act;     // activation records [chunk][act_rows][kActRecord]
-  int64_t act_rows;             // positions per chunk of act (and of hrec)
-  unsigned char* hrec;          // gate/up: h written as activation records (no sums)
-  uint16_t* out;                // projection: plain rows [position][ldo]
+  int64_t act_rows;             // positions per chunk of act
+  uint16_t* out;                // plain rows [position][ldo]: h (gate/up) or the projection
   int64_t ldo;
   int tiles_per_item;           // set by the launcher
   const int32_t* slot_of;       // partial residency: routed expert -> record slot (may be null)
   int slots;
+  int32_t* task_ctr;            // zero at launch: tasks after the first wave are taken from it
+                                // (null: a static round robin)
 };
 
 // x rows (token src_rows[p] for position p < *n_rows, or p when src_rows is
