@@ -50,6 +50,18 @@ VX_DEVICE uint4 lds128(uint32_t addr) {
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
   return v;
 }
+// Named CTA barrier `id` (1..15; 0 is __syncthreads') over `count` threads,
+// a multiple of 32: arrive signals without waiting (the producer's side,
+// release), sync waits until `count` threads have arrived or synced.  The
+// non-aligned forms: each thread counts for itself, so a warp that diverged
+// just before (a lane-0 branch) still counts 32 and no more.
+VX_DEVICE void named_arrive(int id, int count) {
+  asm volatile("barrier.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+VX_DEVICE void named_sync(int id, int count) {
+  asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 VX_DEVICE uint32_t lds32(uint32_t addr) {
   uint32_t v;
   asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));

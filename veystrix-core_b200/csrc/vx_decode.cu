@@ -59,6 +59,7 @@ constexpr int kDecWarps = kDecThreads / 32;
 constexpr int kDecStage = 2560;         // one pool record (largest: gate/up pair, 32 down rows)
 constexpr int kDecLogitRows = 4;        // experts per logit CTA
 constexpr int kDecMaxRoutes = 64;       // T*k for the one-warp sort
+static_assert(kDecWarps >= 5 + kDecodeMaxT, "routing warps: 0 plans, 1..T select, 5..4+T weigh");
 // gate/up partial sums: [task][warp][projection][row 16][token T] float in a
 // region of kDecPartBytes, so a batch holds kDecPartBytes / (1 KB * T) tasks
 constexpr int kDecPartBytes = 16384;
@@ -98,7 +99,7 @@ VX_HOST_DEVICE inline DecLayout dec_layout(int T, int d, int k, int I, int Is, i
   off += kDecPartBytes;
   L.off_tab = off;                                      // routing tables
   off += dec_align(kDecMaxRoutes * 4 * 2 + kDecMaxRoutes * 2 + (kDecMaxRoutes + 16) * 4 +
-                       (kDecMaxRoutes + 2) * 4 * 3 + 64 * 4,
+                       (kDecMaxRoutes + 2) * 4 * 3 + 64 * 4 + kDecMaxRoutes * 4,
                    128);
   L.off_bar = off;                                      // ring mbarriers + the shared-down one
   const int avail = smem_cap - off;
@@ -122,6 +123,7 @@ struct DecTab {
   int32_t* p0;        // [U+1] first position of slot u
   int32_t* cnt;       // [U+1] positions of slot u
   int32_t* plan;      // U, first task, tasks, abort flag
+  uint32_t* keys;     // [T*k] selected keys (top-k to the weights warps)
 };
 
 VX_DEVICE DecTab dec_tab(unsigned char* base) {
@@ -134,6 +136,7 @@ VX_DEVICE DecTab dec_tab(unsigned char* base) {
   t.p0 = t.ex + kDecMaxRoutes + 2;
   t.cnt = t.p0 + kDecMaxRoutes + 2;
   t.plan = t.cnt + kDecMaxRoutes + 2;
+  t.keys = reinterpret_cast<uint32_t*>(t.plan + 64);
   return t;
 }
 
@@ -507,19 +510,6 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const __grid_con
     }
   }
 
-  // ---- x activation records (every CTA, all tokens)
-  {
-    const int n = T * pl.nch_d * 16;   // whole warps run the loop (shuffles inside)
-    for (int i = threadIdx.x; i < ((n + 31) & ~31); i += kDecThreads) {
-      const bool live = i < n;
-      const int t = live ? i / (pl.nch_d * 16) : 0, r = live ? i - t * pl.nch_d * 16 : 0;
-      const int ch = r >> 4, blk = r & 15;
-      const uint4 v = live ? *reinterpret_cast<const uint4*>(a.x + int64_t(t) * d + ch * 128 + blk * 8)
-                           : make_uint4(0, 0, 0, 0);
-      put_record_block(smem + lay.off_x + (ch * T + t) * kActRecord, blk, v, live);
-    }
-  }
-
   // ---- phase R: logits (CTAs [0, L)), shared gate (CTA L)
   if (logit_cta) {
     // the fused router's 16 x 8 tile with rows g < 4 only (the other rows
@@ -603,9 +593,24 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const __grid_con
       if (lane == 0) a.sg[t] = f32_to_bf16(sigmoid_bf16(bf16r(acc)));
     }
   }
-  if (threadIdx.x < T) tb.tok[pl.P + threadIdx.x] = threadIdx.x;   // shared positions P + t
-  __syncthreads();   // logits / sg stored; x records built
+  __syncthreads();   // logits / sg stored
   if (threadIdx.x == 0) grid_arrive(a.sync + 0);
+
+  // ---- x activation records (every CTA, all tokens), after the logits so
+  // that the first barrier waits on the router alone
+  {
+    const int n = T * pl.nch_d * 16;   // whole warps run the loop (shuffles inside)
+    for (int i = threadIdx.x; i < ((n + 31) & ~31); i += kDecThreads) {
+      const bool live = i < n;
+      const int t = live ? i / (pl.nch_d * 16) : 0, r = live ? i - t * pl.nch_d * 16 : 0;
+      const int ch = r >> 4, blk = r & 15;
+      const uint4 v = live ? *reinterpret_cast<const uint4*>(a.x + int64_t(t) * d + ch * 128 + blk * 8)
+                           : make_uint4(0, 0, 0, 0);
+      put_record_block(smem + lay.off_x + (ch * T + t) * kActRecord, blk, v, live);
+    }
+  }
+  if (threadIdx.x < T) tb.tok[pl.P + threadIdx.x] = threadIdx.x;   // shared positions P + t
+  __syncthreads();   // x records built
 
   float* part = reinterpret_cast<float*>(smem + lay.off_part);
 
@@ -686,20 +691,34 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const __grid_con
     return;
   }
 
-  // ---- routing: top-k ids per token (warp t), then the stable expert sort;
-  // the renormalised weights are needed only by the combine and come later
-  // (adaptive top-k needs the probabilities to pick the kept slots: the
-  // whole of topk_row here, weights included)
+  // ---- routing: warp 1 + t selects token t's top-k ids (and their keys)
+  // and hands them to warp 0 (named barrier 1: the stable expert sort and
+  // the task split) and to warp 5 + t (named barrier 2), which meanwhile
+  // computed the softmax statistics of token t and now turns the keys into
+  // the renormalised weights (needed only by the combine).  Adaptive top-k
+  // needs the probabilities to pick the kept slots: the whole of topk_row
+  // in warp 1 + t.
   const bool adapt = a.keep_mass > 0.0 && a.keep_mass < 1.0;
-  if (warp < T) {
+  const int nb1 = 32 * (T + 1), nb2 = 64 * T;
+  if (warp >= 1 && warp <= T) {
+    const int t = warp - 1;
+    const uint16_t* lr = a.logits + int64_t(t) * E;
     if (adapt)
-      topk_row<PER, true>(a.logits + int64_t(warp) * E, E, k, tb.inds + warp * k, nullptr, tb.wts + warp * k,
-                          nullptr, a.keep_mass, a.keep_min);
+      topk_row<PER, true>(lr, E, k, tb.inds + t * k, nullptr, tb.wts + t * k, nullptr, a.keep_mass, a.keep_min);
     else
-      topk_select<PER, true>(a.logits + int64_t(warp) * E, E, k, tb.inds + warp * k);
+      topk_select_keys<PER, true>(lr, E, k, tb.inds + t * k, tb.keys + t * k);
+    named_arrive(1, nb1);
+    named_arrive(2, nb2);
+  } else if (warp >= 5 && warp < 5 + T) {
+    const int t = warp - 5;
+    if (adapt)
+      named_sync(2, nb2);
+    else
+      topk_weights_keys<PER, true>(a.logits + int64_t(t) * E, E, k, tb.keys + t * k, tb.wts + t * k,
+                                   [&]() { named_sync(2, nb2); });
   }
-  __syncthreads();
   if (warp == 0) {
+    named_sync(1, nb1);
     const int P = pl.P;
     // ids outside [0, E) (a selection among NaN logits) are dropped, as the
     // permutation drops them: no position, counted in the error word.  A
@@ -780,51 +799,27 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const __grid_con
     for (int u = lane; u < U; u += 32) tb.cnt[u] = (u + 1 < U ? tb.p0[u + 1] : Pv) - tb.p0[u];
 
     // ---- byte-balanced split of the routed gate/up tasks over the CTAs (in
-    // units of 256 bytes): each CTA's pre-assigned work - its logits (CTAs
-    // [0, L)), its shared gate/up tasks (q + 1 for CTAs [L, L + r), q for
-    // [L + r, G), ns_total = q * (G - L) + r), its down rows (CTAs
-    // [G - n_dt, G)) - plus routed tasks up to an equal share.  The
-    // pre-assigned loads are constant on the intervals those ranges make, so
-    // a CTA's running total of free capacity is a closed form.
+    // units of 256 bytes) for the work left after the routing: the routed
+    // tasks, and on the down owners (CTAs [G - n_dt, G)) their down records,
+    // which stream in the same rings meanwhile.  The logits and the shared
+    // gate/up tasks ran before the routing and do not count.  A CTA's share
+    // of the tasks is its capacity's share of the total, rounded the same way
+    // in every CTA (monotone in the CTA index).
     if (lane == 0) {
       const int nr_total = U * pl.rbg;
-      const int task_w = pl.nch_d * 10;
-      const int logit_w = kDecLogitRows * d * 2 / 256;
-      const int down_w = (U * pl.nch_i + lay.nch_s) * 5;
-      const int span = G - pl.L, sq = ns_total / span, sr = ns_total % span;
-      const int b0 = pl.L, b1 = pl.L + sr, b2 = G - pl.n_dt;
-      const int64_t tot_pre = int64_t(pl.L) * logit_w + int64_t(ns_total) * task_w + int64_t(pl.n_dt) * down_w;
-      const int64_t target = (tot_pre + int64_t(nr_total) * task_w) / G;
-      // breakpoints of the piecewise-constant loads, sorted once
-      int pts[5] = {0, b0, b1, b2, G};
-      for (int x = 1; x < 5; ++x)
-        for (int y = x; y > 0 && pts[y] < pts[y - 1]; --y) {
-          const int t = pts[y];
-          pts[y] = pts[y - 1];
-          pts[y - 1] = t;
-        }
-      int64_t piece[4];
-      for (int x = 0; x < 4; ++x) {
-        const int lo = pts[x];
-        const int64_t load = (lo < b0 ? logit_w : int64_t(lo < b1 ? sq + 1 : sq) * task_w) + (lo >= b2 ? down_w : 0);
-        piece[x] = max(int64_t(0), target - load);
-      }
-      // free capacity of the CTAs in [0, c)
+      const int64_t task_w = pl.nch_d * 10;
+      const int64_t down_w = int64_t(U * pl.nch_i + lay.nch_s) * 5;
+      const int b2 = G - pl.n_dt;
+      const int64_t target = (int64_t(pl.n_dt) * down_w + int64_t(nr_total) * task_w) / G;
+      const int64_t cap_own = target > down_w ? target - down_w : 0;
       auto cum_cap = [&](int c) -> int64_t {
-        int64_t sum = 0;
-        for (int x = 0; x < 4; ++x) {
-          const int lo = pts[x], hi = min(pts[x + 1], c);
-          if (hi > lo) sum += int64_t(hi - lo) * piece[x];
-        }
-        return sum;
+        return int64_t(min(c, b2)) * target + int64_t(max(0, c - b2)) * cap_own;
       };
       const int64_t cap_tot = cum_cap(G), c_lo = cum_cap(int(blockIdx.x)), c_hi = cum_cap(int(blockIdx.x) + 1);
       int first, last;
       if (cap_tot > 0) {
-        // correctly rounded double division: the same in every CTA, monotone in c
-        const double inv = double(nr_total) / double(cap_tot);
-        first = int(floor(double(c_lo) * inv + 0.5));
-        last = int(floor(double(c_hi) * inv + 0.5));
+        first = int((c_lo * nr_total + cap_tot / 2) / cap_tot);
+        last = int((c_hi * nr_total + cap_tot / 2) / cap_tot);
         if (int(blockIdx.x) == G - 1) last = nr_total;
       } else {
         first = int(blockIdx.x) * nr_total / G;
@@ -839,8 +834,12 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const __grid_con
   pl.first = tb.plan[kPlanFirst];
   pl.nr = tb.plan[kPlanNr];
   pl.routed = true;
-  if (blockIdx.x == 0 && a.inds_out)
-    for (int i = threadIdx.x; i < pl.P; i += kDecThreads) a.inds_out[i] = tb.inds[i];
+  if (blockIdx.x == 0) {
+    if (a.inds_out)
+      for (int i = threadIdx.x; i < pl.P; i += kDecThreads) a.inds_out[i] = tb.inds[i];
+    if (a.w_out)
+      for (int i = threadIdx.x; i < pl.P; i += kDecThreads) a.w_out[i] = tb.wts[i];
+  }
 
   // ---- phase G: routed gate/up tasks
   ring_fill(a, pl, tb, rg, warp, pol);
@@ -850,15 +849,6 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const __grid_con
   ring_fill(a, pl, tb, rg, warp, pol);
   if (threadIdx.x == 0) grid_arrive(a.sync + 1);
 
-  // the routing weights (topk_row's arithmetic), off the critical path: the
-  // down owners need them for the combine, CTA 0 writes them out
-  if (pl.td >= 0 || (blockIdx.x == 0 && a.w_out)) {
-    if (warp < T && !adapt)
-      topk_weights<PER, true>(a.logits + int64_t(warp) * E, E, k, tb.inds + warp * k, tb.wts + warp * k);
-    __syncthreads();
-    if (blockIdx.x == 0 && a.w_out)
-      for (int i = threadIdx.x; i < pl.P; i += kDecThreads) a.w_out[i] = tb.wts[i];
-  }
   if (pl.td < 0) {
     if (rg.timed_out) atomicOr(a.err, 0x100);
     return;   // no down tile (and nothing in flight): done

@@ -230,6 +230,82 @@ __device__ __forceinline__ void topk_select(const uint16_t* lr, int E, int k, in
   if (lane < k) inds[lane] = int(0xFFFFu - (my_key & 0xFFFFu));
 }
 
+// topk_select that also leaves each selected key (the order-preserving key
+// of the selected logit and id; 0 past the candidates) in keys[r], for
+// topk_weights_keys.
+template <int PER, bool COHERENT>
+__device__ __forceinline__ void topk_select_keys(const uint16_t* lr, int E, int k, int32_t* inds,
+                                                 uint32_t* keys) {
+  const int lane = threadIdx.x & 31;
+  const int e0 = lane * PER;
+  uint32_t raw[PER / 2];
+  topk_load<PER, COHERENT>(lr, E, raw);
+  uint32_t key[PER];
+  uint32_t lm = 0;
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int e = e0 + j;
+    key[j] = e < E ? logit_key(uint16_t(raw[j / 2] >> (16 * (j & 1))), e) : 0u;
+    lm = max(lm, key[j]);
+  }
+  uint32_t my_key = 0;
+  for (int r = 0; r < k; ++r) {
+    const uint32_t g = __reduce_max_sync(0xFFFFFFFFu, lm);
+    if (lane == r) my_key = g;
+    if (lm == g) {
+      lm = 0;
+#pragma unroll
+      for (int j = 0; j < PER; ++j) {
+        if (key[j] == g) key[j] = 0;
+        lm = max(lm, key[j]);
+      }
+    }
+  }
+  if (lane < k) {
+    inds[lane] = int(0xFFFFu - (my_key & 0xFFFFu));
+    keys[lane] = my_key;
+  }
+}
+
+// topk_weights for the keys topk_select_keys left: the softmax statistics
+// of the row first, then `wait()` (the keys' hand-over), then the weights.
+// Bit for bit topk_weights of the same selection (its per-lane sums in the
+// same order; the key it rebuilds from the reloaded logit is the selected
+// key itself).
+template <int PER, bool COHERENT, class Wait>
+__device__ __forceinline__ void topk_weights_keys(const uint16_t* lr, int E, int k, const uint32_t* keys,
+                                                  uint16_t* weights, Wait wait) {
+  const int lane = threadIdx.x & 31;
+  const int e0 = lane * PER;
+  uint32_t raw[PER / 2];
+  topk_load<PER, COHERENT>(lr, E, raw);
+  float m = -INFINITY;
+  uint32_t key[PER];
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int e = e0 + j;
+    const uint16_t b = uint16_t(raw[j / 2] >> (16 * (j & 1)));
+    key[j] = e < E ? logit_key(b, e) : 0u;
+    if (e < E) m = fmaxf(m, bf16_to_f32(b));
+  }
+  m = warp_max(m);
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < PER; ++j)
+    if (e0 + j < E) s += expf(__fsub_rn(key_logit(key[j]), m));
+  s = warp_sum<32>(s);
+  const float inv = __fdiv_rn(1.0f, s);
+  wait();
+  const uint32_t my_key = lane < k ? keys[lane] : 0u;
+  const float my_p = bf16r(__fmul_rn(expf(__fsub_rn(key_logit(my_key), m)), inv));
+  float tot = 0.f;
+  for (int r = 0; r < k; ++r) tot = __fadd_rn(tot, __shfl_sync(0xFFFFFFFFu, my_p, r));
+  const float msum = bf16r(tot);
+  const float diff = bf16r(__fsub_rn(msum, msum));
+  const float norm = bf16r(__fadd_rn(msum, bf16r(diff)));
+  if (lane < k) weights[lane] = f32_to_bf16(bf16r(__fdiv_rn(my_p, norm)));
+}
+
 template <int PER, bool COHERENT>
 __device__ __forceinline__ void topk_weights(const uint16_t* lr, int E, int k, const int32_t* inds,
                                              uint16_t* weights) {
