@@ -11,19 +11,22 @@
 // every SM runs one CTA for the whole block; the CTAs meet at two grid
 // barriers (bounded waits on global counters):
 //
-//   phase R   CTAs [0, L) compute the bf16 logits of 8 experts each (the
+//   phase R   CTAs [0, L) compute the bf16 logits of 4 experts each (the
 //             fused router's mma.sync tile and K slicing, so the logits are
-//             the router kernel's bit for bit); the other CTAs start on the
+//             the router kernel's bit for bit) before anything else; every
+//             CTA then builds the x records, and the other CTAs start on the
 //             shared expert, whose gate/up projections need no routing.
 //   barrier 1
-//   phase G   every CTA reads all logits, runs the same top-k (one warp per
-//             token) and the same stable expert sort (one warp, bitonic over
-//             at most 64 routes), then takes a byte-balanced slice of the
-//             routed gate/up tasks (expert, 16-row tile); the 8 warps of a
-//             CTA split each task's 128-input chunks, the CTA adds their
-//             partial sums in warp order and applies the bf16 SwiGLU; h goes
-//             to global.  Down-projection weights stream into shared memory
-//             meanwhile.
+//   phase G   every CTA reads all logits: warp 1 + t selects token t's top-k
+//             and hands the ids to warp 0 (named barrier), which runs the
+//             stable expert sort (rank by shuffles over at most 64 routes)
+//             and the closed-form task split, while warp 5 + t turns the
+//             selected keys into the renormalised weights.  The CTA then
+//             takes its byte-balanced slice of the routed gate/up tasks
+//             (expert, 16-row tile); its 16 warps split each task's
+//             128-input chunks, the CTA adds their partial sums in warp
+//             order and applies the bf16 SwiGLU; h goes to global.
+//             Down-projection weights stream into shared memory meanwhile.
 //   barrier 2
 //   phase D   CTA c >= G - n_tiles owns one row tile of the down projection
 //             for every expert of the step: it builds the h records of all
@@ -33,10 +36,12 @@
 //
 // Weights come from the tiled resident pool (vx_q4_tile), one record per
 // (expert, row tile, 128-input chunk): 2,560 bytes for a gate/up pair of 16
-// rows, 1,280 or 2,560 bytes for 16 or 32 down rows.  A warp copies a record
-// into a stage of its ring with per-lane 16-byte cp.async (the load/store
-// path; small bulk copies cost more per byte) that arrive on the stage's
-// mbarrier.  The arithmetic of a record is the tiled GEMV's (vx_gemv_tiled.cu):
+// rows, 1,280 or 2,560 bytes for 16 or 32 down rows.  Lane 0 of a warp
+// copies a record into a stage of its ring with one bulk copy (two for the
+// 16 owned rows of a down record) onto the stage's mbarrier: at one or a few
+// tokens the copies are latency-bound, and the copy engine keeps more
+// of them in flight per SM than per-lane 16-byte copies (C1 34.1 -> 32.5 us).
+// The arithmetic of a record is the tiled GEMV's (vx_gemv_tiled.cu):
 // nibbles to bf16 128+q by one lop3, a block-diagonal B operand on mma.sync
 // so each MMA yields per-group sums, and MLX's qmv formula
 // scale*sum(qx) + bias*sum(x) per group in float32.
@@ -372,8 +377,9 @@ struct DecRing {
   bool timed_out;
 };
 
-// Issues records into free stages: every lane copies its 16-byte pieces with
-// cp.async and arrives on the stage's mbarrier (count 32) once they land.
+// Issues records into free stages: lane 0 arms the stage's mbarrier (count
+// 1) with the record's bytes and bulk-copies it (after a proxy fence: the
+// stage was last read through the generic proxy).
 VX_DEVICE void ring_fill(const DecodeArgs& a, const DecPlan& pl, const DecTab& tb, DecRing& rg, int warp,
                          uint64_t pol) {
   const int lane = threadIdx.x & 31;
@@ -386,24 +392,24 @@ VX_DEVICE void ring_fill(const DecodeArgs& a, const DecPlan& pl, const DecTab& t
       const unsigned char* rec =
           t.u < 0 ? a.gu_rec_s : a.gu_rec + routed_record(a.slot_of, a.slots, tb.ex[t.u]) * a.gu_stride;
       const unsigned char* src = rec + (int64_t(t.rb) * pl.nch_d + rg.cur.ch) * 2560;
-      for (int off = lane * 16; off < 2560; off += 512)
-        asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(dst + off),
-                     "l"(src + off), "l"(pol)
-                     : "memory");
+      if (lane == 0) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_expect(rg.bar0 + 8 * s, 2560);
+        bulk_load(dst, src, 2560, rg.bar0 + 8 * s, pol);
+      }
     } else {
       // the 16 owned rows of a down record (record tile td / dn_mt, m-tile
       // td % dn_mt): their packed words, then their scales and biases
       const int m = pl.td % pl.dn_mt;
       const unsigned char* rec = a.dn_rec + routed_record(a.slot_of, a.slots, tb.ex[rg.cur.j]) * a.dn_stride +
                                  (int64_t(pl.td / pl.dn_mt) * pl.nch_i + rg.cur.ch) * (pl.dn_mt * 1280);
-      for (int off = lane * 16; off < 1280; off += 512) {
-        const unsigned char* src = off < 1024 ? rec + m * 1024 + off : rec + pl.dn_mt * 1024 + m * 256 + (off - 1024);
-        asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(dst + off),
-                     "l"(src), "l"(pol)
-                     : "memory");
+      if (lane == 0) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_expect(rg.bar0 + 8 * s, 1280);
+        bulk_load(dst, rec + m * 1024, 1024, rg.bar0 + 8 * s, pol);
+        bulk_load(dst + 1024, rec + pl.dn_mt * 1024 + m * 256, 256, rg.bar0 + 8 * s, pol);
       }
     }
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(rg.bar0 + 8 * s) : "memory");
     ++rg.issued;
     dec_advance(rg.cur);
   }
@@ -485,7 +491,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const __grid_con
   rg.cur = {0, 0, warp};
   rg.timed_out = false;
   if (lane == 0)
-    for (int s = 0; s < rg.R; ++s) mbar_init_count(rg.bar0 + 8 * s, 32);
+    for (int s = 0; s < rg.R; ++s) mbar_init_count(rg.bar0 + 8 * s, 1);
   const uint32_t sd_bar = smem_u32(smem + lay.off_bar) + lay.ring_stages * 8;
   const bool sd_owner = pl.td >= 0 && a.Is > 0;
   if (threadIdx.x == 0) {

@@ -55,6 +55,42 @@ __device__ __forceinline__ int topk_keep(float my_p, int k, double keep_mass, in
   return keep > lo ? keep : lo;
 }
 
+// Lane r < k gets the r-th largest of the warp's keys (0 once they run
+// out); `key` is consumed.  Each lane sorts its PER keys in descending order
+// (a bitonic network in registers: independent compare-exchanges), then a
+// round is one warp-wide max of the lanes' heads and a one-place shift of
+// the owner's list.  Keys are unique (the id is part of the key), so a
+// nonzero maximum has one owner; the selection and its order are those of
+// repeatedly taking the largest remaining key.
+template <int PER>
+__device__ __forceinline__ uint32_t topk_pick(uint32_t (&key)[PER], int k) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int size = 2; size <= PER; size <<= 1)
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1)
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int l = i ^ stride;
+        if (l > i) {
+          const bool desc = (i & size) == 0;
+          const uint32_t x = key[i], y = key[l];
+          key[i] = desc ? max(x, y) : min(x, y);
+          key[l] = desc ? min(x, y) : max(x, y);
+        }
+      }
+  uint32_t my_key = 0;
+  for (int r = 0; r < k; ++r) {
+    const uint32_t g = __reduce_max_sync(0xFFFFFFFFu, key[0]);
+    if (lane == r) my_key = g;
+    const bool own = key[0] == g;
+#pragma unroll
+    for (int j = 0; j + 1 < PER; ++j) key[j] = own ? key[j + 1] : key[j];
+    key[PER - 1] = own ? 0u : key[PER - 1];
+  }
+  return my_key;
+}
+
 template <int PER, bool COHERENT>
 __device__ __forceinline__ void topk_row(const uint16_t* lr, int E, int k, int32_t* inds, uint16_t* scores,
                                          uint16_t* weights, uint16_t* mass, double keep_mass = 0.0,
@@ -112,22 +148,7 @@ __device__ __forceinline__ void topk_row(const uint16_t* lr, int E, int k, int32
   s = warp_sum<32>(s);
   const float inv = __fdiv_rn(1.0f, s);
 
-  uint32_t lm = 0;
-#pragma unroll
-  for (int j = 0; j < PER; ++j) lm = max(lm, key[j]);
-  uint32_t my_key = 0;
-  for (int r = 0; r < k; ++r) {
-    const uint32_t g = __reduce_max_sync(0xFFFFFFFFu, lm);
-    if (lane == r) my_key = g;
-    if (lm == g) {   // the owner: drop the selected key, refresh the local max
-      lm = 0;
-#pragma unroll
-      for (int j = 0; j < PER; ++j) {
-        if (key[j] == g) key[j] = 0;
-        lm = max(lm, key[j]);
-      }
-    }
-  }
+  const uint32_t my_key = topk_pick<PER>(key, k);
   int my_i = int(0xFFFFu - (my_key & 0xFFFFu));
   const float my_p = bf16r(__fmul_rn(expf(__fsub_rn(key_logit(my_key), m)), inv));
   float tot = 0.f;
@@ -207,26 +228,12 @@ __device__ __forceinline__ void topk_select(const uint16_t* lr, int E, int k, in
   uint32_t raw[PER / 2];
   topk_load<PER, COHERENT>(lr, E, raw);
   uint32_t key[PER];
-  uint32_t lm = 0;
 #pragma unroll
   for (int j = 0; j < PER; ++j) {
     const int e = e0 + j;
     key[j] = e < E ? logit_key(uint16_t(raw[j / 2] >> (16 * (j & 1))), e) : 0u;
-    lm = max(lm, key[j]);
   }
-  uint32_t my_key = 0;
-  for (int r = 0; r < k; ++r) {
-    const uint32_t g = __reduce_max_sync(0xFFFFFFFFu, lm);
-    if (lane == r) my_key = g;
-    if (lm == g) {   // the owner: drop the selected key, refresh the local max
-      lm = 0;
-#pragma unroll
-      for (int j = 0; j < PER; ++j) {
-        if (key[j] == g) key[j] = 0;
-        lm = max(lm, key[j]);
-      }
-    }
-  }
+  const uint32_t my_key = topk_pick<PER>(key, k);
   if (lane < k) inds[lane] = int(0xFFFFu - (my_key & 0xFFFFu));
 }
 
@@ -241,26 +248,12 @@ __device__ __forceinline__ void topk_select_keys(const uint16_t* lr, int E, int 
   uint32_t raw[PER / 2];
   topk_load<PER, COHERENT>(lr, E, raw);
   uint32_t key[PER];
-  uint32_t lm = 0;
 #pragma unroll
   for (int j = 0; j < PER; ++j) {
     const int e = e0 + j;
     key[j] = e < E ? logit_key(uint16_t(raw[j / 2] >> (16 * (j & 1))), e) : 0u;
-    lm = max(lm, key[j]);
   }
-  uint32_t my_key = 0;
-  for (int r = 0; r < k; ++r) {
-    const uint32_t g = __reduce_max_sync(0xFFFFFFFFu, lm);
-    if (lane == r) my_key = g;
-    if (lm == g) {
-      lm = 0;
-#pragma unroll
-      for (int j = 0; j < PER; ++j) {
-        if (key[j] == g) key[j] = 0;
-        lm = max(lm, key[j]);
-      }
-    }
-  }
+  const uint32_t my_key = topk_pick<PER>(key, k);
   if (lane < k) {
     inds[lane] = int(0xFFFFu - (my_key & 0xFFFFu));
     keys[lane] = my_key;
