@@ -231,36 +231,54 @@ VX_DEVICE void rec_mma(uint32_t st, uint32_t brec, const uint32_t (&tokoff)[4], 
     xs[q][0] = __uint_as_float(v.x);
     xs[q][1] = __uint_as_float(v.y);
   }
+  // The MMAs of every 16-row block first, blocks interleaved, so that 2 x NM
+  // (for a single block 4) independent accumulator chains are in flight: a
+  // record on one warp is bound by the dependent MMA latency.  The chains
+  // are added in a fixed order at the end.
+  constexpr int NC = NM == 1 ? 4 : 2;   // chains per block
+  uint32_t ag[NM][4], a8[NM][4];
 #pragma unroll
   for (int pm = 0; pm < NM; ++pm) {
     const uint32_t wrow = st + pm * 1024 + lane * 16;
     const uint4 wg = lds128(wrow), w8 = lds128(wrow + 512);
-    const uint32_t ag[4] = {wg.x, wg.y, wg.z, wg.w};
-    const uint32_t a8[4] = {w8.x, w8.y, w8.z, w8.w};
-    // two independent accumulator chains (low and high nibble pairs), added
-    // at the end: half the dependent MMA latency of one chain
-    float d[NQ][4], e[NQ][4];
+    ag[pm][0] = wg.x, ag[pm][1] = wg.y, ag[pm][2] = wg.z, ag[pm][3] = wg.w;
+    a8[pm][0] = w8.x, a8[pm][1] = w8.y, a8[pm][2] = w8.z, a8[pm][3] = w8.w;
+  }
+  float dc[NM][NC][NQ][4];
 #pragma unroll
-    for (int q = 0; q < NQ; ++q)
+  for (int pm = 0; pm < NM; ++pm)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) d[q][i] = e[q][i] = 0.f;
+    for (int cc = 0; cc < NC; ++cc)
 #pragma unroll
-    for (int mm = 0; mm < 8; mm += 2) {
-      const int wi = mm >> 1;
-      const uint32_t f0 = nib_pair128(ag[wi]), f1 = nib_pair128(a8[wi]);
-      const uint32_t f2 = nib_pair128(ag[wi] >> 4), f3 = nib_pair128(a8[wi] >> 4);
-      const uint32_t h0 = nib_pair128(ag[wi] >> 8), h1 = nib_pair128(a8[wi] >> 8);
-      const uint32_t h2 = nib_pair128(ag[wi] >> 12), h3 = nib_pair128(a8[wi] >> 12);
+      for (int q = 0; q < NQ; ++q)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dc[pm][cc][q][i] = 0.f;
+#pragma unroll
+  for (int wi = 0; wi < 4; ++wi) {
+    const int mm = 2 * wi;
+    const int cf = NC == 4 ? 2 * (wi & 1) : 0;   // chain of the low nibble pairs; +1: the high ones
+#pragma unroll
+    for (int pm = 0; pm < NM; ++pm) {
+      const uint32_t f0 = nib_pair128(ag[pm][wi]), f1 = nib_pair128(a8[pm][wi]);
+      const uint32_t f2 = nib_pair128(ag[pm][wi] >> 4), f3 = nib_pair128(a8[pm][wi] >> 4);
+      const uint32_t h0 = nib_pair128(ag[pm][wi] >> 8), h1 = nib_pair128(a8[pm][wi] >> 8);
+      const uint32_t h2 = nib_pair128(ag[pm][wi] >> 12), h3 = nib_pair128(a8[pm][wi] >> 12);
 #pragma unroll
       for (int q = 0; q < NQ; ++q) {
-        mma16816(d[q], f0, f1, f2, f3, bq[q][2 * mm], bq[q][2 * mm + 1]);
-        mma16816(e[q], h0, h1, h2, h3, bq[q][2 * mm + 2], bq[q][2 * mm + 3]);
+        mma16816(dc[pm][cf][q], f0, f1, f2, f3, bq[q][2 * mm], bq[q][2 * mm + 1]);
+        mma16816(dc[pm][cf + 1][q], h0, h1, h2, h3, bq[q][2 * mm + 2], bq[q][2 * mm + 3]);
       }
     }
+  }
+#pragma unroll
+  for (int pm = 0; pm < NM; ++pm) {
+    float d[NQ][4];
 #pragma unroll
     for (int q = 0; q < NQ; ++q)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) d[q][i] += e[q][i];
+      for (int i = 0; i < 4; ++i)
+        d[q][i] = NC == 4 ? (dc[pm][0][q][i] + dc[pm][2][q][i]) + (dc[pm][1][q][i] + dc[pm][3][q][i])
+                          : dc[pm][0][q][i] + dc[pm][1][q][i];
     const uint4 sb = lds128(st + NM * 1024 + pm * 256 + (g * 2 + (c & 1)) * 16);
     const uint32_t sw[4] = {sb.x, sb.y, sb.z, sb.w};
 #pragma unroll
@@ -751,13 +769,21 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const __grid_con
     // (valid keys are distinct: the flat index is part of the key); the
     // sorted keys go through shared memory (the plan region is free here)
     {
+      // (keys past P are 0xFFFFFFFF and rank below nothing: only the P
+      // routed keys are visited)
       int ra = 0, rb = 0;
-#pragma unroll 8
-      for (int j = 0; j < 32; ++j) {
+      const int n0 = P < 32 ? P : 32, n1 = P > 32 ? P - 32 : 0;
+#pragma unroll 4
+      for (int j = 0; j < n0; ++j) {
         const uint32_t xa = __shfl_sync(0xFFFFFFFFu, kv[0], j);
+        ra += xa < kv[0];
+        rb += xa < kv[1];
+      }
+#pragma unroll 4
+      for (int j = 0; j < n1; ++j) {
         const uint32_t xb = __shfl_sync(0xFFFFFFFFu, kv[1], j);
-        ra += (xa < kv[0]) + (xb < kv[0]);
-        rb += (xa < kv[1]) + (xb < kv[1]);
+        ra += xb < kv[0];
+        rb += xb < kv[1];
       }
       uint32_t* skey = reinterpret_cast<uint32_t*>(part);
       skey[lane] = skey[lane + 32] = 0xFFFFFFFFu;
