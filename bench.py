@@ -83,15 +83,20 @@ def peaks():
 def block_launches(T, k=TOPK, E=EXPERTS):
     """Kernels one single-GPU block call launches (the library's dispatch):
     at most four tokens, the whole block in one cooperative launch; else the
-    router, with the expert sort in its last token block while T*k <=
-    1024, else a permutation launch (three above 16,384 routes); then the
-    activation records, gate/up and down GEMVs (decode), or the x gather and
-    the two tcgen05 GEMMs (T*k >= 4E); then the combine."""
+    router - one fused launch, with the expert sort in its last token block
+    while T*k <= 1024, or from 256 tokens the tiled logits, the top-k and
+    the shared-expert gate (three) - then a permutation launch unless the
+    router sorted (three above 16,384 routes); then the x records, gate/up,
+    h records and down GEMVs (decode), or the x gather and the two tcgen05
+    GEMMs (T*k >= 4E); then the combine."""
     P = T * k
     if T <= 4:
         return 1   # the single cooperative decode launch (and one memset)
-    perm = 0 if P <= 1024 else (1 if P <= 16384 else 3)
-    return 1 + perm + 3 + 1
+    fused_sort = P <= 1024
+    router = 3 if (T >= 256 and not fused_sort) else 1
+    perm = 0 if fused_sort else (1 if P <= 16384 else 3)
+    experts = 3 if P >= 4 * E else 4
+    return router + perm + experts + 1
 
 
 def layer_bytes(U, T):
@@ -650,10 +655,12 @@ def main():
     xs = (torch.randn((nx, T, HIDDEN), device=dev, generator=g)).to(torch.bfloat16)
     torch.cuda.synchronize()
     # our kernels per step on one GPU: block_launches(T); EP runs the router, the
-    # shard's pass (permute, activation records, gate/up, down), the shared expert's own
-    # pass (permute .. unpermute) and, on the peer transport, dispatch, the dispatch
-    # wait and the combine
-    launches_per_step = block_launches(T) if world == 1 else (14 if args.ep_transport == "p2p" else 11)
+    # shard's pass (permute, activation records, gate/up, down; plus the h records when
+    # the shard's rows take the GEMV path), the shared expert's own pass (permute ..
+    # unpermute) and, on the peer transport, dispatch, the dispatch wait and the combine
+    shard_gemv = T * world * TOPK < 4 * (EXPERTS // max(world, 1))
+    launches_per_step = (block_launches(T) if world == 1
+                         else (14 if args.ep_transport == "p2p" else 11) + (1 if shard_gemv else 0))
 
     def step(i):
         return layers[i % len(layers)](xs[i])

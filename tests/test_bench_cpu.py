@@ -14,11 +14,13 @@ def test_block_launches_follow_the_dispatch():
     import bench
     # at most four tokens: the whole block in one cooperative launch
     assert [bench.block_launches(T) for T in (1, 2, 3, 4)] == [1] * 4
-    # router (sort inside while T*k <= 1024), act records / x gather, gate/up, down, combine
-    assert [bench.block_launches(T) for T in (5, 16, 64, 102)] == [5] * 4
-    assert bench.block_launches(103) == 6            # separate one-CTA permutation
-    assert bench.block_launches(1638) == 6           # 16,380 routes: one permutation CTA
-    assert bench.block_launches(2048) == 8           # sliced permutation: count, scan, scatter
+    # router (sort inside while T*k <= 1024), x records, gate/up, h records, down, combine
+    assert [bench.block_launches(T) for T in (5, 16, 64, 102)] == [6] * 4
+    assert bench.block_launches(103) == 7            # separate one-CTA permutation
+    assert bench.block_launches(205) == 6            # T*k >= 4E: x gather and two GEMMs
+    assert bench.block_launches(300) == 8            # tiled router: logits, top-k, shared gate
+    assert bench.block_launches(1638) == 8           # 16,380 routes: one permutation CTA
+    assert bench.block_launches(2048) == 10          # sliced permutation: count, scan, scatter
 
 
 def test_traffic_only_for_the_captured_workload():
