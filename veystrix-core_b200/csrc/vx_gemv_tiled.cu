@@ -451,6 +451,24 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
 // products and an fp32 sum with no offset to cancel.  e stays at or above
 // -103 so that 2^(24-e) is a finite float: a record whose largest |x| is
 // 2^117 or more saturates to infinity.
+// E with m in [2^(E-1), 2^E), for a positive finite float (subnormals too):
+// from the exponent field, or for a subnormal the position of its leading bit.
+VX_DEVICE int pow2_exponent(float m) {
+  const uint32_t b = __float_as_uint(m);
+  const int ex = int(b >> 23);
+  return ex ? ex - 126 : (31 - __clz(int(b))) - 148;
+}
+
+// x * 2^n for n in [-126, 254], by multiplying with exact powers of two (one
+// rounding, as a scaling by 2^n is exact whenever the result is normal).
+VX_DEVICE float times_pow2(float x, int n) {
+  if (n > 127) {
+    x *= __int_as_float((64 + 127) << 23);
+    n -= 64;
+  }
+  return x * __int_as_float((n + 127) << 23);
+}
+
 __global__ void act_records_kernel(const uint16_t* __restrict__ x, int64_t ldx, int K,
                                    const int32_t* __restrict__ src_rows, const int32_t* __restrict__ n_rows,
                                    int64_t rows, unsigned char* __restrict__ act) {
@@ -487,17 +505,13 @@ __global__ void act_records_kernel(const uint16_t* __restrict__ x, int64_t ldx, 
 #pragma unroll
   for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
   int e = 0;
-  if (m > 0.f && isfinite(m)) {
-    int E;
-    frexpf(m, &E);   // m in [2^(E-1), 2^E)
-    e = max(14 - E, -103);
-  }
+  if (m > 0.f && isfinite(m)) e = max(14 - pow2_exponent(m), -103);
   if (!live) return;
   const int ch = blk >> 4, c = (blk >> 2) & 3, ib = blk & 3;
   unsigned char* rec = act + (int64_t(ch) * rows + p) * kActRecord;
   uint16_t h[8];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) h[j] = __half_as_ushort(__float2half_rn(ldexpf(xv[j], (j & 1) ? e - 4 : e)));
+  for (int j = 0; j < 8; ++j) h[j] = __half_as_ushort(__float2half_rn(times_pow2(xv[j], (j & 1) ? e - 4 : e)));
   uint4 o;
   o.x = h[0] | (uint32_t(h[4]) << 16);   // (x0, x4)
   o.y = h[1] | (uint32_t(h[5]) << 16);   // (x1, x5) / 16: B rows k >= 8
@@ -505,7 +519,7 @@ __global__ void act_records_kernel(const uint16_t* __restrict__ x, int64_t ldx, 
   o.w = h[3] | (uint32_t(h[7]) << 16);   // (x3, x7) / 16
   *reinterpret_cast<uint4*>(rec + (ib * 4 + c) * 16) = o;
   if (ib == 0) *reinterpret_cast<float*>(rec + kActXsum + c * 4) = inside ? s : 0.f;
-  if (blk % 16 == 0) *reinterpret_cast<float*>(rec + kActXsum + 16) = ldexpf(1.f, 24 - e);
+  if (blk % 16 == 0) *reinterpret_cast<float*>(rec + kActXsum + 16) = __int_as_float((24 - e + 127) << 23);
 }
 
 cudaError_t launch_act_records(const uint16_t* x, int64_t ldx, int K, const int32_t* src_rows,
