@@ -241,6 +241,9 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
       xa[q] = live ? kXOff + (2 * q + tb) * kActRecord + c * 16 : 0xFFFFFFFFu;
       xsa[q] = kXOff + (2 * q + ts) * kActRecord + kActXsum + (c & 1) * 8;
     }
+    // 2^(24-e) of the lane's token (f16 records: the chunks accumulate on the
+    // records' scaled axis, scaled back once after the last chunk)
+    float xinv[NQ] = {};
     const int nch = (k.K + 127) >> 7;
     for (int ch = 0; ch < nch; ++ch) {
       if (ti < total) issue();
@@ -254,7 +257,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
       parity_bits ^= 1u << st_use;
 
       uint32_t bq[NQ][16];
-      float xs[NQ][2], xinv[NQ];
+      float xs[NQ][2];
 #pragma unroll
       for (int q = 0; q < NQ; ++q) {
         const bool live = xa[q] != 0xFFFFFFFFu;
@@ -354,9 +357,9 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
 #pragma unroll
               for (int q = 0; q < NQ; ++q) {
                 float v = acc[p][m][q][h];
-                v = fmaf(s0, d[q][2 * h] * xinv[q], v);
+                v = fmaf(s0, d[q][2 * h], v);
                 v = fmaf(b0, xs[q][0], v);
-                v = fmaf(s1, d[q][2 * h + 1] * xinv[q], v);
+                v = fmaf(s1, d[q][2 * h + 1], v);
                 v = fmaf(b1, xs[q][1], v);
                 acc[p][m][q][h] = v;
               }
@@ -389,7 +392,10 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
 #pragma unroll
         for (int q = 0; q < NQ; ++q)
 #pragma unroll
-          for (int h = 0; h < 2; ++h) acc[p][m][q][h] += __shfl_xor_sync(0xFFFFFFFFu, acc[p][m][q][h], 1);
+          for (int h = 0; h < 2; ++h) {
+            acc[p][m][q][h] += __shfl_xor_sync(0xFFFFFFFFu, acc[p][m][q][h], 1);
+            if constexpr (F16) acc[p][m][q][h] *= xinv[q];   // lanes c, c^1: the same token
+          }
     if (c & 1) return;
 #pragma unroll
     for (int q = 0; q < NQ; ++q) {
@@ -430,27 +436,33 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
 
 // ---- activation records ----------------------------------------------------
 
-// One thread per 8-input block of a (position, chunk); the record's 16 blocks
-// are 16 consecutive threads.  The block goes to lane-order slot (i*4 + c) in
-// B order (words (x0,x4) (x1,x5) (x2,x6) (x3,x7)) as f16, for the f16 unpack
-// of the GEMV (kActF16; x rows for gate/up, h rows for down), whose weights
-// enter the MMA as f16 subnormals q * 2^-24 (nibbles at bits 0-3) or
-// 16q * 2^-24 (bits 4-7, no shift):
+// One CTA per position; thread i writes 8-input blocks i, i + blockDim, ...
+// of the position's records (a record's 16 blocks are 16 consecutive lanes).  The
+// block goes to lane-order slot (i*4 + c) in B order (words (x0,x4) (x1,x5)
+// (x2,x6) (x3,x7)) as f16, for the f16 unpack of the GEMV (kActF16; x rows
+// for gate/up, h rows for down), whose weights enter the MMA as f16
+// subnormals q * 2^-24 (nibbles at bits 0-3) or 16q * 2^-24 (bits 4-7, no
+// shift):
 //
-//   * the record is scaled by 2^e, e chosen from its largest |x| so that it
-//     lands in [2^13, 2^14): every bf16 input converts exactly (f16 keeps 11
-//     significant bits) unless it is 2^-23 of the largest or smaller;
+//   * all records of a position are scaled by 2^e, e chosen from the
+//     position's largest |x| so that it lands in [2^13, 2^14): every bf16
+//     input converts exactly (f16 keeps 11 significant bits) unless it is
+//     2^-27 of the largest or smaller (then to the nearest multiple of
+//     2^-24 on the scaled axis, an error below 2^-38 of the largest);
 //   * words 1 and 3 of each slot meet the 16q weights (B rows k = 8..15 of
 //     an MMA): those values are stored divided by 16 (exact), so every
 //     product is q * x * 2^(e-24);
-//   * the tail holds the plain sum of each group's 32 inputs at kActXsum +
-//     4g (left to right over 8 inputs, then (s0+s1)+(s2+s3)), for the bias
-//     term, and 2^(24-e) at kActXsum + 16.
+//   * the tail holds the sum of each group's 32 inputs times 2^(e-24) at
+//     kActXsum + 4g (left to right over 8 inputs, then (s0+s1)+(s2+s3), then
+//     the exact scaling), for the bias term, and 2^(24-e) at kActXsum + 16.
 //
-// A group's GEMV term is s * D * 2^(24-e) + b * sum, D the MMA sum: exact
-// products and an fp32 sum with no offset to cancel.  e stays at or above
-// -103 so that 2^(24-e) is a finite float: a record whose largest |x| is
-// 2^117 or more saturates to infinity.
+// A group's GEMV term on the scaled axis is s * D + b * sum', D the MMA sum:
+// exact products and an fp32 sum with no offset to cancel; the task's sum
+// over its chunks is multiplied by 2^(24-e) once, which gives the same bits
+// as scaling every term (a power of two commutes with rounding while the
+// values stay normal).  e stays at or above -103 so that 2^(24-e) is a
+// finite float: a position whose largest |x| is 2^117 or more saturates to
+// infinity.
 // E with m in [2^(E-1), 2^E), for a positive finite float (subnormals too):
 // from the exponent field, or for a subnormal the position of its leading bit.
 VX_DEVICE int pow2_exponent(float m) {
@@ -459,75 +471,93 @@ VX_DEVICE int pow2_exponent(float m) {
   return ex ? ex - 126 : (31 - __clz(int(b))) - 148;
 }
 
-// x * 2^n for n in [-126, 254], by multiplying with exact powers of two (one
+// x * 2^n for n in [-190, 254], by multiplying with exact powers of two (one
 // rounding, as a scaling by 2^n is exact whenever the result is normal).
 VX_DEVICE float times_pow2(float x, int n) {
   if (n > 127) {
     x *= __int_as_float((64 + 127) << 23);
     n -= 64;
+  } else if (n < -126) {
+    x *= __int_as_float((127 - 64) << 23);
+    n += 64;
   }
   return x * __int_as_float((n + 127) << 23);
 }
+
+constexpr int kActThreads = 256;
 
 __global__ void act_records_kernel(const uint16_t* __restrict__ x, int64_t ldx, int K,
                                    const int32_t* __restrict__ src_rows, const int32_t* __restrict__ n_rows,
                                    int64_t rows, unsigned char* __restrict__ act) {
   chain_begin();
-  const int nch = (K + 127) / 128;
-  const int nb = nch * 16;   // 8-input blocks per position, chunk padding included
-  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t n = rows * nb;
-  const int64_t limit = n_rows ? int64_t(*n_rows) : rows;
-  const int64_t p = i < n ? i / nb : 0;
-  const int blk = i < n ? int(i - p * nb) : 0;
-  const bool live = i < n && p < limit;
-  const bool inside = live && blk * 8 < K;
-  uint4 v = make_uint4(0, 0, 0, 0);
-  if (inside) {
-    const int64_t r = src_rows ? int64_t(__ldg(src_rows + p)) : p;
-    v = *reinterpret_cast<const uint4*>(x + r * ldx + blk * 8);
-  }
-  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-  float xv[8];
+  // one CTA per position: the exponent comes from the whole row's largest
+  // |x|, so every chunk of a position shares it (the GEMV accumulates the
+  // chunks on the scaled axis and scales once per task)
+  __shared__ float wmax[kActThreads / 32];
+  const int nb = ((K + 127) / 128) * 16;   // 8-input blocks, chunk padding included
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t p = blockIdx.x;
+  if (p >= (n_rows ? int64_t(*n_rows) : rows)) return;   // CTA-uniform
+  const uint16_t* xr = x + (src_rows ? int64_t(__ldg(src_rows + p)) : p) * ldx;
+  float m = 0.f;
+  for (int blk = threadIdx.x; blk * 8 < K; blk += blockDim.x) {
+    const uint4 v = *reinterpret_cast<const uint4*>(xr + blk * 8);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    xv[2 * j] = __uint_as_float(w[j] << 16);
-    xv[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+    for (int j = 0; j < 4; ++j)
+      m = fmaxf(m, fmaxf(fabsf(__uint_as_float(w[j] << 16)), fabsf(__uint_as_float(w[j] & 0xFFFF0000u))));
   }
-  float s = 0.f, m = 0.f;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    s += xv[j];
-    m = fmaxf(m, fabsf(xv[j]));
-  }
-  s += __shfl_xor_sync(0xFFFFFFFFu, s, 1);
-  s += __shfl_xor_sync(0xFFFFFFFFu, s, 2);
-#pragma unroll
-  for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+  for (int o = 1; o < 32; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+  if (lane == 0) wmax[warp] = m;
+  __syncthreads();
+  m = wmax[0];
+  for (int i = 1; i < int(blockDim.x >> 5); ++i) m = fmaxf(m, wmax[i]);
   int e = 0;
   if (m > 0.f && isfinite(m)) e = max(14 - pow2_exponent(m), -103);
-  if (!live) return;
-  const int ch = blk >> 4, c = (blk >> 2) & 3, ib = blk & 3;
-  unsigned char* rec = act + (int64_t(ch) * rows + p) * kActRecord;
-  uint16_t h[8];
+  for (int b0 = 0; b0 < nb; b0 += blockDim.x) {   // uniform over the CTA
+    const int blk = b0 + threadIdx.x;
+    const bool inside = blk * 8 < K;   // implies blk < nb
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (inside) v = *reinterpret_cast<const uint4*>(xr + blk * 8);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    float xv[8];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) h[j] = __half_as_ushort(__float2half_rn(times_pow2(xv[j], (j & 1) ? e - 4 : e)));
-  uint4 o;
-  o.x = h[0] | (uint32_t(h[4]) << 16);   // (x0, x4)
-  o.y = h[1] | (uint32_t(h[5]) << 16);   // (x1, x5) / 16: B rows k >= 8
-  o.z = h[2] | (uint32_t(h[6]) << 16);   // (x2, x6)
-  o.w = h[3] | (uint32_t(h[7]) << 16);   // (x3, x7) / 16
-  *reinterpret_cast<uint4*>(rec + (ib * 4 + c) * 16) = o;
-  if (ib == 0) *reinterpret_cast<float*>(rec + kActXsum + c * 4) = inside ? s : 0.f;
-  if (blk % 16 == 0) *reinterpret_cast<float*>(rec + kActXsum + 16) = __int_as_float((24 - e + 127) << 23);
+    for (int j = 0; j < 4; ++j) {
+      xv[2 * j] = __uint_as_float(w[j] << 16);
+      xv[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s += xv[j];
+    s += __shfl_xor_sync(0xFFFFFFFFu, s, 1);
+    s += __shfl_xor_sync(0xFFFFFFFFu, s, 2);
+    if (blk >= nb) continue;
+    const int ch = blk >> 4, c = (blk >> 2) & 3, ib = blk & 3;
+    unsigned char* rec = act + (int64_t(ch) * rows + p) * kActRecord;
+    uint16_t h[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) h[j] = __half_as_ushort(__float2half_rn(times_pow2(xv[j], (j & 1) ? e - 4 : e)));
+    uint4 o;
+    o.x = h[0] | (uint32_t(h[4]) << 16);   // (x0, x4)
+    o.y = h[1] | (uint32_t(h[5]) << 16);   // (x1, x5) / 16: B rows k >= 8
+    o.z = h[2] | (uint32_t(h[6]) << 16);   // (x2, x6)
+    o.w = h[3] | (uint32_t(h[7]) << 16);   // (x3, x7) / 16
+    *reinterpret_cast<uint4*>(rec + (ib * 4 + c) * 16) = o;
+    // the group sum on the records' scale, 2^(e-24) (exact: a power of two)
+    if (ib == 0) *reinterpret_cast<float*>(rec + kActXsum + c * 4) = times_pow2(s, e - 24);
+    if ((blk & 15) == 0) *reinterpret_cast<float*>(rec + kActXsum + 16) = __int_as_float((24 - e + 127) << 23);
+  }
 }
 
 cudaError_t launch_act_records(const uint16_t* x, int64_t ldx, int K, const int32_t* src_rows,
                                const int32_t* n_rows, int64_t rows, unsigned char* act,
                                cudaStream_t st) {
-  const int64_t n = rows * ((K + 127) / 128) * 16;
-  if (n == 0) return cudaSuccess;
-  return launch_chained(act_records_kernel, dim3(int((n + 255) / 256)), dim3(256), 0, st, x, ldx, K,
+  if (rows <= 0 || K <= 0) return cudaSuccess;
+  if (rows > 0x7FFFFFFF) return cudaErrorInvalidValue;
+  const int nb = ((K + 127) / 128) * 16;   // threads: one per 8-input block, at most kActThreads
+  const int threads = nb >= kActThreads ? kActThreads : (nb + 31) / 32 * 32;
+  return launch_chained(act_records_kernel, dim3(unsigned(rows)), dim3(threads), 0, st, x, ldx, K,
                         src_rows, n_rows, rows, act);
 }
 
