@@ -500,8 +500,10 @@ __global__ void act_records_kernel(const uint16_t* __restrict__ x, int64_t ldx, 
   if (p >= (n_rows ? int64_t(*n_rows) : rows)) return;   // CTA-uniform
   const uint16_t* xr = x + (src_rows ? int64_t(__ldg(src_rows + p)) : p) * ldx;
   float m = 0.f;
+  uint4 v0 = make_uint4(0, 0, 0, 0);   // the first round's block, kept for the second pass
   for (int blk = threadIdx.x; blk * 8 < K; blk += blockDim.x) {
     const uint4 v = *reinterpret_cast<const uint4*>(xr + blk * 8);
+    if (blk == int(threadIdx.x)) v0 = v;
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j)
@@ -518,8 +520,8 @@ __global__ void act_records_kernel(const uint16_t* __restrict__ x, int64_t ldx, 
   for (int b0 = 0; b0 < nb; b0 += blockDim.x) {   // uniform over the CTA
     const int blk = b0 + threadIdx.x;
     const bool inside = blk * 8 < K;   // implies blk < nb
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (inside) v = *reinterpret_cast<const uint4*>(xr + blk * 8);
+    uint4 v = b0 == 0 ? v0 : make_uint4(0, 0, 0, 0);
+    if (inside && b0 > 0) v = *reinterpret_cast<const uint4*>(xr + blk * 8);
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
     float xv[8];
 #pragma unroll
