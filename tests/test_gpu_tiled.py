@@ -68,6 +68,34 @@ def test_tiled_block_matches_mlx_layout(cfg, down_rows):
         assert_same_products(y1, y0, f"T={T}")
 
 
+def test_tiled_block_rows_of_wide_range():
+    """All activation records of a position share one power-of-two scale,
+    chosen from the row's largest |x|: chunks 2^32 smaller than the row's
+    largest meet f16 subnormals, whose terms sit far below the float32 sums'
+    rounding, so the tiled block still matches the MLX-layout block and the
+    oracle.  Zero chunks and an all-zero row take scale 1.  T > 4 runs the
+    records pass (smaller batches take the single-launch decode kernel)."""
+    import vxmoe
+    p = O.make_params(seed=14, experts=16, hidden=512, inter=128, shared_inter=64, top_k=4)
+    plain, tiled = _pair(p)
+    for T in (5, 40):
+        x = O.make_x(60 + T, T, p.hidden).copy()
+        x[:, :128] *= 2.0 ** 8
+        x[:, 128:256] *= 2.0 ** -24
+        x[1::3, 256:384] = 0.0
+        x[2] = 0.0
+        xt = bf16_t(x)
+        y0, i0, _ = vxmoe.moe_block(xt, plain, return_routing=True)
+        y1, i1, _ = vxmoe.moe_block(xt, tiled, return_routing=True)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(i0.cpu().numpy(), i1.cpu().numpy())
+        assert_same_products(y1, y0, f"wide-range rows, T={T}")
+        assert np.all(np.isfinite(np32(y1)))
+        logits = np32(vxmoe.router(xt, tiled).logits)
+        out = O.moe_block(np32(xt), p, logits=logits)
+        assert O.normwise_error(np32(y1), out.y) < 1e-2, f"T={T}"
+
+
 def test_tiled_block_production_against_oracle():
     import vxmoe
     p = O.make_params(seed=0)
