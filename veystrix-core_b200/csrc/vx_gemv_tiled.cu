@@ -47,9 +47,18 @@
 
 namespace vx {
 
-constexpr int kTiledThreads = 256;
-constexpr int kTiledWarps = kTiledThreads / 32;
+constexpr int kTiledWarps = 8;
 constexpr int kTiledStages = 3;
+// Decode-sized batches have too few (item, row tile) tasks to fill the GPU
+// with warps: each warp then walks its task's chunks with a deep pipeline
+// (kDeepStages - 1 chunks in flight instead of kTiledStages - 1) in 4-warp
+// CTAs, one task per warp.
+constexpr int kDeepStages = 8;
+constexpr int kDeepWarps = 4;
+// Resident CTAs per SM of a GEMV shape: the deep one alone, the others two.
+__host__ __device__ constexpr int tiled_ctas_per_sm(int stages, int warps) {
+  return (stages == kDeepStages && warps == kDeepWarps) ? 1 : 2;
+}
 
 struct TiledTask {
   int e, p0, cnt, row0, N, K;
@@ -119,7 +128,7 @@ constexpr bool kWeightsByLsu = true;
 constexpr int kTaskFifo = 16;
 
 template <bool GATEUP, int MT, bool XMMA, int STAGES, int WARPS, int GS>
-__global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
+__global__ void __launch_bounds__(WARPS * 32, tiled_ctas_per_sm(STAGES, WARPS))
     gemv_tiled_kernel(const __grid_constant__ TiledArgs a) {
   chain_wait();
   constexpr int NP = GATEUP ? 2 : 1;
@@ -425,7 +434,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? 2 : 1)
     if (t < 0) break;
     TiledTask k;
     decode_task<MT>(a, t, k);   // a valid task (seek() skips the others)
-    if (k.cnt > 2)
+    if (kTiledItemChunk > 2 && k.cnt > 2)
       run(k, std::integral_constant<int, 2>());
     else
       run(k, std::integral_constant<int, 1>());
@@ -675,20 +684,13 @@ static cudaError_t launch_tiled_v(TiledArgs a, int64_t tasks, cudaStream_t st) {
   auto kern = gemv_tiled_kernel<GATEUP, MT, XMMA, STAGES, WARPS, GS>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (err != cudaSuccess) return err;
-  // persistent: two resident CTAs per SM for the 8-warp shape, one otherwise
-  const int64_t cap = int64_t(sm_count()) * (WARPS == 8 ? 2 : 1);
+  // persistent: two resident CTAs per SM for the 8-warp shape, one for the deep one
+  const int64_t cap = int64_t(sm_count()) * tiled_ctas_per_sm(STAGES, WARPS);
   int64_t grid = (tasks + WARPS - 1) / WARPS;
   if (grid > cap) grid = cap;
   if (grid <= 0) return cudaSuccess;
   return launch_streaming(kern, dim3(int(grid)), dim3(WARPS * 32), smem, st, a);
 }
-
-// Decode-sized batches have too few (item, row tile) tasks to fill the GPU
-// with warps: each warp then walks its task's chunks with a deep pipeline
-// (kDeepStages - 1 chunks in flight instead of kTiledStages - 1) in 4-warp
-// CTAs, one task per warp.
-constexpr int kDeepStages = 8;
-constexpr int kDeepWarps = 4;
 
 template <bool GATEUP, int MT, bool XMMA, int GS>
 static cudaError_t launch_tiled_t(TiledArgs a, int max_items, int max_out, cudaStream_t st) {
