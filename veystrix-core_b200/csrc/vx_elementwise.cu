@@ -4,12 +4,81 @@
 
 namespace vx {
 
+// V consecutive bf16 values as float32 (V = 8: one 16-byte load; 2: 4 bytes).
+template <int V>
+VX_DEVICE void load_bf16(const uint16_t* p, float (&f)[V]) {
+  if constexpr (V == 8) {
+    const uint4 v = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = __uint_as_float(w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+  } else {
+    static_assert(V == 2, "2 or 8 values");
+    const uint32_t v = *reinterpret_cast<const uint32_t*>(p);
+    f[0] = __uint_as_float(v << 16);
+    f[1] = __uint_as_float(v & 0xFFFF0000u);
+  }
+}
+
+template <int V>
+VX_DEVICE void store_bf16(uint16_t* p, const float (&f)[V]) {
+  uint32_t w[V / 2];
+#pragma unroll
+  for (int i = 0; i < V / 2; ++i) w[i] = uint32_t(f32_to_bf16(f[2 * i])) | (uint32_t(f32_to_bf16(f[2 * i + 1])) << 16);
+  if constexpr (V == 8)
+    *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+  else
+    *reinterpret_cast<uint32_t*>(p) = w[0];
+}
+
+// a[i] = sum over the token's slots, in slot order, of bf16(yd[pos][c + i]) *
+// score, each product and sum rounded (no fused multiply-add); slots with
+// pos < 0 (dropped) add nothing.  The rows of up to kCombineBatch slots are
+// loaded before any of them is added, so a thread keeps that many loads in
+// flight instead of one.
+constexpr int kCombineBatch = 8;
+
+template <int V>
+VX_DEVICE void slot_sum(const uint16_t* __restrict__ yd, int64_t ldy, const int32_t* __restrict__ inv,
+                        const uint16_t* __restrict__ wts, int k, int c, float (&a)[V]) {
+#pragma unroll
+  for (int i = 0; i < V; ++i) a[i] = 0.f;
+  for (int s0 = 0; s0 < k; s0 += kCombineBatch) {
+    int pos[kCombineBatch];
+    float w[kCombineBatch], v[kCombineBatch][V];
+#pragma unroll
+    for (int j = 0; j < kCombineBatch; ++j) {
+      pos[j] = s0 + j < k ? inv[s0 + j] : -1;
+      w[j] = pos[j] >= 0 ? bf16_to_f32(wts[s0 + j]) : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < kCombineBatch; ++j) {
+      if (pos[j] >= 0) {
+        load_bf16<V>(yd + int64_t(pos[j]) * ldy + c, v[j]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < V; ++i) v[j][i] = 0.f;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kCombineBatch; ++j)
+      if (pos[j] >= 0)
+#pragma unroll
+        for (int i = 0; i < V; ++i) a[i] = __fadd_rn(a[i], __fmul_rn(v[j][i], w[j]));
+  }
+}
+
 // Score-weighted combine of the routed outputs, in the order of the fused
 // down+combine kernel of the reference (metal_runtime.py:315-334, patched
 // helpers :404-410): every slot's output is already bf16; it is multiplied
 // by its score and accumulated in float32 in slot order without fused
 // multiply-add; the sum is rounded to bf16, then the shared component is
 // added in float32 and the result rounded to bf16.
+// One thread per V consecutive outputs of token t (blockIdx.x).
+template <int V>
 __global__ void __launch_bounds__(256) combine_kernel(
     const uint16_t* __restrict__ yd, int64_t ldy, const int32_t* __restrict__ inverse,
     const uint16_t* __restrict__ weights, int T, int k, int d, int mode,
@@ -18,24 +87,16 @@ __global__ void __launch_bounds__(256) combine_kernel(
     const uint16_t* __restrict__ shared_gate, uint16_t* __restrict__ y) {
   chain_begin();
   const int t = blockIdx.x;
-  const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 2;   // rows on x: no 65,535 limit
+  const int c = (blockIdx.y * blockDim.x + threadIdx.x) * V;   // rows on x: no 65,535 limit
   if (c >= d) return;
-  float a0 = 0.f, a1 = 0.f;
-  for (int s = 0; s < k; ++s) {
-    const int pos = inverse[int64_t(t) * k + s];
-    if (pos < 0) continue;
-    const float w = bf16_to_f32(weights[int64_t(t) * k + s]);
-    const uint32_t v = *reinterpret_cast<const uint32_t*>(yd + int64_t(pos) * ldy + c);
-    a0 = __fadd_rn(a0, __fmul_rn(__uint_as_float(v << 16), w));
-    a1 = __fadd_rn(a1, __fmul_rn(__uint_as_float(v & 0xFFFF0000u), w));
-  }
-  float r0 = bf16r(a0), r1 = bf16r(a1);
+  float a[V], r[V];
+  slot_sum<V>(yd, ldy, inverse + int64_t(t) * k, weights + int64_t(t) * k, k, c, a);
+#pragma unroll
+  for (int i = 0; i < V; ++i) r[i] = bf16r(a[i]);
   if (mode != kSharedNone) {
-    float s0, s1;
+    float sv[V];
     if (mode == kSharedY) {
-      const uint32_t v = *reinterpret_cast<const uint32_t*>(shared_y + int64_t(t) * d + c);
-      s0 = __uint_as_float(v << 16);
-      s1 = __uint_as_float(v & 0xFFFF0000u);
+      load_bf16<V>(shared_y + int64_t(t) * d + c, sv);
     } else {
       const uint16_t* srow;
       float gate;
@@ -46,16 +107,17 @@ __global__ void __launch_bounds__(256) combine_kernel(
         srow = shared + int64_t(t) * d;
         gate = bf16_to_f32(shared_gate[t]);
       }
-      const uint32_t v = *reinterpret_cast<const uint32_t*>(srow + c);
-      s0 = bf16r(__fmul_rn(__uint_as_float(v << 16), gate));
-      s1 = bf16r(__fmul_rn(__uint_as_float(v & 0xFFFF0000u), gate));
+      load_bf16<V>(srow + c, sv);
+#pragma unroll
+      for (int i = 0; i < V; ++i) sv[i] = bf16r(__fmul_rn(sv[i], gate));
     }
-    r0 = bf16r(__fadd_rn(r0, s0));
-    r1 = bf16r(__fadd_rn(r1, s1));
+#pragma unroll
+    for (int i = 0; i < V; ++i) r[i] = bf16r(__fadd_rn(r[i], sv[i]));
   }
-  const uint32_t outv = uint32_t(f32_to_bf16(r0)) | (uint32_t(f32_to_bf16(r1)) << 16);
-  *reinterpret_cast<uint32_t*>(y + int64_t(t) * d + c) = outv;
+  store_bf16<V>(y + int64_t(t) * d + c, r);
 }
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 cudaError_t launch_combine(const uint16_t* yd, int64_t ldy, const int32_t* inverse,
                            const uint16_t* weights, int T, int k, int d, SharedMode mode,
@@ -63,9 +125,17 @@ cudaError_t launch_combine(const uint16_t* yd, int64_t ldy, const int32_t* inver
                            const uint16_t* shared_y, const uint16_t* shared,
                            const uint16_t* shared_gate, uint16_t* y, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  dim3 grid(T, (d / 2 + 255) / 256);
-  return launch_chained(combine_kernel, grid, dim3(256), 0, st, yd, ldy, inverse, weights, T, k, d,
-                        int(mode), offsets, E, sg, shared_y, shared, shared_gate, y);
+  // eight outputs per thread when every row the kernel reads or writes
+  // starts on a 16-byte boundary and the batch still gives every SM two
+  // CTAs (decode-sized batches keep two outputs per thread and more CTAs)
+  const bool wide = d % 8 == 0 && ldy % 8 == 0 && aligned16(yd) && aligned16(y) &&
+                    (!shared_y || aligned16(shared_y)) && (!shared || aligned16(shared)) &&
+                    int64_t(T) * ((d / 8 + 255) / 256) >= 2 * int64_t(sm_count());
+  if (wide)
+    return launch_chained(combine_kernel<8>, dim3(T, (d / 8 + 255) / 256), dim3(256), 0, st, yd, ldy, inverse,
+                          weights, T, k, d, int(mode), offsets, E, sg, shared_y, shared, shared_gate, y);
+  return launch_chained(combine_kernel<2>, dim3(T, (d / 2 + 255) / 256), dim3(256), 0, st, yd, ldy, inverse,
+                        weights, T, k, d, int(mode), offsets, E, sg, shared_y, shared, shared_gate, y);
 }
 
 // Activations for the grouped GEMV: B order and per-group sums.  One thread
@@ -117,32 +187,31 @@ cudaError_t launch_xprep(const uint16_t* x, int64_t rows, int K, uint16_t* xb, f
 // Float32 partial combine for expert parallelism: the same slot-order
 // float32 sum as combine_kernel, left unrounded and without the shared part
 // (the home rank adds the partials of all ranks, then rounds).
+template <int V>
 __global__ void __launch_bounds__(256) combine_partial_kernel(
     const uint16_t* __restrict__ yd, int64_t ldy, const int32_t* __restrict__ inverse,
     const uint16_t* __restrict__ weights, int k, int d, float* __restrict__ out) {
   chain_begin();
   const int t = blockIdx.x;
-  const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 2;   // rows on x: no 65,535 limit
+  const int c = (blockIdx.y * blockDim.x + threadIdx.x) * V;   // rows on x: no 65,535 limit
   if (c >= d) return;
-  float a0 = 0.f, a1 = 0.f;
-  for (int s = 0; s < k; ++s) {
-    const int pos = inverse[int64_t(t) * k + s];
-    if (pos < 0) continue;
-    const float w = bf16_to_f32(weights[int64_t(t) * k + s]);
-    const uint32_t v = *reinterpret_cast<const uint32_t*>(yd + int64_t(pos) * ldy + c);
-    a0 = __fadd_rn(a0, __fmul_rn(__uint_as_float(v << 16), w));
-    a1 = __fadd_rn(a1, __fmul_rn(__uint_as_float(v & 0xFFFF0000u), w));
-  }
-  *reinterpret_cast<float2*>(out + int64_t(t) * d + c) = make_float2(a0, a1);
+  float a[V];
+  slot_sum<V>(yd, ldy, inverse + int64_t(t) * k, weights + int64_t(t) * k, k, c, a);
+  float* o = out + int64_t(t) * d + c;
+#pragma unroll
+  for (int i = 0; i < V; i += 2) *reinterpret_cast<float2*>(o + i) = make_float2(a[i], a[i + 1]);
 }
 
 cudaError_t launch_combine_partial(const uint16_t* yd, int64_t ldy, const int32_t* inverse,
                                    const uint16_t* weights, int T, int k, int d, float* out,
                                    cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  dim3 grid(T, (d / 2 + 255) / 256);
-  return launch_chained(combine_partial_kernel, grid, dim3(256), 0, st, yd, ldy, inverse, weights, k, d,
-                        out);
+  if (d % 8 == 0 && ldy % 8 == 0 && aligned16(yd) && aligned16(out) &&
+      int64_t(T) * ((d / 8 + 255) / 256) >= 2 * int64_t(sm_count()))
+    return launch_chained(combine_partial_kernel<8>, dim3(T, (d / 8 + 255) / 256), dim3(256), 0, st, yd, ldy,
+                          inverse, weights, k, d, out);
+  return launch_chained(combine_partial_kernel<2>, dim3(T, (d / 2 + 255) / 256), dim3(256), 0, st, yd, ldy,
+                        inverse, weights, k, d, out);
 }
 
 // out[t, s, :] = yd[inverse[t*k+s], :]  (_scatter_unsort)
