@@ -1,12 +1,24 @@
 """Adaptive top-k in the oracle (adaptive_topk.py:44-51, :107-118,
-:224-233): the keep rule on hand-checked weight rows, the masking of the
-dropped slots (the token's first expert, score 0), the renormalisation over
-the kept mass, and threshold 1.0 leaving the exact top-k untouched."""
+:224-233): the keep rule on hand-checked weight rows and against the keep
+counts of the reference's own `_keep_for_mass` (tests/golden/adaptive_keep.npz,
+written by make_adaptive_golden.py), the masking of the dropped slots (the
+token's first expert, score 0), the renormalisation over the kept mass, and
+threshold 1.0 leaving the exact top-k untouched."""
 from __future__ import annotations
+
+import os
 
 import numpy as np
 
 import vxmoe_oracle as O
+
+
+def test_keep_for_mass_matches_reference_counts(golden_dir):
+    g = np.load(os.path.join(golden_dir, "adaptive_keep.npz"))
+    rows, thresholds, keeps = g["weights"], g["thresholds"], g["keeps"]
+    assert keeps.shape == (len(thresholds), len(rows)) and set(np.unique(keeps)) == set(range(1, 11))
+    got = np.array([[O.keep_for_mass(r.tolist(), float(t)) for r in rows] for t in thresholds])
+    np.testing.assert_array_equal(got, keeps)
 
 
 def test_keep_for_mass_hand_cases():
