@@ -95,16 +95,17 @@ __host__ __device__ constexpr int tile_unit_bytes(int group) { return group == 6
 constexpr int kTiledItemChunk = 4;
 
 // Activation records of the tiled GEMV: per (128-input chunk, position) 320
-// bytes - the chunk's 128 bf16 inputs in lane order [i][c] (8 inputs each,
-// B order inside), then the four group sums as float32, then padding.  An
-// item's positions are consecutive, so one bulk copy brings all its tokens.
-// The 320-byte pitch puts the two tokens a B operand reads on disjoint banks.
+// bytes - the chunk's 128 inputs in lane order [i][c] (8 inputs each, B
+// order inside), then the four group sums as float32 and the record's
+// inverse scale, then padding.  An item's positions are consecutive, so one
+// bulk copy brings all its tokens.  The 320-byte pitch puts the two tokens a
+// B operand reads on disjoint banks.
 constexpr int kActRecord = 320;
 constexpr int kActXsum = 256;
-// act_records_kernel writes f16 records (scaled by a power of two per
-// record) of x (gate/up's input) and of h (down's input, from the plain h
-// rows the gate/up pass writes); both GEMV passes read them with the f16
-// unpack.
+// act_records_kernel writes f16 records (every record of a position scaled
+// by the same power of two) of x (gate/up's input) and of h (down's input,
+// from the plain h rows the gate/up pass writes); both GEMV passes read them
+// with the f16 unpack.
 constexpr bool kActF16 = true;
 
 struct TiledArgs {
