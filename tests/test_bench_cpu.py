@@ -1,5 +1,6 @@
-"""Host-side pieces of bench.py (no GPU): the kernel-launch count it claims
-and the DRAM traffic it quotes from the committed ncu summary."""
+"""Host-side pieces of bench.py (no GPU): the kernel-launch count it claims,
+the DRAM traffic it quotes from the committed ncu summary, and the reference
+arm's JSON line."""
 from __future__ import annotations
 
 import os
@@ -31,3 +32,28 @@ def test_traffic_only_for_the_captured_workload():
         assert bench.traffic_for(kernel, e["tokens"]) == e["dram_bytes_per_launch"]
         assert bench.traffic_for(kernel, e["tokens"] + 1) is None
     assert bench.traffic_for("no_such_kernel", 64) is None
+
+
+def test_reference_arm_prints_the_contract_line():
+    """`bench.py --impl reference` (the driver's reference arm) times the C
+    restatement of the block on the host cores and prints one JSON line with
+    the main arm's metric, unit and config, its own CPU baseline and an
+    end-to-end figure without device copies."""
+    import json
+    import subprocess
+
+    import bench
+
+    proc = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference",
+                           "--steps", "1", "--warmup", "1"],
+                          capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    line = json.loads([ln for ln in proc.stdout.splitlines() if ln.startswith("{")][-1])
+    assert line["impl"] == "reference" and line["metric"] == bench.METRIC
+    assert line["unit"] == "tokens/s" and line["higher_is_better"] is True
+    assert (line["n_gpus"], line["steps"], line["warmup"]) == (1, 1, 1)
+    assert line["value"] > 0 and line["config"]["workload"].startswith("BASELINE config 2")
+    cpu = line["cpu_baseline"]
+    assert cpu["kind"] == "port" and cpu["cores"] >= 1 and cpu["value"] == line["value"]
+    assert line["e2e"] == {"value": line["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                           "d2h_bytes_per_step": 0}
